@@ -1,0 +1,236 @@
+/*
+ * loopsgl_b200.h -- C ABI of the B200 (sm_100a) looped-decoder hot path.
+ *
+ * Plain pointers, sizes and a CUDA stream (passed as void*); no framework
+ * types. Every entry point returns LSB_OK (0) or an LSB_ERR_* code and, on
+ * failure, leaves a message for lsb_last_error() on the calling thread.
+ * Tensors are device pointers in the layouts stated per function; "bf16" is
+ * IEEE bfloat16. Launches are asynchronous on `stream`, never synchronise the
+ * host, and can be captured into CUDA graphs unless stated otherwise.
+ *
+ * Each declaration names the reference interface (Loop-SGLang,
+ * python/loopsgl/...) whose work it replaces.
+ */
+#ifndef LOOPSGL_B200_H_
+#define LOOPSGL_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSB_OK 0
+#define LSB_ERR_INVALID 1     /* an argument is out of range, misaligned or null */
+#define LSB_ERR_CUDA 2        /* the CUDA runtime reported an error */
+#define LSB_ERR_TIMEOUT 3     /* a bounded cross-GPU wait gave up */
+#define LSB_ERR_UNSUPPORTED 4 /* shape or mode this build does not implement */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* lsb_last_error(void);
+/* ABI version, bumped on any signature change. */
+int lsb_abi_version(void);
+
+/* Reads the sticky device error word that kernels set, instead of faulting,
+ * when they meet an out-of-range index: LSB_DEVERR_* bits. reset != 0 clears it.
+ * Synchronises `stream` (not capturable). */
+#define LSB_DEVERR_POSITION 1 /* a RoPE position outside the cos/sin table */
+#define LSB_DEVERR_SLOT 2     /* a KV slot outside the pool */
+#define LSB_DEVERR_SEQLEN 4   /* a sequence longer than the max_seqlen bound */
+#define LSB_DEVERR_TIMEOUT 8  /* a bounded in-kernel wait gave up */
+int lsb_device_error_word(int32_t* out, int32_t reset, void* stream);
+
+/* ---------------------------------------------------------------- norms --
+ * Row-wise RMSNorm over `dim` bf16 elements: fp32 sum of squares, output
+ * dtype(x * rsqrt(mean(x^2) + eps) * w). dim % 8 == 0, rows 16-byte aligned.
+ */
+
+/* out[r] = rmsnorm(x[r]) * w.  Replaces layers/norm.py:16-17 (RMSNorm.forward,
+ * flashinfer.rmsnorm). */
+int lsb_rmsnorm(void* out, int64_t out_stride, const void* x, int64_t x_stride,
+                const void* weight, int64_t rows, int64_t dim, float eps, void* stream);
+
+/* residual <- x + residual; x <- rmsnorm(residual) * w, with the norm taken on
+ * the fp32 sum.  Replaces layers/norm.py:32-38 (RMSNormFused.forward with a
+ * residual, flashinfer.fused_add_rmsnorm). In place on x and residual. */
+int lsb_fused_add_rmsnorm(void* x, void* residual, const void* weight, int64_t rows, int64_t dim,
+                          float eps, void* stream);
+
+/* The sandwich step of the Ouro layer: y = rmsnorm(x) * w_a (rounded), then
+ * residual <- y + residual and out = rmsnorm(residual) * w_b.  Replaces the
+ * pair models/looped/ouro.py:49-50 (input_layernorm_2 then
+ * post_attention_layernorm) and :52 + :45 (post_attention_layernorm_2 then the
+ * next layer's input_layernorm). out may alias x. */
+int lsb_sandwich_norm(void* out, const void* x, void* residual, const void* w_a,
+                      const void* w_b, int64_t rows, int64_t dim, float eps, void* stream);
+
+/* ------------------------------------------------------ RoPE + KV store --
+ * qkv: [T, (hq + 2*hkv) * head_dim] bf16 rows of stride qkv_stride elements.
+ * Applies neox RoPE in place to the q and k heads at positions[T] using the
+ * fp32 table cos_sin[max_pos, head_dim] = cat(cos, sin), then stores the
+ * rotated k heads and the v heads of row t into slot out_loc[t] of k_cache /
+ * v_cache ([slots, hkv, head_dim] bf16, slot stride slot_stride elements),
+ * skipping slot 0 (the padding slot).  Replaces layers/attention.py:88-90
+ * (rotary.py:40-55, flashinfer apply_rope_with_cos_sin_cache_inplace) and the
+ * backend's store_kv (kvcache/mha_pool.py:54-66, kernel/store.py:89-152,
+ * kernel/csrc/jit/store.cu:127-156). */
+int lsb_rope_store_kv(void* qkv, int64_t qkv_stride, const int32_t* positions,
+                      const float* cos_sin, int64_t max_pos, void* k_cache, void* v_cache,
+                      int64_t slot_stride, int64_t num_slots, const int32_t* out_loc,
+                      int64_t tokens, int32_t hq, int32_t hkv, int32_t head_dim, void* stream);
+
+/* Scatter k[t] and v[t] (rows of row_elems bf16, row strides k_stride /
+ * v_stride) into slot out_loc[t] of k_cache / v_cache, skipping slot 0.
+ * Replaces kvcache/mha_pool.py:54-66 / last_exited.py:298-311 store_kv
+ * (kernel/store.py:89-152, kernel/csrc/jit/store.cu:127-156). */
+int lsb_store_kv(void* k_cache, void* v_cache, int64_t slot_stride, int64_t num_slots,
+                 const void* k, int64_t k_stride, const void* v, int64_t v_stride,
+                 const int32_t* out_loc, int64_t tokens, int64_t row_elems, void* stream);
+
+/* ------------------------------------------------------ paged attention --
+ * Causal attention of query rows over one paged KV layer.
+ *   q:        [rows, hq, head_dim] bf16, row stride q_stride elements
+ *   out:      [rows, hq, head_dim] bf16, row stride out_stride elements
+ *   k_cache/v_cache: slots of hkv*head_dim bf16 (slot = page*page_size + offset),
+ *             slot stride slot_stride elements
+ *   page_table: [num_reqs, pt_stride] int32 page ids (page_size 1: slots)
+ *   cache_seqlens: [num_reqs] keys of each request (its last query row sees all)
+ *   cu_seqlens_q: [num_reqs + 1] query-row offsets per request
+ * Row i of the n rows of a request attends to keys 0 .. seqlen - n + i.
+ * Splits the keys of long rows across CTAs; the partial results go to the
+ * caller's workspace (lsb_paged_attention_workspace_size bytes, zeroed once
+ * before first use and left zeroed by every call). Slots outside [0, num_slots)
+ * are skipped and flagged in the device error word instead of being read.  Replaces the backends'
+ * attention call (attention/trtllm.py:80-91 decode, :62-78 prefill;
+ * attention/fa.py:82-93; attention/fi.py:161-199). */
+int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, int32_t head_dim,
+                                           int64_t max_seqlen);
+int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                        const void* k_cache, const void* v_cache, int64_t slot_stride,
+                        int64_t num_slots, const int32_t* page_table, int64_t pt_stride,
+                        const int32_t* cache_seqlens, const int32_t* cu_seqlens_q,
+                        int64_t num_reqs, int64_t rows, int32_t hq, int32_t hkv,
+                        int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
+                        void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ GEMM --------
+ * y[M, N] = x[M, K] . w[N, K]^T (+ bias[N]) in bf16 with fp32 accumulation on
+ * the sm_100a tensor cores (tcgen05.mma, TMEM accumulators, TMA-fed).
+ * x, w row-major with leading dimensions ldx, ldw (elements); y row stride ldy.
+ * epilogue: LSB_EPI_NONE, LSB_EPI_BIAS (fp32 bias add before rounding),
+ * LSB_EPI_BIAS_AFTER_ROUND (round, then add bias and round again),
+ * LSB_EPI_SWIGLU (w rows interleaved in blocks of 64 gate / 64 up rows by
+ * lsb_swiglu_interleave; y[M, N/2] = silu(g) * u of the rounded g, u).
+ * K % 64 == 0, N % 128 == 0, ldx/ldw/ldy multiples of 8, pointers 16-byte
+ * aligned. workspace: split-K partials, lsb_gemm_workspace_size bytes, zeroed
+ * once and left zeroed by every call.
+ * Replaces layers/linear.py:32-33 (F.linear, cuBLAS) for the QKV, o_proj,
+ * gate_up, down, adapter and LM-head projections, and models/utils.py:46-48
+ * (gate_up + silu_and_mul) with LSB_EPI_SWIGLU. */
+#define LSB_EPI_NONE 0
+#define LSB_EPI_BIAS 1
+#define LSB_EPI_BIAS_AFTER_ROUND 2
+#define LSB_EPI_SWIGLU 3
+int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, int64_t ldw,
+             const void* bias, int64_t M, int64_t N, int64_t K, int32_t epilogue,
+             void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
+ * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
+ * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */
+int lsb_swiglu_interleave(void* out, const void* w, int64_t inter, int64_t K, void* stream);
+
+/* ---------------------------------------------- loop-step exit kernels ---
+ * Ouro step end fused with the exit gate and the CDB state scatter:
+ *   y = rmsnorm(x) * w_post2 (rounded); residual <- y + residual;
+ *   h = rmsnorm(residual) * w_final                      (ouro.py:52, :136)
+ *   logit = bf16(h . gate_w + gate_b)                     (ouro.py:149)
+ *   p' = p + (1 - p) * sigmoid(logit)                     (exit_gates.py:6-15)
+ *   signal = p' >= threshold && depth + 1 + lookahead >= min_loop_steps
+ * Row r writes h to hidden_out[slot[r]] (slot == NULL: row r), reads and writes
+ * exit_state[slot[r]] (fp32), writes signal[r] (uint8 0/1). depth: per-row int32
+ * array, or NULL to use depth_scalar. gate_w/gate_b may be NULL (no gate: only
+ * h is written).  Replaces ouro.py:136 + :142-155 and
+ * model_executor/cdb_model_runner.py:102-108. */
+int lsb_ouro_step_exit(void* hidden_out, int64_t hidden_stride, const void* x, void* residual,
+                       const void* w_post2, const void* w_final, const void* gate_w,
+                       const void* gate_b, const int64_t* slot, float* exit_state,
+                       uint8_t* signal, const int32_t* depth, int32_t depth_scalar,
+                       int32_t lookahead, int32_t min_loop_steps, float threshold,
+                       int64_t rows, int64_t dim, float eps, void* stream);
+
+/* Huginn exit: signal[r] = ||h - prev|| / max(||h||, 1e-9) < threshold in fp32,
+ * prev = exit_state[slot[r]] (bf16 rows), then exit_state[slot[r]] = h and
+ * hidden_out[slot[r]] = h.  Replaces huginn.py:184-194, exit_gates.py:18-24 and
+ * cdb_model_runner.py:102-108. */
+int lsb_huginn_step_exit(void* hidden_out, void* exit_state, const void* h, const int64_t* slot,
+                         uint8_t* signal, float threshold, int64_t rows, int64_t dim,
+                         void* stream);
+
+/* ------------------------------------------------ gathers and sampling ---
+ * out[t] = dtype(weight[ids[t] - vocab_start] * scale), zero rows for ids outside
+ * [vocab_start, vocab_start + vocab_len).  Replaces layers/embedding.py:34-43
+ * (VocabParallelEmbedding.forward before its all-reduce) and huginn.py:147-148. */
+int lsb_embedding(void* out, const int32_t* ids, const void* weight, int64_t tokens, int64_t dim,
+                  int64_t vocab_start, int64_t vocab_len, float scale, void* stream);
+
+/* out[r] = src[index[r]] over rows of `dim` bf16 (index_select).
+ * Replaces cdb_model_runner.py:94-101 (state-pool gathers). */
+int lsb_gather_rows(void* out, const void* src, const int64_t* index, int64_t rows, int64_t dim,
+                    void* stream);
+
+/* out[r] = argmax_j logits[r, j] (first index on ties), logits bf16 [rows, vocab]
+ * with row stride ld.  Replaces model_executor/sample.py:108-112. */
+int lsb_argmax(int32_t* out, const void* logits, int64_t rows, int64_t vocab, int64_t ld,
+               void* stream);
+
+/* silu(x[:, :I]) * x[:, I:] -> out[:, :I].  Replaces layers/activation.py:9-12. */
+int lsb_silu_and_mul(void* out, const void* x, int64_t rows, int64_t inter, void* stream);
+
+/* ------------------------------------------------- last-exited metadata --
+ * Resolve logical token handles to physical KV slots at each row's depth:
+ * physical_table[g, r, c] = version_map[depth_r, g, logical_table[r, c]] for
+ * c < cache_seqlens[r]; physical_out[g, i] = version_map[depth_r, g,
+ * logical_out[i]] for the query rows i of request r. version_map is
+ * [steps, groups, num_handles] int32 (group stride vm_group_stride, depth stride
+ * vm_depth_stride); depth = depths[r] or depth_scalar when depths is NULL.
+ * Replaces attention/metadata.py:220-291 (prepare_last_exited_metadata). */
+int lsb_last_exited_resolve(int32_t* physical_table, int64_t pt_group_stride, int64_t pt_stride,
+                            int32_t* physical_out, int64_t out_group_stride,
+                            const int32_t* logical_table, int64_t lt_stride,
+                            const int32_t* version_map, int64_t vm_depth_stride,
+                            int64_t vm_group_stride, const int32_t* cache_seqlens,
+                            const int32_t* cu_seqlens_q, const int32_t* logical_out,
+                            const int32_t* depths, int32_t depth_scalar, int64_t num_reqs,
+                            int64_t cols, int32_t groups, void* stream);
+
+/* Reserve the KV versions of n new token handles (one per loop depth and
+ * layer group) from the shared free-slot stack, exactly as the reference's
+ * _reserve_versions does when its programs run in handle order:
+ * token t pops fixed_groups + d_t * core_groups slots (d_t = steps, or
+ * restore_depths[t] when not NULL) and depths it did not compute alias the
+ * last computed version. slot_map [fixed + steps*core, width] int32,
+ * completed_depth [width], free_slots stack, free_count [1] (device).
+ * Replaces kvcache/last_exited.py:15-47 and :181-202, :269-290. */
+int lsb_last_exited_reserve(int32_t* slot_map, int32_t* completed_depth, int64_t width,
+                            int32_t* free_slots, int32_t* free_count, const int32_t* handles,
+                            const int32_t* restore_depths, int64_t n, int32_t steps,
+                            int32_t fixed_groups, int32_t core_groups, void* stream);
+
+/* Release versions back to the stack in handle order (the reference's
+ * _release_versions): with exits (alias) the versions at depths >= exits[t]
+ * are freed and alias the final computed version; with exits == NULL every
+ * version of the token is freed.  Replaces kvcache/last_exited.py:50-84,
+ * :204-248. */
+int lsb_last_exited_release(int32_t* slot_map, int32_t* completed_depth, int64_t width,
+                            int32_t* free_slots, int32_t* free_count, const int32_t* handles,
+                            const int32_t* exits, int64_t n, int32_t steps, int32_t fixed_groups,
+                            int32_t core_groups, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOOPSGL_B200_H_ */

@@ -147,3 +147,101 @@ def replay_cdb(name: str, dtype=torch.float32) -> tuple[dict, dict[str, torch.Te
                                        dec).float()
     res["kv_buf"] = pool.buf
     return fx, res
+
+
+# ---------------------------------------------------------------------------
+# The same scenarios through the CUDA path (GPU tests only)
+# ---------------------------------------------------------------------------
+
+
+def gpu_model(cfg: LoopedConfig, weights, policy: str):
+    from __graft_entry__ import load_package
+
+    load_package()
+    from loop_sglang_b200.model import LoopedConfig as GpuConfig
+    from loop_sglang_b200.model import LoopedDecoder
+
+    return LoopedDecoder(GpuConfig(**cfg.__dict__), weights, policy, torch.device("cuda"))
+
+
+def device_batch(fx: dict, prefix: str, ids, is_prefill: bool, page_size: int):
+    from loop_sglang_b200.model import DeviceBatch
+
+    b = batch_from(fx, prefix, ids, is_prefill)
+    dev = torch.device("cuda")
+    return DeviceBatch(b.input_ids.to(dev), b.positions.to(dev), b.out_loc.to(dev),
+                       b.page_table.to(dev).contiguous(), b.cache_seqlens.to(dev),
+                       b.cu_seqlens_q.to(dev), is_prefill,
+                       max_seqlen=int(b.page_table.shape[1]) * page_size)
+
+
+def gpu_replay_cb(name: str) -> tuple[dict, dict[str, torch.Tensor]]:
+    """CUDA-path logits for every step of a CB fixture (bf16 weights)."""
+    cfg, policy = CB_CASES[name]
+    fx = load(name)
+    weights = make_weights(cfg, int(fx["seed"]), dtype=torch.float32, gate_bias=0.0)
+    model = gpu_model(cfg, weights, policy)
+    page = int(fx["page_size"])
+    kv = model.make_kv_cache(NUM_PAGES, page)
+    out = {}
+    for prefix, is_prefill in cb_steps(fx):
+        batch = device_batch(fx, prefix, fx[f"{prefix}_ids"], is_prefill, page)
+        if policy == "last_exited":
+            kv.reserve_versions(batch.out_loc)
+        out[prefix] = model.forward(batch, kv).float().cpu()
+    return fx, out
+
+
+def gpu_replay_cdb(name: str) -> tuple[dict, dict[str, torch.Tensor]]:
+    """CUDA-path prefill, prelude, mixed-depth fused core phases and coda of a CDB fixture."""
+    cfg, policy = CDB_CASES[name]
+    fx = load(name)
+    weights = make_weights(cfg, int(fx["seed"]), dtype=torch.float32, gate_bias=0.3)
+    model = gpu_model(cfg, weights, policy)
+    dev = torch.device("cuda")
+    kv = model.make_kv_cache(CDB_NUM_PAGES, 1)
+    res: dict[str, torch.Tensor] = {}
+    pre = device_batch(fx, "prefill", fx["prefill_ids"], True, 1)
+    if policy == "last_exited":
+        kv.reserve_versions(pre.out_loc)
+    res["prefill_logits"] = model.forward(pre, kv).float().cpu()
+    dec = device_batch(fx, "decode", fx["tokens"], False, 1)
+    if policy == "last_exited":
+        kv.reserve_versions(dec.out_loc)
+    rows = len(fx["tokens"])
+    cap = rows + 5
+    state = {"hidden": torch.zeros(cap, cfg.hidden, dtype=torch.bfloat16, device=dev)}
+    if cfg.arch == "huginn":
+        state["injection"] = torch.zeros(cap, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        state["exit"] = torch.zeros(cap, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    else:
+        state["exit"] = torch.zeros(cap, dtype=torch.float32, device=dev)
+    slots = torch.arange(1, rows + 1, device=dev)
+    if policy == "last_exited":
+        model.resolve_fixed(dec, kv)
+    hidden, inj = model.forward_prelude(dec, kv)
+    state["hidden"][slots] = hidden
+    if inj is not None:
+        state["injection"][slots] = inj
+    state["exit"][slots] = model.init_exit_state(hidden)
+    res["prelude_hidden"] = state["hidden"][slots].float().cpu()
+    k = 0
+    while f"core{k}_rows" in fx:
+        srows = torch.from_numpy(fx[f"core{k}_rows"]).long().to(dev)
+        depths = torch.from_numpy(fx[f"core{k}_depths"]).to(dev)
+        ids = fx["tokens"][(fx[f"core{k}_rows"] - 1)]
+        batch = device_batch(fx, f"core{k}", ids, False, 1)
+        signal = torch.zeros(srows.numel(), dtype=torch.uint8, device=dev)
+        model.core_step_exit(state, srows, depths, batch, kv, signal)
+        res[f"core{k}_gates"] = signal.bool().cpu()
+        res[f"core{k}_hidden"] = state["hidden"][srows].float().cpu()
+        res[f"core{k}_exit"] = state["exit"][srows].float().cpu()
+        if policy == "last_exited":
+            res[f"core{k}_core_page_table"] = batch.core_page_table.cpu()
+            res[f"core{k}_core_out_loc"] = batch.core_out_loc.cpu()
+        k += 1
+    if policy == "last_exited":
+        model.resolve_fixed(dec, kv)
+    res["coda_logits"] = model.lm_head(model.forward_coda(state["hidden"][slots], dec, kv),
+                                       dec).float().cpu()
+    return fx, res
