@@ -1,0 +1,413 @@
+"""Decode throughput of the looped-decoder hot path on B200 (one JSON line on stdout).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: Ouro-1.4B architecture (24 shared layers x 4 loop
+steps, hidden 2048, 16 MHA heads x 128, SwiGLU 5632, vocab 49152), random-init bf16,
+full-depth CB decode, depth-indexed KV with 16-token pages, TP=1. 256 requests with
+uniform-random prompt lengths in [512, 2048] and 256 output tokens; the requests
+are admitted in order while their full length fits the KV pool (768 KiB per token:
+the running batch is capacity-limited) and every admitted request decodes from the
+middle of its generation (prompt + 128). A step is one decode step of the running
+batch: batch metadata, embedding, 4 x 24 layers, LM head and greedy sampling, all
+from this repository's kernels, replayed as one CUDA graph. KV contents and token
+ids are synthetic (seeded random), as are the weights.
+
+``value`` times K device-resident steps; ``e2e`` times K steps through the public
+per-step call with host buffers (H2D of the scheduler inputs, D2H of the tokens).
+``--impl reference`` times the CPU oracle restatement of the same decode step
+(the reference's own code path restated on the host cores) on a bounded sample.
+With N > 1 (torchrun) every rank runs an independent replica (weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+OURO_14B = dict(arch="ouro", hidden=2048, heads=16, kv_heads=16, head_dim=128,
+                intermediate=5632, vocab=49152, num_core_layers=24, loop_steps=4,
+                rope_theta=1e6, rms_eps=1e-6, max_position=4096)
+PAGE = 16
+NUM_REQS = 256
+PROMPT_RANGE = (512, 2048)
+OUT_TOKENS = 256
+MID = 128  # decode position inside the generation when timing starts
+SEED = 0
+
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def request_lengths() -> np.ndarray:
+    rng = np.random.default_rng(SEED)
+    return rng.integers(PROMPT_RANGE[0], PROMPT_RANGE[1] + 1, NUM_REQS)
+
+
+def admit(prompts: np.ndarray, free_pages: int) -> int:
+    """How many requests (in order) fit: each reserves pages for prompt + outputs."""
+    need = np.cumsum((prompts + OUT_TOKENS + PAGE - 1) // PAGE)
+    return int(np.searchsorted(need, free_pages, side="right"))
+
+
+def gpu_weights(cfg, device, seed: int) -> dict[str, torch.Tensor]:
+    """Seeded N(0, 0.02) weights (norms 1 + N(0, 0.05)) generated on the GPU."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    w: dict[str, torch.Tensor] = {}
+
+    def mat(name, *shape):
+        w[name] = (torch.randn(*shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+    def norm(name, n):
+        w[name] = (1 + 0.05 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16)
+
+    h, i = cfg.hidden, cfg.intermediate
+    mat("model.embed_tokens.weight", cfg.vocab, h)
+    for p in cfg.layer_names():
+        mat(f"{p}.self_attn.qkv_proj.weight", cfg.qkv_out, h)
+        mat(f"{p}.self_attn.o_proj.weight", h, cfg.heads * cfg.head_dim)
+        mat(f"{p}.mlp.gate_up_proj.weight", 2 * i, h)
+        mat(f"{p}.mlp.down_proj.weight", h, i)
+        for n in ("input_layernorm", "input_layernorm_2", "post_attention_layernorm",
+                  "post_attention_layernorm_2"):
+            norm(f"{p}.{n}.weight", h)
+    norm("model.norm.weight", h)
+    mat("model.early_exit_gate.weight", 1, h)
+    w["model.early_exit_gate.bias"] = torch.zeros(1, dtype=torch.bfloat16, device=device)
+    mat("lm_head.weight", cfg.vocab, h)
+    return w
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device) -> None:
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            ident = str(device.index or 0)
+        self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-i", ident, "-lms", "200"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU side --
+
+def cpu_decode_sample(steps: int, batch: int, threads: int) -> dict:
+    """The oracle (CPU restatement of the reference decode step) on a bounded sample:
+    ``batch`` requests of the workload at mean context, ``steps`` decode steps."""
+    from oracle import model as om
+
+    torch.set_num_threads(threads)
+    cfg = om.LoopedConfig(**OURO_14B)
+    t0 = time.perf_counter()
+    w = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
+    mdl = om.LoopedModel(cfg, w, "depth_indexed")
+    prompts = request_lengths()[:batch]
+    ctx = prompts + MID
+    pages_per = [(int(c) + steps + PAGE) // PAGE for c in ctx]
+    num_pages = sum(pages_per) + 1
+    pool = om.PagedKVPool(mdl.num_kv_layers, num_pages, PAGE, cfg.kv_heads, cfg.head_dim,
+                          torch.bfloat16)
+    pool.buf.normal_(generator=torch.Generator().manual_seed(1))
+    table = torch.zeros(batch, max(pages_per), dtype=torch.int32)
+    nxt = 1
+    for b, n in enumerate(pages_per):
+        table[b, :n] = torch.arange(nxt, nxt + n, dtype=torch.int32)
+        nxt += n
+    setup = time.perf_counter() - t0
+    ids = torch.randint(0, cfg.vocab, (batch,), generator=torch.Generator().manual_seed(2),
+                        dtype=torch.int32)
+    times = []
+    for s in range(steps):
+        pos = torch.as_tensor(ctx + s, dtype=torch.int32)
+        loc = table[torch.arange(batch), pos.long() // PAGE] * PAGE + pos % PAGE
+        b = om.Batch(ids, pos, loc.to(torch.int32), table, pos + 1,
+                     torch.arange(batch + 1, dtype=torch.int32), False)
+        t = time.perf_counter()
+        logits = mdl.forward(b, pool)
+        ids = logits.float().argmax(-1).to(torch.int32)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    return {"value": batch * steps / total, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"{batch} requests at context {int(ctx.mean())} (mean), {steps} decode "
+                       f"steps of Ouro-1.4B through the CPU oracle in torch bf16/fp32, "
+                       f"{threads} threads; setup {setup:.0f}s untimed"),
+            "p50_step_s": statistics.median(times)}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    base = cpu_decode_sample(max(1, args.steps), args.cpu_batch, threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * base["p50_step_s"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random weights, KV and token ids)",
+        "config": {"workload": WORKLOAD, "sample_batch": args.cpu_batch},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "decode output tok/s, Ouro-1.4B CB full depth (configs[1]), TP1 per replica"
+WORKLOAD = ("configs[1]: Ouro-1.4B random-init bf16, full-depth CB decode, depth-indexed KV, "
+            "16-token pages, 256 requests prompt U[512,2048] + 256 outputs, capacity-limited "
+            "running batch decoding at prompt+128")
+
+
+# ---------------------------------------------------------------- GPU side --
+
+def run_b200(args) -> None:
+    from __graft_entry__ import load_package
+
+    load_package()
+    from loop_sglang_b200 import _lib, ops
+    from loop_sglang_b200.engine import DecodeEngine
+    from loop_sglang_b200.model import LoopedConfig, LoopedDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = LoopedConfig(**OURO_14B)
+    t0 = time.perf_counter()
+    weights = gpu_weights(cfg, dev, SEED)
+    model = LoopedDecoder(cfg, weights, "depth_indexed", dev)
+    del weights
+    torch.cuda.empty_cache()
+    prompts = request_lengths()
+    page_bytes = 2 * model.num_kv_layers * PAGE * cfg.kv_heads * cfg.head_dim * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    pool_pages = int((free - 8 * 2**30) // page_bytes)
+    if args.batch:
+        bs = args.batch
+    else:
+        bs = min(admit(prompts, pool_pages - 1), NUM_REQS)
+    prompts = prompts[:bs]
+    full = prompts + OUT_TOKENS
+    pages_per = (full + PAGE - 1) // PAGE
+    num_pages = min(pool_pages, int(pages_per.sum()) + 1)
+    kv = model.make_kv_cache(num_pages, PAGE, zero=False)
+    kv._kv_buffer.normal_(generator=torch.Generator(device=dev).manual_seed(SEED + 1))
+    kv._kv_buffer[:, :, 0].zero_()
+    max_len = int(full.max())
+    eng = DecodeEngine(model, kv, bs, max_len, PAGE, max_reqs=bs)
+    perm = torch.randperm(num_pages - 1, generator=torch.Generator().manual_seed(SEED + 2)) + 1
+    off = 0
+    for r in range(bs):
+        n = int(pages_per[r])
+        eng.assign_pages(r + 1, perm[off:off + n].to(dev))
+        off += n
+    rows = torch.arange(1, bs + 1, dtype=torch.int32, device=dev)
+    steps_total = args.warmup + args.steps
+    base_seq = torch.as_tensor(prompts + MID, dtype=torch.int32, device=dev)
+    sched = torch.stack([base_seq + 1 + s for s in range(steps_total + 1)])  # incl. new token
+    eng.ids.copy_(torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32))
+    eng.set_batch(rows, sched[0])
+    eng.capture()
+    setup_s = time.perf_counter() - t0
+    log(f"[bench] rank {rank}: batch {bs}, pool {num_pages} pages, setup {setup_s:.1f}s, "
+        f"{eng.launches_per_step} kernels/step")
+
+    s = eng.stream
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(s):
+        for k in range(args.warmup):
+            eng.seq_lens.copy_(sched[k], non_blocking=True)
+            eng.replay()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(dev) as clocks, torch.cuda.stream(s):
+        ev[0].record(s)
+        for k in range(args.steps):
+            eng.seq_lens.copy_(sched[args.warmup + k], non_blocking=True)
+            eng.replay()
+            ev[k + 1].record(s)
+        s.synchronize()
+    barrier()
+    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    clk = clocks.summary()
+
+    # e2e: the public per-step call with host buffers (pinned H2D in, D2H out).
+    host_rows = torch.arange(1, bs + 1, dtype=torch.int32).pin_memory()
+    host_sched = sched.cpu().pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for k in range(args.steps):
+        eng.decode_step_host(host_rows, host_sched[k])
+    e1.record(s)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # roofline of the dominant kernel: layer-0 attention of the same batch, timed alone
+    ctx = (sched[args.warmup + args.steps - 1]).to(torch.int64)
+    attn_bytes = int(ctx.sum().item()) * cfg.kv_heads * cfg.head_dim * 2 * 2 \
+        + 2 * bs * cfg.heads * cfg.head_dim * 2
+    q = torch.randn(bs, cfg.heads, cfg.head_dim, device=dev).to(torch.bfloat16)
+    kc, vc = kv.slots(0)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    with torch.cuda.stream(s):
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, cfg.kv_heads, out=out)
+        a0.record(s)
+        for _ in range(reps):
+            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, cfg.kv_heads, out=out)
+        a1.record(s)
+        s.synchronize()
+    attn_s = a0.elapsed_time(a1) / 1000.0 / reps
+
+    t_max = total_ms
+    e2e_max = e2e_ms
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_max, e2e_max = float(t[0]), float(t[1])
+    tokens = bs * args.steps * world
+    value = tokens / (t_max / 1000.0)
+    mean_ctx = float(ctx.float().mean())
+    weight_bytes = sum(t.numel() * 2 for lw in model.layers.values()
+                       for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) * cfg.loop_steps \
+        + model.lm_head_w.numel() * 2 + bs * cfg.hidden * 2
+    kv_bytes = int(ctx.sum().item()) * model.num_kv_layers * cfg.kv_heads * cfg.head_dim * 4
+    step_bytes = weight_bytes + kv_bytes
+    peak, peak_kind = peaks()
+    achieved = attn_bytes / attn_s / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+        "p50_tpot_ms": statistics.median(step_ms), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded random-init weights, random KV contents and token ids",
+        "config": {"workload": WORKLOAD, "model": "Ouro-1.4B architecture (random init)",
+                   "global_batch": bs * world, "running_batch_per_gpu": bs,
+                   "mean_context": round(mean_ctx, 1), "kv_pool_pages": num_pages,
+                   "page_size": PAGE, "parallelism": f"dp{world}" if world > 1 else "tp1",
+                   "l2": "inputs larger than L2 (each step streams the KV pool, ~%d GB)"
+                         % (step_bytes // 10**9)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "paged_attention (layer-0 decode, whole running batch)",
+                     "peak_kind": peak_kind,
+                     "step_frac": round(step_bytes / (t_max / 1000.0 / args.steps) / 1e9 / peak
+                                        * (1 if world == 1 else 1), 4),
+                     "step_bytes": step_bytes},
+        "e2e": {"value": tokens / (e2e_max / 1000.0), "unit": "tok/s",
+                "h2d_bytes_per_step": 2 * bs * 4, "d2h_bytes_per_step": bs * 4},
+        "gpu_launches": eng.launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_decode_sample(args.cpu_steps, args.cpu_batch,
+                                                     os.cpu_count() or 1)
+            line["cpu_baseline"].pop("p50_step_s", None)
+        except Exception as exc:  # reported, never silently dropped
+            line["cpu_baseline"] = {"value": None, "error": repr(exc)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.graph = None
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    _ = _lib
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--batch", type=int, default=0, help="override the admitted batch (debug)")
+    ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--cpu-batch", type=int, default=2)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -100,7 +100,8 @@ int lsb_store_kv(void* k_cache, void* v_cache, int64_t slot_stride, int64_t num_
  * Row i of the n rows of a request attends to keys 0 .. seqlen - n + i.
  * Splits the keys of long rows across CTAs; the partial results go to the
  * caller's workspace (lsb_paged_attention_workspace_size bytes, zeroed once
- * before first use and left zeroed by every call). Slots outside [0, num_slots)
+ * before first use; its head holds arrival counters that every call leaves zeroed,
+ * so one workspace serves calls of any shape). head_dim 32, 64, 96 or 128. Slots outside [0, num_slots)
  * are skipped and flagged in the device error word instead of being read.  Replaces the backends'
  * attention call (attention/trtllm.py:80-91 decode, :62-78 prefill;
  * attention/fa.py:82-93; attention/fi.py:161-199). */
@@ -123,8 +124,8 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
  * LSB_EPI_SWIGLU (w rows interleaved in blocks of 64 gate / 64 up rows by
  * lsb_swiglu_interleave; y[M, N/2] = silu(g) * u of the rounded g, u).
  * K % 64 == 0, N % 128 == 0, ldx/ldw/ldy multiples of 8, pointers 16-byte
- * aligned. workspace: split-K partials, lsb_gemm_workspace_size bytes, zeroed
- * once and left zeroed by every call.
+ * aligned. workspace: split-K arrival counters (head, left zeroed by every call)
+ * and partials, lsb_gemm_workspace_size bytes, zeroed once before first use.
  * Replaces layers/linear.py:32-33 (F.linear, cuBLAS) for the QKV, o_proj,
  * gate_up, down, adapter and LM-head projections, and models/utils.py:46-48
  * (gate_up + silu_and_mul) with LSB_EPI_SWIGLU. */
@@ -228,6 +229,31 @@ int lsb_last_exited_release(int32_t* slot_map, int32_t* completed_depth, int64_t
                             int32_t* free_slots, int32_t* free_count, const int32_t* handles,
                             const int32_t* exits, int64_t n, int32_t steps, int32_t fixed_groups,
                             int32_t core_groups, void* stream);
+
+/* --------------------------------------------------- batch metadata ----
+ * Per-token batch inputs from the token-granular request table req_to_token
+ * [rows, r2t_stride] int32 (locations page*page_size + offset): for request r,
+ * query token j sits at seq_lens[r] - extend_lens[r] + j (decode: extend 1,
+ * token r) and reads its KV location from req_to_token[req_pool_indices[r], pos].
+ * Writes positions, req_mapping (may be NULL) and out_loc, flattened over
+ * requests.  Replaces kernel/batch.py:72-129 (_prepare_batch_inputs). */
+int lsb_prepare_batch_inputs(int32_t* positions, int32_t* req_mapping, int32_t* out_loc,
+                             const int32_t* seq_lens, const int32_t* extend_lens,
+                             const int32_t* req_pool_indices, const int32_t* req_to_token,
+                             int64_t r2t_stride, int64_t bs, int32_t is_decode, void* stream);
+
+/* Attention metadata: cache_seqlens = seq_lens + seq_len_delta; prefix sums
+ * cu_seqlens_k / cu_seqlens_q (decode: one query per request); page-table row r
+ * = req_to_token[req_pool_indices[r], c * page_size] / page_size for the
+ * min(ceil(seq/page), max_seq_pages) live columns (others untouched).
+ * Replaces attention/metadata.py:59-216 (_fused_metadata_kernel_general via
+ * normal_decode_set_metadata / extend_set_metadata). */
+int lsb_set_metadata(int32_t* cache_seqlens, int32_t* cu_seqlens_k, int32_t* cu_seqlens_q,
+                     int32_t* page_table, int64_t pt_stride, const int32_t* req_to_token,
+                     int64_t r2t_stride, const int32_t* req_pool_indices,
+                     const int32_t* seq_lens, const int32_t* extend_lens, int64_t bs,
+                     int64_t max_seq_pages, int32_t page_size, int32_t seq_len_delta,
+                     int32_t is_decode, void* stream);
 
 #ifdef __cplusplus
 }

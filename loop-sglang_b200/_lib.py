@@ -59,6 +59,9 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_silu_and_mul": (ctypes.c_int, [P, P, I64, I64, P]),
     "lsb_last_exited_resolve": (ctypes.c_int, [P, I64, I64, P, I64, P, I64, P, I64, I64, P, P, P,
                                                P, I32, I64, I64, I32, P]),
+    "lsb_prepare_batch_inputs": (ctypes.c_int, [P, P, P, P, P, P, P, I64, I64, I32, P]),
+    "lsb_set_metadata": (ctypes.c_int, [P, P, P, P, I64, P, I64, P, P, P, I64, I64, I32, I32, I32,
+                                        P]),
     "lsb_last_exited_reserve": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
     "lsb_last_exited_release": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
 }
@@ -97,5 +100,18 @@ def check(rc: int, what: str) -> None:
     raise LsbError(f"{what} failed ({rc}): {msg}")
 
 
+_launches = 0
+_NOT_LAUNCHES = {"lsb_device_error_word"}
+
+
+def launch_count() -> int:
+    """Kernels launched through ``call`` so far in this process (one per call)."""
+    return _launches
+
+
 def call(name: str, *args) -> None:
+    """Invoke a launching entry point; every such call enqueues exactly one kernel."""
+    global _launches
     check(getattr(lib(), name)(*args), name)
+    if name not in _NOT_LAUNCHES:
+        _launches += 1

@@ -24,7 +24,7 @@ constexpr int kUnroll = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -1e30f;
 
-__host__ __device__ constexpr int lanes_for(int d) { return d <= 64 ? 8 : 16; }
+__host__ __device__ constexpr int lanes_for(int d) { return d <= 32 ? 4 : (d <= 64 ? 8 : 16); }
 
 int64_t chunk_for(int64_t rows, int32_t hq, int64_t max_seqlen) {
   int64_t chunk = 1024;
@@ -42,20 +42,24 @@ struct Workspace {
   int* counters;      // [rows, head_groups]
 };
 
+// Layout: a fixed region of per-(row, head group) arrival counters at the head
+// (so calls of any shape find them zeroed), then the fp32 partials.
+constexpr int64_t kCounterCap = 65536;
+constexpr int64_t kCounterBytes = kCounterCap * sizeof(int);
+
 Workspace carve(void* base, int64_t rows, int32_t hq, int32_t d, int64_t splits) {
   Workspace w;
   char* p = static_cast<char*>(base);
+  w.counters = reinterpret_cast<int*>(p);
+  p += kCounterBytes;
   w.partial_o = reinterpret_cast<float*>(p);
   p += rows * hq * splits * d * sizeof(float);
   w.partial_ml = reinterpret_cast<float*>(p);
-  p += rows * hq * splits * 2 * sizeof(float);
-  w.counters = reinterpret_cast<int*>(p);
   return w;
 }
 
 int64_t workspace_bytes_for(int64_t rows, int32_t hq, int32_t d, int64_t splits) {
-  const int64_t groups = (hq + kWarps - 1) / kWarps;
-  int64_t b = rows * hq * splits * (d + 2) * sizeof(float) + rows * groups * sizeof(int);
+  int64_t b = kCounterBytes + rows * hq * splits * (d + 2) * sizeof(float);
   return (b + 255) & ~int64_t(255);
 }
 
@@ -273,8 +277,8 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
                                    void* stream) {
   LSB_REQUIRE(out && q && k_cache && v_cache && page_table && cache_seqlens && cu_seqlens_q,
               "paged_attention: null pointer");
-  LSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128,
-              "paged_attention: head_dim %d unsupported (64, 96, 128)", head_dim);
+  LSB_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 96 || head_dim == 128,
+              "paged_attention: head_dim %d unsupported (32, 64, 96, 128)", head_dim);
   LSB_REQUIRE(hq > 0 && hkv > 0 && hq % hkv == 0, "paged_attention: bad heads %d/%d", hq, hkv);
   LSB_REQUIRE(page_size > 0 && max_seqlen > 0 && num_reqs > 0, "paged_attention: bad sizes");
   LSB_REQUIRE(aligned(out, 16) && aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16),
@@ -291,6 +295,9 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
               "paged_attention: workspace of %lld bytes needed", (long long)need);
   const int groups = (hq + kWarps - 1) / kWarps;
   LSB_REQUIRE(rows * groups < (int64_t(1) << 31), "paged_attention: too many rows");
+  LSB_REQUIRE(splits == 1 || rows * groups <= kCounterCap,
+              "paged_attention: %lld rows x %d head groups exceed the %lld split counters",
+              (long long)rows, groups, (long long)kCounterCap);
   Workspace ws = splits > 1 ? carve(workspace, rows, hq, head_dim, splits) : Workspace{};
   dim3 grid(static_cast<unsigned>(rows * groups), static_cast<unsigned>(splits));
   const float scale_log2 = scale * kLog2e;
@@ -302,7 +309,8 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
         static_cast<int>(num_reqs), hq, hkv, page_size, chunk, splits, scale_log2, ws,
         lsb_device_error_flag());
   };
-  if (head_dim == 64) launch(paged_attention_kernel<64>);
+  if (head_dim == 32) launch(paged_attention_kernel<32>);
+  else if (head_dim == 64) launch(paged_attention_kernel<64>);
   else if (head_dim == 96) launch(paged_attention_kernel<96>);
   else launch(paged_attention_kernel<128>);
   return check_launch("lsb_paged_attention");

@@ -34,6 +34,9 @@ constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxStages = 8;
 constexpr int kXchStride = 17;
 constexpr long long kTimeoutCycles = 4000000000LL;
+// Split-K arrival counters live in a fixed region at the head of the workspace, so
+// calls of any shape find them where the previous call left them: zero.
+constexpr int64_t kCounterBytes = 16 * 1024;
 
 struct GemmParams {
   bf16* y;
@@ -411,10 +414,7 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
 
 int64_t workspace_for(const Plan& pl, int64_t M, int64_t N) {
   if (pl.splits <= 1) return 0;
-  int64_t b = static_cast<int64_t>(pl.splits) * M * N * 4;
-  b = (b + 255) & ~int64_t(255);
-  b += static_cast<int64_t>(pl.tiles_n) * pl.tiles_m * 4;
-  return (b + 255) & ~int64_t(255);
+  return kCounterBytes + ((static_cast<int64_t>(pl.splits) * M * N * 4 + 255) & ~int64_t(255));
 }
 
 uint32_t make_idesc(int bn) {
@@ -465,9 +465,10 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   p.y = static_cast<bf16*>(y);
   p.ldy = ldy;
   p.bias = static_cast<const bf16*>(bias);
-  p.partials = static_cast<float*>(workspace);
-  p.counters = need ? reinterpret_cast<int*>(static_cast<char*>(workspace) +
-                                             (((static_cast<int64_t>(pl.splits) * M * N * 4) + 255) & ~int64_t(255)))
+  LSB_REQUIRE(need == 0 || static_cast<int64_t>(pl.tiles_n) * pl.tiles_m * 4 <= kCounterBytes,
+              "gemm: too many split tiles");
+  p.counters = need ? static_cast<int*>(workspace) : nullptr;
+  p.partials = need ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes)
                     : nullptr;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);

@@ -370,3 +370,111 @@ extern "C" int lsb_last_exited_release(int32_t* slot_map, int32_t* completed_dep
       fixed_groups, core_groups);
   return check_launch("lsb_last_exited_release");
 }
+
+// ---------------------------------------------------------------------------
+// Batch inputs and attention metadata from the token-granular request table.
+// ---------------------------------------------------------------------------
+namespace lsb {
+namespace {
+
+// One CTA per request (kernel/batch.py:72-103).
+__global__ void prepare_batch_inputs_kernel(int32_t* __restrict__ positions,
+                                            int32_t* __restrict__ mapping,
+                                            int32_t* __restrict__ out_loc,
+                                            const int32_t* __restrict__ seq_lens,
+                                            const int32_t* __restrict__ extend_lens,
+                                            const int32_t* __restrict__ rpi,
+                                            const int32_t* __restrict__ r2t, int64_t stride,
+                                            int is_decode) {
+  const int r = blockIdx.x;
+  __shared__ int64_t offset;
+  if (threadIdx.x == 0) {
+    int64_t o = 0;
+    if (is_decode) o = r;
+    else
+      for (int i = 0; i < r; ++i) o += extend_lens[i];
+    offset = o;
+  }
+  __syncthreads();
+  const int q = is_decode ? 1 : extend_lens[r];
+  const int64_t row = rpi[r];
+  for (int j = threadIdx.x; j < q; j += blockDim.x) {
+    const int pos = seq_lens[r] - q + j;
+    positions[offset + j] = pos;
+    if (mapping) mapping[offset + j] = static_cast<int32_t>(row);
+    out_loc[offset + j] = r2t[row * stride + pos];
+  }
+}
+
+// Grid (bs): CTA 0 also writes the prefix sums (metadata.py:59-90).
+__global__ void set_metadata_kernel(int32_t* __restrict__ cache_seqlens,
+                                    int32_t* __restrict__ cu_k, int32_t* __restrict__ cu_q,
+                                    int32_t* __restrict__ page_table, int64_t pt_stride,
+                                    const int32_t* __restrict__ r2t, int64_t r2t_stride,
+                                    const int32_t* __restrict__ rpi,
+                                    const int32_t* __restrict__ seq_lens,
+                                    const int32_t* __restrict__ extend_lens, int64_t bs,
+                                    int64_t max_seq_pages, int page_size, int delta,
+                                    int is_decode) {
+  const int64_t r = blockIdx.x;
+  if (r == 0 && threadIdx.x == 0) {
+    int acc_k = 0, acc_q = 0;
+    for (int64_t i = 0; i < bs; ++i) {
+      const int seq = seq_lens[i] + delta;
+      const int qn = is_decode ? 1 : extend_lens[i];
+      cache_seqlens[i] = seq;
+      cu_k[i] = acc_k;
+      cu_q[i] = acc_q;
+      acc_k += seq;
+      acc_q += qn;
+    }
+    cu_k[bs] = acc_k;
+    cu_q[bs] = acc_q;
+  }
+  const int seq = seq_lens[r] + delta;
+  int64_t live = (seq + page_size - 1) / page_size;
+  if (live > max_seq_pages) live = max_seq_pages;
+  const int64_t row = rpi[r];
+  for (int64_t c = threadIdx.x; c < live; c += blockDim.x)
+    page_table[r * pt_stride + c] = r2t[row * r2t_stride + c * page_size] / page_size;
+}
+
+}  // namespace
+}  // namespace lsb
+
+extern "C" int lsb_prepare_batch_inputs(int32_t* positions, int32_t* req_mapping,
+                                        int32_t* out_loc, const int32_t* seq_lens,
+                                        const int32_t* extend_lens,
+                                        const int32_t* req_pool_indices,
+                                        const int32_t* req_to_token, int64_t r2t_stride,
+                                        int64_t bs, int32_t is_decode, void* stream) {
+  LSB_REQUIRE(positions && out_loc && seq_lens && req_pool_indices && req_to_token,
+              "prepare_batch_inputs: null pointer");
+  LSB_REQUIRE(is_decode || extend_lens, "prepare_batch_inputs: extend needs extend_lens");
+  if (bs <= 0) return LSB_OK;
+  prepare_batch_inputs_kernel<<<bs, 256, 0, as_stream(stream)>>>(
+      positions, req_mapping, out_loc, seq_lens, extend_lens, req_pool_indices, req_to_token,
+      r2t_stride, is_decode);
+  return check_launch("lsb_prepare_batch_inputs");
+}
+
+extern "C" int lsb_set_metadata(int32_t* cache_seqlens, int32_t* cu_seqlens_k,
+                                int32_t* cu_seqlens_q, int32_t* page_table, int64_t pt_stride,
+                                const int32_t* req_to_token, int64_t r2t_stride,
+                                const int32_t* req_pool_indices, const int32_t* seq_lens,
+                                const int32_t* extend_lens, int64_t bs, int64_t max_seq_pages,
+                                int32_t page_size, int32_t seq_len_delta, int32_t is_decode,
+                                void* stream) {
+  LSB_REQUIRE(cache_seqlens && cu_seqlens_k && cu_seqlens_q && page_table && req_to_token &&
+                  req_pool_indices && seq_lens,
+              "set_metadata: null pointer");
+  LSB_REQUIRE(is_decode || extend_lens, "set_metadata: extend needs extend_lens");
+  LSB_REQUIRE(page_size > 0 && max_seq_pages > 0 && max_seq_pages <= pt_stride,
+              "set_metadata: bad page geometry");
+  if (bs <= 0) return LSB_OK;
+  set_metadata_kernel<<<bs, 128, 0, as_stream(stream)>>>(
+      cache_seqlens, cu_seqlens_k, cu_seqlens_q, page_table, pt_stride, req_to_token, r2t_stride,
+      req_pool_indices, seq_lens, extend_lens, bs, max_seq_pages, page_size, seq_len_delta,
+      is_decode);
+  return check_launch("lsb_set_metadata");
+}

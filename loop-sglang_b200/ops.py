@@ -10,6 +10,8 @@ their counters zeroed, so one buffer serves every later call.
 
 from __future__ import annotations
 
+import math
+
 import torch
 
 from ._lib import (
@@ -26,7 +28,8 @@ __all__ = [
     "paged_attention",
     "gemm", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
     "gather_rows", "argmax", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
-    "last_exited_release", "device_error_word", "Workspace",
+    "last_exited_release", "device_error_word", "Workspace", "prepare_batch_inputs",
+    "set_metadata",
     "LSB_EPI_NONE", "LSB_EPI_BIAS", "LSB_EPI_BIAS_AFTER_ROUND", "LSB_EPI_SWIGLU",
 ]
 
@@ -148,8 +151,8 @@ def store_kv(k_cache: torch.Tensor, v_cache: torch.Tensor, out_loc: torch.Tensor
              k: torch.Tensor, v: torch.Tensor) -> None:
     """``store_cache`` (kernel/store.py:89-152): rows of k/v into slots, slot 0 skipped.
     Caches are ``[slots, ...]`` views; k/v are ``[T, row]`` (row stride free)."""
-    k2 = k.reshape(k.shape[0], -1) if k.dim() != 2 else k
-    v2 = v.reshape(v.shape[0], -1) if v.dim() != 2 else v
+    k2 = k.reshape(k.shape[0], math.prod(k.shape[1:])) if k.dim() != 2 else k
+    v2 = v.reshape(v.shape[0], math.prod(v.shape[1:])) if v.dim() != 2 else v
     for t, n in ((k2, "k"), (v2, "v")):
         _need(t, BF16, n, contiguous=False)
     _need(out_loc, torch.int32, "out_loc")
@@ -339,3 +342,25 @@ def last_exited_release(slot_map, completed, free_slots, free_count, handles, st
          free_slots.data_ptr(), free_count.data_ptr(), handles.data_ptr(), _p(exits),
          handles.numel(), steps, fixed, core, _stream())
 
+
+
+# -------------------------------------------------------- batch metadata --
+
+def prepare_batch_inputs(seq_lens, extend_lens, req_pool_indices, req_to_token, is_decode,
+                         positions, out_loc, req_mapping=None) -> None:
+    """``_prepare_batch_inputs`` (kernel/batch.py:72-129) into preallocated outputs."""
+    call("lsb_prepare_batch_inputs", positions.data_ptr(), _p(req_mapping), out_loc.data_ptr(),
+         seq_lens.data_ptr(), _p(extend_lens), req_pool_indices.data_ptr(),
+         req_to_token.data_ptr(), req_to_token.stride(0), seq_lens.numel(), int(is_decode),
+         _stream())
+
+
+def set_metadata(seq_lens, extend_lens, req_to_token, req_pool_indices, max_seq_pages,
+                 page_size, is_decode, cache_seqlens, cu_seqlens_k, cu_seqlens_q, page_table,
+                 seq_len_delta: int = 0) -> None:
+    """``_fused_metadata_kernel_general`` (attention/metadata.py:59-216)."""
+    call("lsb_set_metadata", cache_seqlens.data_ptr(), cu_seqlens_k.data_ptr(),
+         cu_seqlens_q.data_ptr(), page_table.data_ptr(), page_table.stride(0),
+         req_to_token.data_ptr(), req_to_token.stride(0), req_pool_indices.data_ptr(),
+         seq_lens.data_ptr(), _p(extend_lens), seq_lens.numel(), max_seq_pages, page_size,
+         seq_len_delta, int(is_decode), _stream())

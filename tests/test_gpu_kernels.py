@@ -351,3 +351,30 @@ def test_last_exited_maps(layout) -> None:
     kvmeta.resolve_last_exited(table.numpy(), ver.version_map, seq.numpy(), cu.numpy(),
                                lout.numpy(), depths.numpy(), et, eo)
     assert np.array_equal(pt.cpu().numpy(), et) and np.array_equal(po.cpu().numpy(), eo)
+
+
+def test_batch_metadata_golden() -> None:
+    """Batch inputs and page-table metadata, bit-exact with the reference's Triton kernels
+    (golden vectors from kernel/batch.py and attention/metadata.py run on the CPU)."""
+    from replay import load
+
+    fx = load("metadata")
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    r2t, seq, ext, rpi = d(fx["r2t"]), d(fx["seq"]), d(fx["ext"]), d(fx["rpi"])
+    for tag, is_decode in (("decode", True), ("extend", False)):
+        n = 3 if is_decode else int(fx["ext"].sum())
+        pos = torch.zeros(n, dtype=torch.int32, device=DEV)
+        mapping = torch.zeros_like(pos)
+        loc = torch.zeros_like(pos)
+        ops.prepare_batch_inputs(seq, ext, rpi, r2t, is_decode, pos, loc, mapping)
+        assert np.array_equal(pos.cpu().numpy(), fx[f"{tag}_positions"])
+        assert np.array_equal(mapping.cpu().numpy(), fx[f"{tag}_mapping"])
+        assert np.array_equal(loc.cpu().numpy(), fx[f"{tag}_outloc"])
+        cache = torch.zeros(3, dtype=torch.int32, device=DEV)
+        cuk = torch.zeros(4, dtype=torch.int32, device=DEV)
+        cuq = torch.zeros(4, dtype=torch.int32, device=DEV)
+        pt = torch.full((3, 8), -1, dtype=torch.int32, device=DEV)
+        maxp = (int(fx["seq"].max()) + 3) // 4
+        ops.set_metadata(seq, ext, r2t, rpi, maxp, 4, is_decode, cache, cuk, cuq, pt)
+        for got, key in ((cache, "cache"), (cuk, "cuk"), (cuq, "cuq"), (pt, "pt")):
+            assert np.array_equal(got.cpu().numpy(), fx[f"{tag}_{key}"]), (tag, key)
