@@ -123,8 +123,8 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
  * LSB_EPI_BIAS_AFTER_ROUND (round, then add bias and round again),
  * LSB_EPI_SWIGLU (w rows interleaved in blocks of 64 gate / 64 up rows by
  * lsb_swiglu_interleave; y[M, N/2] = silu(g) * u of the rounded g, u).
- * K % 64 == 0, N % 128 == 0, ldx/ldw/ldy multiples of 8, pointers 16-byte
- * aligned. workspace: split-K arrival counters (head, left zeroed by every call)
+ * Any M, N, K (ragged tails are zero-filled by TMA); SwiGLU needs N % 128 == 0;
+ * ldx/ldw multiples of 8 and x, w 16-byte aligned (TMA); y any row stride. workspace: split-K arrival counters (head, left zeroed by every call)
  * and partials, lsb_gemm_workspace_size bytes, zeroed once before first use.
  * Replaces layers/linear.py:32-33 (F.linear, cuBLAS) for the QKV, o_proj,
  * gate_up, down, adapter and LM-head projections, and models/utils.py:46-48

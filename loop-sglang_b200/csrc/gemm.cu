@@ -164,6 +164,7 @@ __device__ __forceinline__ void emit16(const GemmParams& p, const float* v, int 
     epi_barrier();
     return;
   }
+  if (row >= p.N) return;
   float b = 0.f;
   if (p.epilogue != LSB_EPI_NONE) b = __bfloat162float(p.bias[row]);
 #pragma unroll
@@ -197,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
   const int n0 = tile_n * kBM, m0 = tile_m * p.bn;
-  const int kblocks = p.K / kBK;
+  const int kblocks = (p.K + kBK - 1) / kBK;
   const int kb_begin = static_cast<int>(static_cast<int64_t>(kblocks) * split / p.splits);
   const int kb_end = static_cast<int>(static_cast<int64_t>(kblocks) * (split + 1) / p.splits);
   const int nk = kb_end - kb_begin;
@@ -287,10 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        if (row < p.N) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < p.M) mine[static_cast<int64_t>(m) * p.N + row] = v[j];
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < p.M) mine[static_cast<int64_t>(m) * p.N + row] = v[j];
+          }
         }
       }
       __threadfence();
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               const int m = m0 + c0 + j;
-              if (m < p.M) v[j] += __ldcg(part + static_cast<int64_t>(m) * p.N + row);
+              if (m < p.M && row < p.N) v[j] += __ldcg(part + static_cast<int64_t>(m) * p.N + row);
             }
           }
           emit16(p, v, m0 + c0, row, q, lane, tile_n, xch);
@@ -394,10 +397,10 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
   pl.stages = budget / stage_bytes;
   if (pl.stages > kMaxStages) pl.stages = kMaxStages;
   if (pl.stages < 2) pl.stages = 2;
-  pl.tiles_n = static_cast<int>(N / kBM);
+  pl.tiles_n = static_cast<int>((N + kBM - 1) / kBM);
   pl.tiles_m = static_cast<int>((M + pl.bn - 1) / pl.bn);
   const int tiles = pl.tiles_n * pl.tiles_m;
-  const int kblocks = static_cast<int>(K / kBK);
+  const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
   int splits = 1;
   const int sms = num_sms();
   if (tiles < sms) {
@@ -431,7 +434,7 @@ uint32_t make_idesc(int bn) {
 using namespace lsb;
 
 extern "C" int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K <= 0 || N % kBM || K % kBK) return 0;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
   return workspace_for(plan_for(M, N, K), M, N);
 }
 
@@ -440,14 +443,15 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
                         int32_t epilogue, void* workspace, int64_t workspace_bytes,
                         void* stream) {
   LSB_REQUIRE(y && x && w, "gemm: null pointer");
-  LSB_REQUIRE(N > 0 && K > 0 && N % kBM == 0 && K % kBK == 0,
-              "gemm: N %% 128 == 0 and K %% 64 == 0 required (N=%lld K=%lld)", (long long)N,
-              (long long)K);
+  LSB_REQUIRE(N > 0 && K > 0, "gemm: empty N or K (N=%lld K=%lld)", (long long)N, (long long)K);
+  LSB_REQUIRE(epilogue != LSB_EPI_SWIGLU || N % kBM == 0,
+              "gemm: the SwiGLU epilogue needs N %% 128 == 0 (N=%lld)", (long long)N);
   LSB_REQUIRE(N < (int64_t(1) << 31) && K < (int64_t(1) << 31) && M < (int64_t(1) << 31),
               "gemm: dimension too large");
-  LSB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldy % 8 == 0 && ldx >= K && ldw >= K,
-              "gemm: leading dimensions must be multiples of 8 and >= K");
-  LSB_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 16), "gemm: pointers must be 16-byte aligned");
+  LSB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldx >= K && ldw >= K,
+              "gemm: ldx/ldw must be multiples of 8 (16-byte TMA strides) and >= K");
+  LSB_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 2),
+              "gemm: x and w must be 16-byte aligned");
   LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue <= LSB_EPI_SWIGLU, "gemm: bad epilogue");
   LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_SWIGLU || bias,
               "gemm: bias required");

@@ -124,6 +124,7 @@ extern "C" int lsb_store_kv(void* k_cache, void* v_cache, int64_t slot_stride, i
                             const void* k, int64_t k_stride, const void* v, int64_t v_stride,
                             const int32_t* out_loc, int64_t tokens, int64_t row_elems,
                             void* stream) {
+  if (tokens <= 0) return LSB_OK;
   LSB_REQUIRE(k_cache && v_cache && k && v && out_loc, "store_kv: null pointer");
   LSB_REQUIRE(row_elems > 0 && row_elems % 2 == 0 && slot_stride >= row_elems &&
                   slot_stride % 2 == 0 && k_stride % 2 == 0 && v_stride % 2 == 0,

@@ -194,7 +194,9 @@ def test_paged_attention_full_size_property() -> None:
 
 
 GEMM_SHAPES = [(1, 128, 64), (3, 256, 128), (16, 384, 512), (144, 6144, 2048), (300, 256, 256),
-               (8, 2048, 5632), (256, 1024, 2048), (40, 11264, 2048)]
+               (8, 2048, 5632), (256, 1024, 2048), (40, 11264, 2048),
+               # ragged N and K (Huginn: H = 5280, QKV N = 15840; tiny shapes below 64 / 128)
+               (7, 288, 96), (33, 15840, 5280), (5, 100, 40), (130, 5280, 10560)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
@@ -230,10 +232,14 @@ def test_gemm_epilogues(epi: str, m: int) -> None:
 
 
 def test_gemm_rejects_bad_shapes() -> None:
-    x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)
+    x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)  # row stride 200 B: not TMA-able
     w = torch.zeros(128, 100, dtype=torch.bfloat16, device=DEV)
     with pytest.raises(ValueError):
         ops.gemm(x, w)
+    with pytest.raises(ValueError):  # SwiGLU tiles need N % 128 == 0
+        ops.gemm(torch.zeros(4, 64, dtype=torch.bfloat16, device=DEV),
+                 torch.zeros(192, 64, dtype=torch.bfloat16, device=DEV),
+                 epilogue=ops.LSB_EPI_SWIGLU)
 
 
 def test_small_ops() -> None:
@@ -241,8 +247,8 @@ def test_small_ops() -> None:
     wt = bf(torch.randn(50, 64, generator=g))
     ids = torch.tensor([3, 12, 49, 29], dtype=torch.int32)
     assert torch.equal(ops.embedding(ids.to(DEV), wt.to(DEV)).cpu(), wt[ids.long()])
-    close(ops.embedding(ids.to(DEV), wt.to(DEV), scale=1.5), bf(wt.float() * 1.5), rtol=0,
-          atol=0)
+    close(ops.embedding(ids.to(DEV), wt.to(DEV), scale=1.5), bf(wt[ids.long()].float() * 1.5),
+          rtol=0, atol=0)
     shard = ops.embedding(ids.to(DEV), wt[10:30].contiguous().to(DEV), vocab_start=10,
                           vocab_len=20)
     assert torch.equal(shard.cpu(), O.embedding(ids, wt[10:30], 10, 20))

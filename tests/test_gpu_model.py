@@ -25,13 +25,24 @@ def rel_err(got: torch.Tensor, ref: torch.Tensor) -> float:
     return float((got.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6))
 
 
+def greedy_agrees(got: torch.Tensor, ref: torch.Tensor, tol: float = 2e-2) -> bool:
+    """Same greedy token per row, except where the reference's top two logits are within
+    the bf16 tolerance of each other (a near-tie either side may take)."""
+    g, r = got.float().argmax(-1), ref.float().argmax(-1)
+    scale = ref.float().abs().max(-1).values
+    for i in torch.nonzero(g != r).flatten().tolist():
+        if ref[i, g[i]] < ref[i, r[i]] - tol * scale[i]:
+            return False
+    return True
+
+
 @pytest.mark.parametrize("name", sorted(CB_CASES))
 def test_cb_decode_matches_oracle(name: str) -> None:
     fx, got = gpu_replay_cb(name)
     _, ref, _ = replay_cb(name, dtype=torch.bfloat16)
     for prefix, logits in got.items():
         assert rel_err(logits, ref[prefix]) < 2e-2, prefix
-        assert torch.equal(logits.argmax(-1), ref[prefix].argmax(-1)), prefix
+        assert greedy_agrees(logits, ref[prefix]), prefix
         gold = torch.from_numpy(fx[f"{prefix}_logits"])
         assert rel_err(logits, gold) < 5e-2, prefix
 
@@ -62,4 +73,4 @@ def test_cdb_phases_match_oracle(name: str) -> None:
                                           fx[f"core{k}_core_out_loc"])
         k += 1
     assert rel_err(got["coda_logits"], ref["coda_logits"]) < 2e-2
-    assert torch.equal(got["coda_logits"].argmax(-1), ref["coda_logits"].argmax(-1))
+    assert greedy_agrees(got["coda_logits"], ref["coda_logits"])
