@@ -71,7 +71,8 @@ int lsb_sandwich_norm(void* out, const void* x, void* residual, const void* w_a,
  * fp32 table cos_sin[max_pos, head_dim] = cat(cos, sin), then stores the
  * rotated k heads and the v heads of row t into slot out_loc[t] of k_cache /
  * v_cache ([slots, hkv, head_dim] bf16, slot stride slot_stride elements),
- * skipping slot 0 (the padding slot).  Replaces layers/attention.py:88-90
+ * skipping slot 0 (the padding slot). With hkv == 0 (and no caches) it only
+ * rotates the hq heads of each row.  Replaces layers/attention.py:88-90
  * (rotary.py:40-55, flashinfer apply_rope_with_cos_sin_cache_inplace) and the
  * backend's store_kv (kvcache/mha_pool.py:54-66, kernel/store.py:89-152,
  * kernel/csrc/jit/store.cu:127-156). */

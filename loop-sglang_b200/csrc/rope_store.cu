@@ -101,8 +101,10 @@ extern "C" int lsb_rope_store_kv(void* qkv, int64_t qkv_stride, const int32_t* p
                                  const int32_t* out_loc, int64_t tokens, int32_t hq,
                                  int32_t hkv, int32_t head_dim, void* stream) {
   LSB_REQUIRE(qkv && positions && cos_sin, "null pointer");
-  LSB_REQUIRE(head_dim % 4 == 0 && head_dim > 0 && hq > 0 && hkv > 0 && hq % hkv == 0,
+  LSB_REQUIRE(head_dim % 4 == 0 && head_dim > 0 && hq > 0 && hkv >= 0 &&
+                  (hkv == 0 || hq % hkv == 0),
               "rope_store_kv: bad head shape hq=%d hkv=%d head_dim=%d", hq, hkv, head_dim);
+  LSB_REQUIRE(hkv > 0 || !k_cache, "rope_store_kv: a KV store needs k/v heads");
   LSB_REQUIRE(qkv_stride >= (int64_t)(hq + 2 * hkv) * head_dim && qkv_stride % 2 == 0,
               "rope_store_kv: qkv_stride too small");
   LSB_REQUIRE(aligned(qkv, 4) && aligned(cos_sin, 8), "rope_store_kv: misaligned pointers");

@@ -24,7 +24,7 @@ from ._lib import (
 )
 
 __all__ = [
-    "rmsnorm", "fused_add_rmsnorm", "sandwich_norm", "rope_store_kv", "store_kv",
+    "rmsnorm", "fused_add_rmsnorm", "sandwich_norm", "rope_store_kv", "rope_only", "store_kv",
     "paged_attention",
     "gemm", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
     "gather_rows", "argmax", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
@@ -159,6 +159,12 @@ def store_kv(k_cache: torch.Tensor, v_cache: torch.Tensor, out_loc: torch.Tensor
     call("lsb_store_kv", k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
          k_cache.shape[0], k2.data_ptr(), _row_stride(k2, "k"), v2.data_ptr(),
          _row_stride(v2, "v"), out_loc.data_ptr(), out_loc.numel(), k2.shape[1], _stream())
+
+
+def rope_only(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, heads: int,
+              head_dim: int) -> None:
+    """Neox RoPE in place on ``heads`` heads of each row of ``x`` (rotary.py:40-55)."""
+    rope_store_kv(x, positions, cos_sin, heads, 0, head_dim)
 
 
 # -------------------------------------------------------------- attention --
