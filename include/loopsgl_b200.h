@@ -116,6 +116,25 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
                         int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
                         void* workspace, int64_t workspace_bytes, void* stream);
 
+/* lsb_paged_attention for callers that cannot allocate device memory (a plugin
+ * whose host framework owns all device memory and passes only inputs and
+ * outputs, or a loop that must not pay cudaMalloc's device-wide
+ * synchronisation). No counterpart in the reference. The split-KV scratch is a
+ * static device array of LSB_NOALLOC_ATTENTION_SCRATCH_BYTES per GPU, held
+ * until the process exits; calls needing more (see
+ * lsb_paged_attention_workspace_size) fail with LSB_ERR_INVALID. All calls on a
+ * device share the array: calls that overlap on the GPU race. The first call on
+ * a device looks up the array and clears its counters (an async memset on
+ * `stream`); make it before any stream capture. Allocates nothing. */
+#define LSB_NOALLOC_ATTENTION_SCRATCH_BYTES (16 * 1024 * 1024)
+int lsb_paged_attention_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                                const void* k_cache, const void* v_cache, int64_t slot_stride,
+                                int64_t num_slots, const int32_t* page_table, int64_t pt_stride,
+                                const int32_t* cache_seqlens, const int32_t* cu_seqlens_q,
+                                int64_t num_reqs, int64_t rows, int32_t hq, int32_t hkv,
+                                int32_t head_dim, int32_t page_size, int64_t max_seqlen,
+                                float scale, void* stream);
+
 /* ------------------------------------------------------------ GEMM --------
  * y[M, N] = x[M, K] . w[N, K]^T (+ bias[N]) in bf16 with fp32 accumulation on
  * the sm_100a tensor cores (tcgen05.mma, TMEM accumulators, TMA-fed).

@@ -47,6 +47,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_paged_attention_workspace_size": (c_int64, [I64, I32, I32, I64]),
     "lsb_paged_attention": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64, P, P, I64, I64,
                                            I32, I32, I32, I32, I64, F, P, I64, P]),
+    "lsb_paged_attention_noalloc": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64, P, P,
+                                                   I64, I64, I32, I32, I32, I32, I64, F, P]),
     "lsb_gemm_workspace_size": (c_int64, [I64, I64, I64]),
     "lsb_gemm": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P, I64, P]),
     "lsb_swiglu_interleave": (ctypes.c_int, [P, P, I64, I64, P]),
