@@ -102,8 +102,9 @@ int lsb_store_kv(void* k_cache, void* v_cache, int64_t slot_stride, int64_t num_
  * Splits the keys of long rows across CTAs; the partial results go to the
  * caller's workspace (lsb_paged_attention_workspace_size bytes, zeroed once
  * before first use; its head holds arrival counters that every call leaves zeroed,
- * so one workspace serves calls of any shape). head_dim 32, 64, 96 or 128. Slots outside [0, num_slots)
- * are skipped and flagged in the device error word instead of being read.  Replaces the backends'
+ * so one workspace serves calls of any shape). head_dim 32, 64, 96 or 128.
+ * Slots outside [0, num_slots) are skipped and flagged in the device error
+ * word instead of being read.  Replaces the backends'
  * attention call (attention/trtllm.py:80-91 decode, :62-78 prefill;
  * attention/fa.py:82-93; attention/fi.py:161-199). */
 int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, int32_t head_dim,
@@ -144,8 +145,12 @@ int lsb_paged_attention_noalloc(void* out, int64_t out_stride, const void* q, in
  * LSB_EPI_SWIGLU (w rows interleaved in blocks of 64 gate / 64 up rows by
  * lsb_swiglu_interleave; y[M, N/2] = silu(g) * u of the rounded g, u).
  * Any M, N, K (ragged tails are zero-filled by TMA); SwiGLU needs N % 128 == 0;
- * ldx/ldw multiples of 8 and x, w 16-byte aligned (TMA); y any row stride. workspace: split-K arrival counters (head, left zeroed by every call)
- * and partials, lsb_gemm_workspace_size bytes, zeroed once before first use.
+ * ldx/ldw multiples of 8 and x, w 16-byte aligned (TMA); y any row stride.
+ * Split-K (when the tiles alone cannot fill the SMs) runs in thread-block
+ * clusters reduced through distributed shared memory, so no workspace is used:
+ * lsb_gemm_workspace_size returns 0 and `workspace` may be NULL. Launched with
+ * programmatic stream serialisation: the weight stream starts before the
+ * previous kernel on `stream` has finished; `x` is read only after it has.
  * Replaces layers/linear.py:32-33 (F.linear, cuBLAS) for the QKV, o_proj,
  * gate_up, down, adapter and LM-head projections, and models/utils.py:46-48
  * (gate_up + silu_and_mul) with LSB_EPI_SWIGLU. */

@@ -26,8 +26,10 @@ constexpr float kNegBig = -1e30f;
 
 __host__ __device__ constexpr int lanes_for(int d) { return d <= 32 ? 4 : (d <= 64 ? 8 : 16); }
 
+constexpr int kMaxChunk = 1024;  // keys per split (upper bound)
+
 int64_t chunk_for(int64_t rows, int32_t hq, int64_t max_seqlen) {
-  int64_t chunk = 1024;
+  int64_t chunk = kMaxChunk;
   while (chunk > 64) {
     const int64_t splits = (max_seqlen + chunk - 1) / chunk;
     if (rows * hq * splits >= 8192) break;
@@ -74,6 +76,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                            const int32_t* __restrict__ cu_seqlens_q, int num_reqs, int hq,
                            int hkv, int page_size, int64_t chunk, int64_t max_splits,
                            float scale_log2, Workspace ws, int* __restrict__ error_flag) {
+  allow_dependent_launch();
   constexpr int kLanes = lanes_for(D);        // lanes per key
   constexpr int kGroups = 32 / kLanes;        // keys per warp per load
   constexpr int kVec = D / 8;                 // active lanes per key
@@ -122,7 +125,19 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
   float m = kNegBig, l = 0.f;
 
+  // The split's page ids go to shared memory once, so the key loop issues its KV
+  // loads without a dependent page-table load in front of them.
+  __shared__ int32_t s_pages[kMaxChunk + 1];
   const int32_t* pt_row = page_table + static_cast<int64_t>(b) * pt_stride;
+  const bool pow2 = (page_size & (page_size - 1)) == 0;
+  const int pshift = __ffs(page_size) - 1;
+  const int64_t p_first = pow2 ? (k_begin >> pshift) : k_begin / page_size;
+  if (k_end > k_begin) {
+    const int64_t p_last = pow2 ? ((k_end - 1) >> pshift) : (k_end - 1) / page_size;
+    for (int64_t i = threadIdx.x; i <= p_last - p_first; i += blockDim.x)
+      s_pages[i] = pt_row[p_first + i];
+  }
+  __syncthreads();
   const int64_t head_off = static_cast<int64_t>(kvh) * D + 8 * c;
   if (head_ok) {
     for (int64_t base = k_begin; base < k_end; base += kGroups * kUnroll) {
@@ -133,8 +148,9 @@ __global__ void __launch_bounds__(kWarps * 32)
         const int64_t t = base + u * kGroups + g;
         valid[u] = t < k_end;
         if (valid[u]) {
-          const int64_t page = pt_row[t / page_size];
-          const int64_t slot = page * page_size + t % page_size;
+          const int64_t pg = pow2 ? (t >> pshift) : t / page_size;
+          const int64_t page = s_pages[pg - p_first];
+          const int64_t slot = page * page_size + (t - pg * page_size);
           if (slot < 0 || slot >= num_slots) {
             valid[u] = false;
             if (c == 0 && error_flag) atomicOr(error_flag, LSB_DEVERR_SLOT);

@@ -113,6 +113,13 @@ __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Lets a kernel launched after this one with programmatic stream serialisation (the
+// GEMM) start its prologue and weight prefetch while this grid drains; the GEMM waits
+// with griddepcontrol.wait before it reads anything this grid writes.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
 // Streaming 16-byte load that bypasses L1 (KV and weights are read once).
 __device__ __forceinline__ bf16x8 ldg_stream(const void* p) {
   uint4 r;

@@ -10,11 +10,16 @@
 //               (kind::f16, fp32 accumulator in TMEM, 4 MMAs of K=16 per stage),
 //               tcgen05.commit frees each stage and finally signals the epilogue;
 //   warps 2..5  epilogue: tcgen05.ld of the 128 x bn accumulator (warp w reads
-//               TMEM lanes 32*(w%4)..+31), fused bias / SwiGLU, bf16 stores.
-// When the tile grid alone cannot fill the 148 SMs the K loop is split across
-// CTAs (split-K): each split stores an fp32 partial to the workspace and the
-// last split to arrive (per-tile counter) sums the partials in split order —
-// deterministic — and runs the epilogue.
+//               TMEM lanes 32*(w%4)..+31) into a token-major fp32 tile in shared
+//               memory (the drained stage buffers), then coalesced 8-byte stores
+//               of 4 output columns per thread with the fused bias / SwiGLU.
+// When the tile grid alone cannot fill the SMs the K loop is split over the S
+// CTAs of a thread-block cluster: each computes a K range, and after a cluster
+// barrier every CTA sums one slice of the tile over the S shared-memory tiles
+// (distributed shared memory, fixed order: deterministic) and stores it.
+// The weight stream does not depend on the previous kernel, so the producer
+// issues the first stages' weight loads before griddepcontrol.wait (programmatic
+// dependent launch) and only the activation loads after it.
 // Every mbarrier wait is bounded: on timeout the kernel sets LSB_DEVERR_TIMEOUT
 // in the device error word and winds down instead of spinning forever.
 #include <cuda.h>
@@ -32,18 +37,13 @@ constexpr int kBK = 64;
 constexpr int kThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxStages = 8;
-constexpr int kXchStride = 17;
+constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr long long kTimeoutCycles = 4000000000LL;
-// Split-K arrival counters live in a fixed region at the head of the workspace, so
-// calls of any shape find them where the previous call left them: zero.
-constexpr int64_t kCounterBytes = 16 * 1024;
 
 struct GemmParams {
   bf16* y;
   int64_t ldy;
   const bf16* bias;
-  float* partials;  // [splits, M, N] fp32
-  int* counters;    // [tiles]
   int M, N, K;
   int bn, stages, splits, epilogue;
   uint32_t idesc;
@@ -99,6 +99,33 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+__device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(addr), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 // K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc(const void* tile) {
   const uint64_t addr = smem_u32(tile);
@@ -139,46 +166,30 @@ __device__ __forceinline__ void epi_barrier() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-// Writes 16 accumulator columns (tokens m0 .. m0+15) of weight row `row`.
-__device__ __forceinline__ void emit16(const GemmParams& p, const float* v, int m0, int row,
-                                       int q, int lane, int tile_n, float* xch) {
-  if (p.epilogue == LSB_EPI_SWIGLU) {
-    const int r = 32 * (q & 1) + lane;  // row within the 64-row half
-    if (q >= 2) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) xch[r * kXchStride + j] = round_bf16(v[j]);
-    }
-    epi_barrier();
-    if (q < 2) {
-      const int col = tile_n * 64 + r;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = m0 + j;
-        if (m < p.M) {
-          const float g = round_bf16(v[j]);
-          const float u = xch[r * kXchStride + j];
-          p.y[static_cast<int64_t>(m) * p.ldy + col] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
-        }
-      }
-    }
-    epi_barrier();
+// Four consecutive output columns col..col+3 of token m (bf16), 8-byte store when
+// aligned and in range, else element by element.
+__device__ __forceinline__ void store4(bf16* y, int64_t ldy, int m, int col, int ncols,
+                                       float a, float b, float c, float d) {
+  bf16* dst = y + static_cast<int64_t>(m) * ldy + col;
+  if (col + 3 < ncols && (reinterpret_cast<uintptr_t>(dst) & 7) == 0) {
+    uint2 packed;
+    bf162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst) = packed;
     return;
   }
-  if (row >= p.N) return;
-  float b = 0.f;
-  if (p.epilogue != LSB_EPI_NONE) b = __bfloat162float(p.bias[row]);
+  const float v[4] = {a, b, c, d};
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int m = m0 + j;
-    if (m < p.M) {
-      float o = v[j];
-      if (p.epilogue == LSB_EPI_BIAS) o += b;
-      else if (p.epilogue == LSB_EPI_BIAS_AFTER_ROUND) o = round_bf16(o) + b;
-      p.y[static_cast<int64_t>(m) * p.ldy + row] = __float2bfloat16_rn(o);
-    }
-  }
+  for (int e = 0; e < 4; ++e)
+    if (col + e < ncols) dst[e] = __float2bfloat16_rn(v[e]);
 }
 
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+template <int EPI, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
@@ -192,19 +203,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + kMaxStages;
   uint64_t* tmem_full = empty + kMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* xch = reinterpret_cast<float*>(tmem_slot + 4);
+  // After the main loop the drained stage buffers hold the token-major fp32 tile.
+  float* red = reinterpret_cast<float*>(smem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
+  const int S = CLUSTER ? p.splits : 1;
+  const int split = CLUSTER ? static_cast<int>(cluster_rank()) : 0;
+  const int tile_n = blockIdx.x / S, tile_m = blockIdx.y;
   const int n0 = tile_n * kBM, m0 = tile_m * p.bn;
   const int kblocks = (p.K + kBK - 1) / kBK;
-  const int kb_begin = static_cast<int>(static_cast<int64_t>(kblocks) * split / p.splits);
-  const int kb_end = static_cast<int>(static_cast<int64_t>(kblocks) * (split + 1) / p.splits);
+  const int kb_begin = static_cast<int>(static_cast<int64_t>(kblocks) * split / S);
+  const int kb_end = static_cast<int>(static_cast<int64_t>(kblocks) * (split + 1) / S);
   const int nk = kb_end - kb_begin;
+  // Every tile reads the same activation rows; starting each tile's K loop at a
+  // different block spreads those reads over all of x instead of having every CTA
+  // hit the same L2 lines at the same moment. (The fp32 sum order per tile changes
+  // with it; results stay deterministic.)
+  const int rot = nk > 0 ? static_cast<int>((static_cast<int64_t>(tile_n) * 7 + tile_m * 3) % nk) : 0;
   uint32_t tmem_cols = 32;
   while (tmem_cols < static_cast<uint32_t>(p.bn)) tmem_cols <<= 1;
 
+  asm volatile("griddepcontrol.launch_dependents;");
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
@@ -225,16 +244,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem_base = *tmem_slot;
+  bool have_acc = false;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
+      // Weights do not depend on the previous kernel: fetch the first stages of the
+      // weight stream, then wait for the producer of x, then fetch x.
+      const int pre = nk < stages ? nk : stages;
+      auto kx_of = [&](int i) { return (kb_begin + (i + rot) % nk) * kBK; };
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
+        tma_load_2d(smem + i * stage_bytes, &tmap_w, &full[i], kx_of(i), n0);
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * stage_bytes + kABytes, &tmap_x, &full[i], kx_of(i), m0);
+      for (int i = pre; i < nk; ++i) {
         const int s = i % stages;
         const uint32_t round = static_cast<uint32_t>(i / stages);
         if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, p.error_flag)) break;
         uint8_t* a_tile = smem + s * stage_bytes;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
-        const int kx = (kb_begin + i) * kBK;
+        const int kx = kx_of(i);
         tma_load_2d(a_tile, &tmap_w, &full[s], kx, n0);
         tma_load_2d(a_tile + kABytes, &tmap_x, &full[s], kx, m0);
       }
@@ -264,66 +295,98 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) umma_commit(tmem_full);
     }
   } else {
-    // Epilogue warps 2..5.
+    // Phase 1: accumulator (TMEM lanes = weight rows) -> red[token][row] in fp32.
     const int q = warp & 3;
-    const int row = n0 + 32 * q + lane;
-    const bool have_acc = nk > 0 && mbar_wait(tmem_full, 0, p.error_flag);
+    const int row = 32 * q + lane;
+    have_acc = nk > 0 && mbar_wait(tmem_full, 0, p.error_flag);
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
     float v[16];
-    if (p.splits == 1) {
-      for (int c0 = 0; c0 < p.bn; c0 += 16) {
-        if (have_acc) tmem_ld16(taddr + c0, v);
-        else
+    for (int c0 = 0; c0 < p.bn; c0 += 16) {
+      if (have_acc) tmem_ld16(taddr + c0, v);
+      else
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
-        if (m0 + c0 < p.M) emit16(p, v, m0 + c0, row, q, lane, tile_n, xch);
-      }
-    } else {
-      const int64_t plane = static_cast<int64_t>(p.M) * p.N;
-      float* mine = p.partials + split * plane;
-      for (int c0 = 0; c0 < p.bn; c0 += 16) {
-        if (m0 + c0 >= p.M) break;
-        if (have_acc) tmem_ld16(taddr + c0, v);
-        else
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
-        if (row < p.N) {
+      for (int j = 0; j < 16; ++j) red[(c0 + j) * kBM + row] = v[j];
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  if (CLUSTER) cluster_sync_all();
+  else __syncthreads();
+
+  if (warp >= 2) {
+    // Phase 2: 4-column quads of the output rows, summed over the cluster's tiles.
+    // Specialised at compile time (epilogue kind, one tile or a cluster): a generic
+    // loop with runtime branches compiles to a several times slower sequence.
+    constexpr bool kSwiglu = EPI == LSB_EPI_SWIGLU;
+    constexpr int kQuadShift = kSwiglu ? 4 : 5;  // 16 or 32 quads per token row
+    bf16* const y = p.y;
+    const int64_t ldy = p.ldy;
+    const int ncols = kSwiglu ? p.N / 2 : p.N;
+    const int t = threadIdx.x - 64;
+    const int tokens = p.M - m0 < p.bn ? p.M - m0 : p.bn;
+    int tb = 0, te = tokens;
+    if (CLUSTER) {  // each CTA of the cluster finishes a token slice of the tile
+      const int per = (tokens + S - 1) / S;
+      tb = split * per;
+      te = tb + per < tokens ? tb + per : tokens;
+    }
+    const int count = te > tb ? (te - tb) << kQuadShift : 0;
+    const uint32_t red_addr = smem_u32(red);
+    for (int idx = t; idx < count; idx += 128) {
+      const int qi = idx & ((1 << kQuadShift) - 1);
+      const int m = tb + (idx >> kQuadShift);
+      const int off = m * kBM + 4 * qi;
+      float4 a, u;
+      if (!CLUSTER) {
+        a = *reinterpret_cast<const float4*>(red + off);
+        if (kSwiglu) u = *reinterpret_cast<const float4*>(red + off + 64);
+      } else {
+        // issue every peer's load before summing (fixed rank order: deterministic)
+        float4 xs[kMaxSplits], gs[kMaxSplits];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < p.M) mine[static_cast<int64_t>(m) * p.N + row] = v[j];
+        for (int s2 = 0; s2 < kMaxSplits; ++s2) {
+          if (s2 < S) {
+            xs[s2] = ld_cluster_f4(map_rank(red_addr + 4u * off, s2));
+            if (kSwiglu) gs[s2] = ld_cluster_f4(map_rank(red_addr + 4u * (off + 64), s2));
+          }
+        }
+        a = make_float4(0.f, 0.f, 0.f, 0.f);
+        u = a;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxSplits; ++s2) {
+          if (s2 < S) {
+            a.x += xs[s2].x; a.y += xs[s2].y; a.z += xs[s2].z; a.w += xs[s2].w;
+            if (kSwiglu) { u.x += gs[s2].x; u.y += gs[s2].y; u.z += gs[s2].z; u.w += gs[s2].w; }
           }
         }
       }
-      __threadfence();
-      epi_barrier();
-      if (warp == 2 && lane == 0) {
-        int* counter = p.counters + tile_m * gridDim.x + tile_n;
-        const int prev = atomicAdd(counter, 1);
-        *last_flag = prev == p.splits - 1;
-        if (prev == p.splits - 1) *counter = 0;
-      }
-      epi_barrier();
-      if (*last_flag) {
-        __threadfence();
-        for (int c0 = 0; c0 < p.bn; c0 += 16) {
-          if (m0 + c0 >= p.M) break;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float* part = p.partials + s * plane;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int m = m0 + c0 + j;
-              if (m < p.M && row < p.N) v[j] += __ldcg(part + static_cast<int64_t>(m) * p.N + row);
-            }
+      if (kSwiglu) {
+        // gate_up is rounded to bf16 before the activation, as in the reference
+        store4(y, ldy, m0 + m, tile_n * 64 + 4 * qi, ncols,
+               silu_mul(round_bf16(a.x), round_bf16(u.x)), silu_mul(round_bf16(a.y), round_bf16(u.y)),
+               silu_mul(round_bf16(a.z), round_bf16(u.z)), silu_mul(round_bf16(a.w), round_bf16(u.w)));
+      } else {
+        const int col = n0 + 4 * qi;
+        float o0 = a.x, o1 = a.y, o2 = a.z, o3 = a.w;
+        if (EPI != LSB_EPI_NONE) {
+          const float b0 = col < p.N ? __bfloat162float(p.bias[col]) : 0.f;
+          const float b1 = col + 1 < p.N ? __bfloat162float(p.bias[col + 1]) : 0.f;
+          const float b2 = col + 2 < p.N ? __bfloat162float(p.bias[col + 2]) : 0.f;
+          const float b3 = col + 3 < p.N ? __bfloat162float(p.bias[col + 3]) : 0.f;
+          if (EPI == LSB_EPI_BIAS) {
+            o0 += b0; o1 += b1; o2 += b2; o3 += b3;
+          } else {
+            o0 = round_bf16(o0) + b0; o1 = round_bf16(o1) + b1;
+            o2 = round_bf16(o2) + b2; o3 = round_bf16(o3) + b3;
           }
-          emit16(p, v, m0 + c0, row, q, lane, tile_n, xch);
         }
+        store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
       }
     }
   }
+  if (CLUSTER) cluster_sync_all();  // peers may still be reading this CTA's tile
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 1) {
@@ -331,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(tmem_cols));
   }
+  (void)have_acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -396,7 +460,7 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
   const int budget = 220 * 1024;
   pl.stages = budget / stage_bytes;
   if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-  if (pl.stages < 2) pl.stages = 2;
+  if (pl.stages < 4) pl.stages = 4;  // the drained stages must hold the fp32 tile
   pl.tiles_n = static_cast<int>((N + kBM - 1) / kBM);
   pl.tiles_m = static_cast<int>((M + pl.bn - 1) / pl.bn);
   const int tiles = pl.tiles_n * pl.tiles_m;
@@ -405,19 +469,13 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
   const int sms = num_sms();
   if (tiles < sms) {
     splits = sms / tiles;
-    if (splits > kblocks / 2) splits = kblocks / 2;
-    if (splits > 16) splits = 16;
+    if (splits > kMaxSplits) splits = kMaxSplits;
+    if (splits > kblocks) splits = kblocks;
     if (splits < 1) splits = 1;
   }
   pl.splits = splits;
-  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes + (2 * kMaxStages + 1) * 8 + 16 +
-            64 * kXchStride * 4;
+  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes + (2 * kMaxStages + 1) * 8 + 16;
   return pl;
-}
-
-int64_t workspace_for(const Plan& pl, int64_t M, int64_t N) {
-  if (pl.splits <= 1) return 0;
-  return kCounterBytes + ((static_cast<int64_t>(pl.splits) * M * N * 4 + 255) & ~int64_t(255));
 }
 
 uint32_t make_idesc(int bn) {
@@ -434,14 +492,18 @@ uint32_t make_idesc(int bn) {
 using namespace lsb;
 
 extern "C" int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K <= 0) return 0;
-  return workspace_for(plan_for(M, N, K), M, N);
+  (void)M;
+  (void)N;
+  (void)K;
+  return 0;  // split-K partials are reduced in distributed shared memory
 }
 
 extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
                         int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
                         int32_t epilogue, void* workspace, int64_t workspace_bytes,
                         void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
   LSB_REQUIRE(y && x && w, "gemm: null pointer");
   LSB_REQUIRE(N > 0 && K > 0, "gemm: empty N or K (N=%lld K=%lld)", (long long)N, (long long)K);
   LSB_REQUIRE(epilogue != LSB_EPI_SWIGLU || N % kBM == 0,
@@ -459,9 +521,6 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   LSB_REQUIRE(ldy >= out_cols, "gemm: ldy too small");
   if (M <= 0) return LSB_OK;
   Plan pl = plan_for(M, N, K);
-  const int64_t need = workspace_for(pl, M, N);
-  LSB_REQUIRE(need == 0 || (workspace && workspace_bytes >= need && aligned(workspace, 256)),
-              "gemm: workspace of %lld bytes needed", (long long)need);
   CUtensorMap tw, tx;
   if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
   if (int rc = make_tmap(&tx, x, M, K, ldx, pl.bn)) return rc;
@@ -469,11 +528,6 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   p.y = static_cast<bf16*>(y);
   p.ldy = ldy;
   p.bias = static_cast<const bf16*>(bias);
-  LSB_REQUIRE(need == 0 || static_cast<int64_t>(pl.tiles_n) * pl.tiles_m * 4 <= kCounterBytes,
-              "gemm: too many split tiles");
-  p.counters = need ? static_cast<int*>(workspace) : nullptr;
-  p.partials = need ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes)
-                    : nullptr;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -483,13 +537,39 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   p.epilogue = epilogue;
   p.idesc = make_idesc(pl.bn);
   p.error_flag = lsb_device_error_flag();
-  static size_t configured = 0;
-  if (pl.smem > configured) {
-    LSB_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
+  static const Kernel kernels[2][4] = {
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false>},
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true>}};
+  static size_t configured[2][4] = {{0}};
+  const int ci = pl.splits > 1 ? 1 : 0;
+  Kernel kernel = kernels[ci][epilogue];
+  if (pl.smem > configured[ci][epilogue]) {
+    LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(pl.smem)));
-    configured = pl.smem;
+    configured[ci][epilogue] = pl.smem;
   }
-  dim3 grid(pl.tiles_n, pl.tiles_m, pl.splits);
-  gemm_tcgen05_kernel<<<grid, kThreads, pl.smem, as_stream(stream)>>>(tw, tx, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.tiles_n * pl.splits, pl.tiles_m, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attrs[2];
+  int nattr = 0;
+  attrs[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[nattr].val.programmaticStreamSerializationAllowed = 1;
+  ++nattr;
+  if (pl.splits > 1) {
+    attrs[nattr].id = cudaLaunchAttributeClusterDimension;
+    attrs[nattr].val.clusterDim.x = pl.splits;
+    attrs[nattr].val.clusterDim.y = 1;
+    attrs[nattr].val.clusterDim.z = 1;
+    ++nattr;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = nattr;
+  LSB_CUDA(cudaLaunchKernelEx(&cfg, kernel, tw, tx, p));
   return check_launch("lsb_gemm");
 }

@@ -91,6 +91,7 @@ __device__ __forceinline__ void add_residual(RowRegs& r, bf16* res, int64_t dim)
 __global__ void rmsnorm_kernel(bf16* __restrict__ out, int64_t out_stride,
                                const bf16* __restrict__ x, int64_t x_stride,
                                const bf16* __restrict__ w, int64_t dim, float eps) {
+  allow_dependent_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
@@ -102,6 +103,7 @@ __global__ void rmsnorm_kernel(bf16* __restrict__ out, int64_t out_stride,
 
 __global__ void add_rmsnorm_kernel(bf16* __restrict__ x, bf16* __restrict__ res,
                                    const bf16* __restrict__ w, int64_t dim, float eps) {
+  allow_dependent_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
@@ -127,6 +129,7 @@ __device__ __forceinline__ void sandwich_row(RowRegs& r, const bf16* x, bf16* re
 __global__ void sandwich_kernel(bf16* __restrict__ out, const bf16* x, bf16* __restrict__ res,
                                 const bf16* __restrict__ wa, const bf16* __restrict__ wb,
                                 int64_t dim, float eps) {
+  allow_dependent_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
@@ -146,6 +149,7 @@ __global__ void ouro_step_exit_kernel(bf16* hidden_out, int64_t hidden_stride, c
                                       const int32_t* __restrict__ depth, int32_t depth_scalar,
                                       int32_t lookahead, int32_t min_loop_steps, float threshold,
                                       int64_t dim, float eps) {
+  allow_dependent_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
@@ -188,6 +192,7 @@ __global__ void huginn_step_exit_kernel(bf16* hidden_out, bf16* exit_state,
                                         const int64_t* __restrict__ slot,
                                         uint8_t* __restrict__ signal, float threshold,
                                         int64_t dim) {
+  allow_dependent_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int64_t dst = slot ? slot[row] : row;
