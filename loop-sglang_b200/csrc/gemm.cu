@@ -25,6 +25,10 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 
 extern int* lsb_device_error_flag();
@@ -38,6 +42,7 @@ constexpr int kThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // portable cluster size
+constexpr int kSmemPerSm = 228 * 1024;
 constexpr long long kTimeoutCycles = 4000000000LL;
 
 struct GemmParams {
@@ -450,6 +455,99 @@ int num_sms() {
   return sms;
 }
 
+using Kernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
+
+Kernel kernel_for(bool cluster, int epilogue) {
+  static const Kernel kernels[2][4] = {
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false>},
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true>}};
+  return kernels[cluster ? 1 : 0][epilogue];
+}
+
+constexpr int kMaxSmem = 227 * 1024;
+
+// Raises a kernel's dynamic shared-memory limit once per device (needed before both
+// the launch and the occupancy queries below).
+int configure(bool cluster, int epilogue) {
+  static std::mutex mu;
+  static uint64_t done[64] = {0};  // bit (cluster*4 + epilogue) per device
+  int dev = 0;
+  LSB_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = uint64_t(1) << ((cluster ? 4 : 0) + epilogue);
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && (done[dev] & bit)) return LSB_OK;
+  LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue),
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  if (dev < 64) done[dev] |= bit;
+  return LSB_OK;
+}
+
+// Stand-in with the GEMM's block size and no tensor memory, for the occupancy query
+// below: the runtime reports one resident block per SM for the GEMM kernel itself at
+// any shared-memory size, while two 3-stage GEMM CTAs do run side by side on an SM
+// (their TMEM allocations, at most 256 columns each, fit the 512 columns of an SM).
+__global__ void __launch_bounds__(kThreads, 1) cluster_capacity_probe() {}
+
+// How many clusters of `splits` CTAs with `smem` bytes each the device runs at once
+// (the GPCs bound it: on a 148-SM B200 only 15 clusters of 8 or 45 of 3 fit with one
+// CTA per SM). Cached per device and configuration; 0 if the query fails.
+int max_active_clusters(int splits, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  static uint64_t configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const auto key = std::make_tuple(dev, splits, smem);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  bool ok = true;
+  if (dev < 64 && !(configured & (uint64_t(1) << dev))) {
+    ok = cudaFuncSetAttribute(cluster_capacity_probe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kMaxSmem) == cudaSuccess;
+    if (ok) configured |= uint64_t(1) << dev;
+  }
+  if (ok) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(splits, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = splits;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    ok = cudaOccupancyMaxActiveClusters(&n, cluster_capacity_probe, &cfg) == cudaSuccess;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+size_t smem_for(int stages, int stage_bytes) {
+  return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * kMaxStages + 1) * 8 + 16;
+}
+
+// Tile shape, pipeline depth and split-K factor. Two layouts are considered:
+//  * one CTA per SM: as many stages as fit (up to 8); the K loop is split over a
+//    cluster only as far as tiles x splits <= SMs and every cluster is co-resident;
+//  * two CTAs per SM: 3 stages (the least that still holds the fp32 tile for the
+//    epilogue), splits up to 2 x SMs / tiles.
+// The second is taken when it puts more CTAs than SMs on the device: the per-SM
+// ingest of weight and activation tiles, not the pipeline depth, then limits the
+// main loop. A split is only used when all clusters of the grid run at once; a
+// cluster left for a second wave would double the kernel's time.
 Plan plan_for(int64_t M, int64_t N, int64_t K) {
   Plan pl;
   int64_t bn = ((M + 15) / 16) * 16;
@@ -457,24 +555,37 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
   if (bn < 16) bn = 16;
   pl.bn = static_cast<int>(bn);
   const int stage_bytes = kABytes + pl.bn * kBK * 2;
-  const int budget = 220 * 1024;
-  pl.stages = budget / stage_bytes;
-  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-  if (pl.stages < 4) pl.stages = 4;  // the drained stages must hold the fp32 tile
   pl.tiles_n = static_cast<int>((N + kBM - 1) / kBM);
   pl.tiles_m = static_cast<int>((M + pl.bn - 1) / pl.bn);
   const int tiles = pl.tiles_n * pl.tiles_m;
   const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
-  int splits = 1;
   const int sms = num_sms();
-  if (tiles < sms) {
-    splits = sms / tiles;
-    if (splits > kMaxSplits) splits = kMaxSplits;
-    if (splits > kblocks) splits = kblocks;
-    if (splits < 1) splits = 1;
+
+  int stages_a = (220 * 1024) / stage_bytes;
+  if (stages_a > kMaxStages) stages_a = kMaxStages;
+  if (stages_a < 3) stages_a = 3;
+  const size_t smem_a = smem_for(stages_a, stage_bytes);
+  auto best_split = [&](int limit, size_t smem) {
+    if (limit > kMaxSplits) limit = kMaxSplits;
+    if (limit > kblocks) limit = kblocks;
+    for (int sp = limit; sp >= 2; --sp)
+      if (tiles <= max_active_clusters(sp, smem)) return sp;
+    return 1;
+  };
+  const int split_a = tiles < sms ? best_split(sms / tiles, smem_a) : 1;
+  pl.stages = stages_a;
+  pl.splits = split_a;
+  pl.smem = smem_a;
+
+  const size_t smem_b = smem_for(3, stage_bytes);
+  if (2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
+    const int split_b = tiles < 2 * sms ? best_split(2 * sms / tiles, smem_b) : 1;
+    if (static_cast<int64_t>(tiles) * split_b > sms) {
+      pl.stages = 3;
+      pl.splits = split_b;
+      pl.smem = smem_b;
+    }
   }
-  pl.splits = splits;
-  pl.smem = 1024 + static_cast<size_t>(pl.stages) * stage_bytes + (2 * kMaxStages + 1) * 8 + 16;
   return pl;
 }
 
@@ -537,20 +648,9 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   p.epilogue = epilogue;
   p.idesc = make_idesc(pl.bn);
   p.error_flag = lsb_device_error_flag();
-  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
-  static const Kernel kernels[2][4] = {
-      {gemm_tcgen05_kernel<LSB_EPI_NONE, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false>,
-       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false>},
-      {gemm_tcgen05_kernel<LSB_EPI_NONE, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true>,
-       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true>}};
-  static size_t configured[2][4] = {{0}};
-  const int ci = pl.splits > 1 ? 1 : 0;
-  Kernel kernel = kernels[ci][epilogue];
-  if (pl.smem > configured[ci][epilogue]) {
-    LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(pl.smem)));
-    configured[ci][epilogue] = pl.smem;
-  }
+  const bool cluster = pl.splits > 1;
+  if (int rc = configure(cluster, epilogue)) return rc;
+  Kernel kernel = kernel_for(cluster, epilogue);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles_n * pl.splits, pl.tiles_m, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);

@@ -1,0 +1,179 @@
+"""Single-kernel timing at the decode shapes of the looped decoder.
+
+Runs one kernel of the library on its own, at one shape, with inputs larger than
+the L2 cache, and prints one JSON line per shape with the device time per launch
+and the algorithmic bytes moved per second. The launches are captured into a
+CUDA graph so the host launch rate does not limit short kernels, and timed with
+CUDA events on the capturing stream after warm-up replays.
+
+    python loop-sglang_b200/kernel_bench.py attention --rows 143 --ctx 1448
+    python loop-sglang_b200/kernel_bench.py gemm --tokens 143 --shape qkv o gate_up down
+
+It is also the small case for profiler captures of one kernel (one KV layer of a
+few GB instead of the whole pool that the decode benchmark holds).
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import pathlib
+import sys
+
+import torch
+
+
+def _package():
+    """Import this directory as the ``loop_sglang_b200`` package when run as a script."""
+    if "loop_sglang_b200" in sys.modules:
+        return sys.modules["loop_sglang_b200"]
+    here = pathlib.Path(__file__).resolve().parent
+    spec = importlib.util.spec_from_file_location(
+        "loop_sglang_b200", here / "__init__.py", submodule_search_locations=[str(here)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["loop_sglang_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# Ouro-1.4B per-layer GEMMs at TP1: (out rows N, reduction K, SwiGLU epilogue)
+OURO_GEMMS = {
+    "qkv": (3 * 2048, 2048, False),
+    "o": (2048, 2048, False),
+    "gate_up": (2 * 5632, 2048, True),
+    "down": (2048, 5632, False),
+    "lm_head": (49152, 2048, False),
+}
+
+L2_BYTES = 126 * 2**20
+
+
+def _time_graph(fn, reps: int, warmup: int = 3) -> float:
+    """Microseconds per call of ``fn`` (reps calls captured in one graph)."""
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            fn(0)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(reps):
+            fn(i)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end)
+    del graph
+    return ms * 1e3 / reps
+
+
+def bench_attention(args, ops) -> dict:
+    """One decode launch of paged attention over one depth-indexed KV layer."""
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(args.seed)
+    rows, hq, hkv, d, page = args.rows, args.heads, args.kv_heads, args.head_dim, args.page
+    if args.ctx_spread > 0:
+        ctx = torch.randint(max(1, args.ctx - args.ctx_spread), args.ctx + args.ctx_spread + 1,
+                            (rows,), generator=gen)
+    else:
+        ctx = torch.full((rows,), args.ctx)
+    pages_per = (ctx + page - 1) // page
+    num_pages = int(pages_per.sum()) + 1
+    perm = torch.randperm(num_pages - 1, generator=gen) + 1
+    table = torch.zeros(rows, int(pages_per.max()), dtype=torch.int32)
+    off = 0
+    for r in range(rows):
+        n = int(pages_per[r])
+        table[r, :n] = perm[off:off + n].to(torch.int32)
+        off += n
+    slots = num_pages * page
+    kv = torch.empty(2, slots, hkv, d, dtype=torch.bfloat16, device=dev).normal_()
+    q = torch.randn(rows, hq, d, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(q)
+    table_d = table.to(dev)
+    seqlens = ctx.to(torch.int32).to(dev)
+    cu = torch.arange(rows + 1, dtype=torch.int32, device=dev)
+    max_seqlen = int(ctx.max())
+    scale = d ** -0.5
+
+    def launch(_i):
+        ops.paged_attention(q, kv[0], kv[1], table_d, seqlens, cu, page, max_seqlen, scale,
+                            hkv, out=out)
+
+    us = _time_graph(launch, args.reps)
+    kv_bytes = int(ctx.sum()) * hkv * d * 2 * 2
+    nbytes = kv_bytes + rows * hq * d * 2 * 2
+    return {"kernel": "paged_attention", "rows": rows, "mean_ctx": float(ctx.float().mean()),
+            "heads": hq, "kv_heads": hkv, "head_dim": d, "page_size": page,
+            "kv_layer_bytes": slots * hkv * d * 2 * 2, "algorithmic_bytes": nbytes,
+            "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}
+
+
+def bench_gemm(args, ops, name: str) -> dict:
+    """One ``y = x . w^T`` launch with the weight streamed from HBM (rotating copies)."""
+    dev = torch.device("cuda", 0)
+    n, k, swiglu = OURO_GEMMS[name]
+    m = args.tokens
+    w_bytes = n * k * 2
+    copies = max(2, math.ceil(2 * L2_BYTES / w_bytes))
+    ws = [torch.randn(n, k, dtype=torch.bfloat16, device=dev).mul_(0.02) for _ in range(copies)]
+    x = torch.randn(m, k, dtype=torch.bfloat16, device=dev)
+    cols = n // 2 if swiglu else n
+    y = torch.empty(m, cols, dtype=torch.bfloat16, device=dev)
+    epi = ops.LSB_EPI_SWIGLU if swiglu else ops.LSB_EPI_NONE
+
+    def launch(i):
+        ops.gemm(x, ws[i % copies], None, epi, out=y)
+
+    us = _time_graph(launch, args.reps)
+    nbytes = w_bytes + m * k * 2 + m * cols * 2
+    flops = 2.0 * m * n * k
+    return {"kernel": "gemm", "shape": name, "tokens": m, "N": n, "K": k, "swiglu": swiglu,
+            "weight_copies": copies, "algorithmic_bytes": nbytes, "us": round(us, 2),
+            "GBps": round(nbytes / us / 1e3, 1), "TFLOPs": round(flops / us / 1e6, 1)}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    sub = ap.add_subparsers(dest="kernel", required=True)
+    at = sub.add_parser("attention")
+    at.add_argument("--rows", type=int, default=143)
+    at.add_argument("--ctx", type=int, default=1448)
+    at.add_argument("--ctx-spread", type=int, default=0,
+                    help="contexts uniform in [ctx-spread, ctx+spread] (0: all equal)")
+    at.add_argument("--heads", type=int, default=16)
+    at.add_argument("--kv-heads", type=int, default=16)
+    at.add_argument("--head-dim", type=int, default=128)
+    at.add_argument("--page", type=int, default=16)
+    at.add_argument("--reps", type=int, default=20)
+    at.add_argument("--seed", type=int, default=0)
+    gm = sub.add_parser("gemm")
+    gm.add_argument("--tokens", type=int, default=143)
+    gm.add_argument("--shape", nargs="+", default=["qkv", "o", "gate_up", "down"],
+                    choices=sorted(OURO_GEMMS))
+    gm.add_argument("--reps", type=int, default=60)
+    args = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel_bench needs a CUDA device")
+    _package()
+    import importlib
+    ops = importlib.import_module("loop_sglang_b200.ops")
+    torch.cuda.set_device(0)
+    if args.kernel == "attention":
+        print(json.dumps(bench_attention(args, ops)), flush=True)
+    else:
+        for name in args.shape:
+            print(json.dumps(bench_gemm(args, ops, name)), flush=True)
+
+
+if __name__ == "__main__":
+    main()
