@@ -153,18 +153,21 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// Starts loading 16 accumulator columns of this thread's TMEM lane (one weight
+// row); the registers are valid after tmem_ld_wait().
+__device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 __device__ __forceinline__ void epi_barrier() {
@@ -195,7 +198,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 template <int EPI, bool CLUSTER>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -306,14 +309,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     have_acc = nk > 0 && mbar_wait(tmem_full, 0, p.error_flag);
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
-    float v[16];
-    for (int c0 = 0; c0 < p.bn; c0 += 16) {
-      if (have_acc) tmem_ld16(taddr + c0, v);
-      else
+    // Double-buffered: the load of columns c0+16.. is in flight while columns
+    // c0.. are stored (tcgen05.wait::ld waits for every earlier load).
+    uint32_t va[16], vb[16];
+    if (have_acc) {
+      tmem_ld16_issue(taddr, va);
+      tmem_ld_wait();
+    } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+      for (int j = 0; j < 16; ++j) va[j] = 0u, vb[j] = 0u;
+    }
+    for (int c0 = 0; c0 < p.bn; c0 += 32) {
+      const bool more_b = c0 + 16 < p.bn, more_a = c0 + 32 < p.bn;
+      if (have_acc && more_b) tmem_ld16_issue(taddr + c0 + 16, vb);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) red[(c0 + j) * kBM + row] = v[j];
+      for (int j = 0; j < 16; ++j) red[(c0 + j) * kBM + row] = __uint_as_float(va[j]);
+      if (have_acc) tmem_ld_wait();
+      if (!more_b) break;
+      if (have_acc && more_a) tmem_ld16_issue(taddr + c0 + 32, va);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) red[(c0 + 16 + j) * kBM + row] = __uint_as_float(vb[j]);
+      if (have_acc) tmem_ld_wait();
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -339,34 +355,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int count = te > tb ? (te - tb) << kQuadShift : 0;
     const uint32_t red_addr = smem_u32(red);
-    for (int idx = t; idx < count; idx += 128) {
-      const int qi = idx & ((1 << kQuadShift) - 1);
-      const int m = tb + (idx >> kQuadShift);
-      const int off = m * kBM + 4 * qi;
-      float4 a, u;
+    // kU quads per thread and pass: with every split's loads of all of them issued
+    // before the sums, kU x S distributed-shared-memory loads are in flight.
+    constexpr int kU = kSwiglu ? 1 : 2;
+    for (int base = t; base < count; base += 128 * kU) {
+      float4 acc[kU], accu[kU];
       if (!CLUSTER) {
-        a = *reinterpret_cast<const float4*>(red + off);
-        if (kSwiglu) u = *reinterpret_cast<const float4*>(red + off + 64);
-      } else {
-        // issue every peer's load before summing (fixed rank order: deterministic)
-        float4 xs[kMaxSplits], gs[kMaxSplits];
 #pragma unroll
-        for (int s2 = 0; s2 < kMaxSplits; ++s2) {
-          if (s2 < S) {
-            xs[s2] = ld_cluster_f4(map_rank(red_addr + 4u * off, s2));
-            if (kSwiglu) gs[s2] = ld_cluster_f4(map_rank(red_addr + 4u * (off + 64), s2));
+        for (int u2 = 0; u2 < kU; ++u2) {
+          const int idx = base + 128 * u2;
+          const int off = (tb + (idx >> kQuadShift)) * kBM + 4 * (idx & ((1 << kQuadShift) - 1));
+          if (idx < count) {
+            acc[u2] = *reinterpret_cast<const float4*>(red + off);
+            if (kSwiglu) accu[u2] = *reinterpret_cast<const float4*>(red + off + 64);
           }
         }
-        a = make_float4(0.f, 0.f, 0.f, 0.f);
-        u = a;
+      } else {
+        float4 xs[kU][kMaxSplits], gs[kU][kMaxSplits];
 #pragma unroll
         for (int s2 = 0; s2 < kMaxSplits; ++s2) {
-          if (s2 < S) {
-            a.x += xs[s2].x; a.y += xs[s2].y; a.z += xs[s2].z; a.w += xs[s2].w;
-            if (kSwiglu) { u.x += gs[s2].x; u.y += gs[s2].y; u.z += gs[s2].z; u.w += gs[s2].w; }
+#pragma unroll
+          for (int u2 = 0; u2 < kU; ++u2) {
+            const int idx = base + 128 * u2;
+            const int off = (tb + (idx >> kQuadShift)) * kBM + 4 * (idx & ((1 << kQuadShift) - 1));
+            if (s2 < S && idx < count) {
+              xs[u2][s2] = ld_cluster_f4(map_rank(red_addr + 4u * off, s2));
+              if (kSwiglu) gs[u2][s2] = ld_cluster_f4(map_rank(red_addr + 4u * (off + 64), s2));
+            }
+          }
+        }
+        // summed in split order: deterministic
+#pragma unroll
+        for (int u2 = 0; u2 < kU; ++u2) {
+          acc[u2] = make_float4(0.f, 0.f, 0.f, 0.f);
+          accu[u2] = acc[u2];
+#pragma unroll
+          for (int s2 = 0; s2 < kMaxSplits; ++s2) {
+            if (s2 < S) {
+              acc[u2].x += xs[u2][s2].x; acc[u2].y += xs[u2][s2].y;
+              acc[u2].z += xs[u2][s2].z; acc[u2].w += xs[u2][s2].w;
+              if (kSwiglu) {
+                accu[u2].x += gs[u2][s2].x; accu[u2].y += gs[u2][s2].y;
+                accu[u2].z += gs[u2][s2].z; accu[u2].w += gs[u2][s2].w;
+              }
+            }
           }
         }
       }
+#pragma unroll
+      for (int u2 = 0; u2 < kU; ++u2) {
+      const int idx = base + 128 * u2;
+      if (idx >= count) break;
+      const int qi = idx & ((1 << kQuadShift) - 1);
+      const int m = tb + (idx >> kQuadShift);
+      const float4 a = acc[u2], u = accu[u2];
       if (kSwiglu) {
         // gate_up is rounded to bf16 before the activation, as in the reference
         store4(y, ldy, m0 + m, tile_n * 64 + 4 * qi, ncols,
@@ -388,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
+      }
       }
     }
   }
