@@ -49,6 +49,11 @@ MID = 128  # decode position inside the generation when timing starts
 SEED = 0
 
 
+# Measured DRAM traffic of the decode attention kernel per context token (K+V of 16
+# heads x 128 = 8192 algorithmic bytes), from the ncu capture in profiles/.
+ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8220.5
+
+
 def log(msg: str) -> None:
     print(msg, file=sys.stderr, flush=True)
 
@@ -351,6 +356,10 @@ def run_b200(args) -> None:
     step_bytes = weight_bytes + kv_bytes
     peak, peak_kind = peaks()
     achieved = attn_bytes / attn_s / 1e9
+    # DRAM bytes per launch: ncu's dram__bytes_read.sum + dram__bytes_write.sum of one
+    # launch of the same kernel on a one-layer case (profiles/paged_attention_*.md),
+    # per context token, scaled by this batch's context tokens (traffic grows with them).
+    traffic = ATTN_DRAM_BYTES_PER_CTX_TOKEN * int(ctx.sum().item())
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_max / args.steps,
@@ -364,7 +373,7 @@ def run_b200(args) -> None:
                    "l2": "inputs larger than L2 (each step streams the KV pool, ~%d GB)"
                          % (step_bytes // 10**9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": round(traffic),
                      "kernel": "paged_attention (layer-0 decode, whole running batch)",
                      "peak_kind": peak_kind,
                      "step_frac": round(step_bytes / (t_max / 1000.0 / args.steps) / 1e9 / peak

@@ -13,6 +13,7 @@
 // workspace; the last CTA of the row to finish (a per-row arrival counter)
 // merges them and resets the counter, so one launch serves a whole layer.
 #include "common.cuh"
+#include "mbarrier.cuh"
 
 extern int* lsb_device_error_flag();
 
@@ -75,7 +76,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                            const int32_t* __restrict__ cache_seqlens,
                            const int32_t* __restrict__ cu_seqlens_q, int num_reqs, int hq,
                            int hkv, int page_size, int64_t chunk, int64_t max_splits,
-                           float scale_log2, Workspace ws, int* __restrict__ error_flag) {
+                           int64_t max_seqlen, float scale_log2, Workspace ws,
+                           int* __restrict__ error_flag) {
   allow_dependent_launch();
   constexpr int kLanes = lanes_for(D);        // lanes per key
   constexpr int kGroups = 32 / kLanes;        // keys per warp per load
@@ -97,9 +99,9 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int b = lo;
   const int64_t q_end = cu_seqlens_q[b + 1];
   int64_t kv_len = static_cast<int64_t>(cache_seqlens[b]) - (q_end - 1 - row);
-  if (kv_len > chunk * max_splits) {
+  if (kv_len > max_seqlen) {  // cut at max_seqlen (flagged): the page table ends there
     if (threadIdx.x == 0 && error_flag) atomicOr(error_flag, LSB_DEVERR_SEQLEN);
-    kv_len = chunk * max_splits;
+    kv_len = max_seqlen;
   }
   const int64_t nsplit = kv_len > 0 ? (kv_len + chunk - 1) / chunk : 1;
   if (split >= nsplit) return;
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   __syncthreads();
   __shared__ int is_last;
   if (threadIdx.x == 0) {
-    int* counter = ws.counters + row * groups_per_row + hgroup;
+    int* counter = ws.counters + 2 + row * groups_per_row + hgroup;  // [0], [1]: stream queue
     const int prev = atomicAdd(counter, 1);
     is_last = prev == nsplit - 1;
     if (is_last) *counter = 0;  // every split has arrived: reset for the next launch
@@ -269,17 +271,522 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Streaming kernel (up to 64 query heads): persistent CTAs fed by bulk copies.
+//
+// One CTA per SM takes work items from a queue in the workspace head; an item is
+// one query row and one split of `chunk` keys, numbered split-major so the short
+// last splits of long rows come last. Warp 0 is the producer: for each item it
+// copies the row's q (all heads) into one of two q buffers and streams the
+// split's keys in stages of T tokens -- the K and V rows of every KV head of a
+// token (hkv x D x 2 bytes each) -- with cp.async.bulk into a ring of shared-memory
+// stages (one copy per run of consecutive slots inside a page), completing on the
+// stage's mbarrier. The 16 consumer warps compute from shared memory: warp w owns
+// query heads w, w+16, w+32, w+48; within a warp, lane groups of kLanes lanes own
+// one key each (8 head dims per lane) and 4 keys per lane group are reduced
+// together (a transposing butterfly: 5 shuffles instead of 16 for 4 dot products
+// over 16 lanes). The online softmax, the split partials and the last-arriving
+// merge are those of the kernel above, with one arrival counter per (row, consumer
+// warp).
+// ---------------------------------------------------------------------------
+constexpr int kConsumerWarps = 16;
+constexpr int kStreamThreads = 32 * (kConsumerWarps + 1);
+constexpr int kStreamMaxHeads = 4 * kConsumerWarps;
+constexpr int kStreamUnroll = 4;             // keys per lane group per stage
+constexpr int kStreamStageBudget = 64 * 1024;  // bytes of K + V per stage
+constexpr int kStreamSmemBudget = 220 * 1024;
+constexpr int kMaxStreamStages = 8;
+constexpr int kRowCounterBase = 2;  // counters[0]: next item, [1]: CTAs finished
+
+enum : int { kItemFirst = 1, kItemLast = 2, kStreamExit = 4 };
+
+struct StageHdr {
+  int row, split, nsplit, t0, ntok, flags, qbuf;
+  uint32_t valid;  // bit i: key t0 + i has a slot inside the pool
+};
+
+struct StreamParams {
+  bf16* out;
+  int64_t out_stride;
+  const bf16* q;
+  int64_t q_stride;
+  const bf16* k_cache;
+  const bf16* v_cache;
+  int64_t slot_stride, num_slots;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  const int32_t* cache_seqlens;
+  const int32_t* cu_seqlens_q;
+  int num_reqs, rows, hq, hkv, page_size;
+  int chunk, max_splits, stages;
+  int64_t max_seqlen;
+  float scale_log2;
+  Workspace ws;
+  int* error_flag;
+};
+
+__host__ __device__ constexpr int stream_tokens(int d) { return (32 / lanes_for(d)) * kStreamUnroll; }
+
+struct StreamLayout {
+  int stage_bytes, q_bytes, pages_cap;
+  int off_q, off_pages, off_hdr, off_bar, total;
+};
+
+__host__ __device__ inline StreamLayout stream_layout(int d, int hq, int hkv, int chunk,
+                                                      int page_size, int stages) {
+  StreamLayout L;
+  const int row_bytes = hkv * d * 2;
+  L.stage_bytes = 2 * stream_tokens(d) * row_bytes;
+  L.q_bytes = (hq * d * 2 + 127) & ~127;
+  L.pages_cap = chunk / page_size + 2;
+  L.off_q = stages * L.stage_bytes;
+  L.off_pages = L.off_q + 2 * L.q_bytes;
+  L.off_hdr = L.off_pages + ((L.pages_cap * 4 + 15) & ~15);
+  L.off_bar = L.off_hdr + kMaxStreamStages * static_cast<int>(sizeof(StageHdr));
+  L.off_bar = (L.off_bar + 15) & ~15;
+  L.total = L.off_bar + (2 * kMaxStreamStages + 4) * 8 + 16;
+  return L;
+}
+
+// Sum over the kL lanes of a key group of 4 values per lane. Lane i of the group ends
+// up with the total of value 2*bit(kL/2) + bit(kL/4) of its lane index.
+template <int kL>
+__device__ __forceinline__ float butterfly4(float v0, float v1, float v2, float v3, int lane) {
+  const bool b1 = lane & (kL / 2);
+  float k0 = b1 ? v2 : v0, k1 = b1 ? v3 : v1;
+  const float s0 = b1 ? v0 : v2, s1 = b1 ? v1 : v3;
+  k0 += __shfl_xor_sync(0xffffffffu, s0, kL / 2);
+  k1 += __shfl_xor_sync(0xffffffffu, s1, kL / 2);
+  const bool b0 = lane & (kL / 4);
+  float k = b0 ? k1 : k0;
+  const float sx = b0 ? k0 : k1;
+  k += __shfl_xor_sync(0xffffffffu, sx, kL / 4);
+#pragma unroll
+  for (int o = kL / 8; o > 0; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
+  return k;
+}
+
+template <int D, int HPW>
+__global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kernel(StreamParams p) {
+  allow_dependent_launch();
+  constexpr int kLanes = lanes_for(D);
+  constexpr int kGroups = 32 / kLanes;
+  constexpr int kVec = D / 8;
+  constexpr int T = stream_tokens(D);
+  extern __shared__ __align__(128) uint8_t smem[];
+  const StreamLayout L = stream_layout(D, p.hq, p.hkv, p.chunk, p.page_size, p.stages);
+  const int row_bytes = p.hkv * D * 2;
+  uint8_t* const sq = smem + L.off_q;
+  int32_t* const s_pages = reinterpret_cast<int32_t*>(smem + L.off_pages);
+  StageHdr* const hdr = reinterpret_cast<StageHdr*>(smem + L.off_hdr);
+  uint64_t* const full = reinterpret_cast<uint64_t*>(smem + L.off_bar);
+  uint64_t* const empty = full + kMaxStreamStages;
+  uint64_t* const qfull = empty + kMaxStreamStages;
+  uint64_t* const qempty = qfull + 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int stages = p.stages;
+  int* const queue = p.ws.counters;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&qfull[b], 1);
+      mbar_init(&qempty[b], kConsumerWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ----------------------------------------------------------- producer --
+    const bool pow2 = (p.page_size & (p.page_size - 1)) == 0;
+    const int pshift = __ffs(p.page_size) - 1;
+    const int total = p.max_splits * p.rows;
+    const int q_copy = p.hq * D * 2;
+    int gs = 0, nitem = 0;
+    bool ok = true;
+    while (ok) {
+      int item = 0;
+      if (lane == 0) item = atomicAdd(queue, 1);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= total) break;
+      const int split = item / p.rows;
+      const int row = item - split * p.rows;
+      int lo = 0, hi = p.num_reqs - 1;  // request of the row
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.cu_seqlens_q[mid] <= row) lo = mid; else hi = mid - 1;
+      }
+      const int b = lo;
+      int64_t kv_len = static_cast<int64_t>(p.cache_seqlens[b]) - (p.cu_seqlens_q[b + 1] - 1 - row);
+      // a context longer than max_seqlen is cut there (and flagged): the page table of
+      // the row has no entries beyond it
+      const int64_t cap = p.max_seqlen;
+      if (kv_len > cap) {
+        if (lane == 0 && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SEQLEN);
+        kv_len = cap;
+      }
+      const int nsplit = kv_len > 0 ? static_cast<int>((kv_len + p.chunk - 1) / p.chunk) : 1;
+      if (split >= nsplit) continue;
+      const int k_begin = split * p.chunk;
+      const int k_end = static_cast<int>(kv_len < k_begin + p.chunk ? kv_len : k_begin + p.chunk);
+      const int p_first = pow2 ? (k_begin >> pshift) : k_begin / p.page_size;
+      if (k_end > k_begin) {
+        const int p_last = pow2 ? ((k_end - 1) >> pshift) : (k_end - 1) / p.page_size;
+        const int32_t* pt_row = p.page_table + static_cast<int64_t>(b) * p.pt_stride;
+        for (int i = lane; i <= p_last - p_first; i += 32) s_pages[i] = pt_row[p_first + i];
+      }
+      __syncwarp();
+      const int qb = nitem & 1;
+      const uint32_t quse = static_cast<uint32_t>(nitem >> 1);
+      ++nitem;
+      if (lane == 0) {
+        if (!mbar_wait(&qempty[qb], (quse & 1u) ^ 1u, p.error_flag)) ok = false;
+        if (ok) {
+          mbar_expect_tx(&qfull[qb], static_cast<uint32_t>(q_copy));
+          bulk_load(sq + qb * L.q_bytes, p.q + static_cast<int64_t>(row) * p.q_stride,
+                    static_cast<uint32_t>(q_copy), &qfull[qb]);
+        }
+        int t0 = k_begin;
+        while (ok) {
+          const int ntok = k_end - t0 < T ? (k_end - t0 > 0 ? k_end - t0 : 0) : T;
+          const int s = gs % stages;
+          const uint32_t use = static_cast<uint32_t>(gs / stages);
+          ++gs;
+          if (!mbar_wait(&empty[s], (use & 1u) ^ 1u, p.error_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* const sk = smem + s * L.stage_bytes;
+          uint8_t* const sv = sk + T * row_bytes;
+          uint32_t valid = 0, bytes = 0;
+          int run_i = 0, run_n = 0;
+          int64_t run_slot = 0;
+          auto flush = [&]() {
+            if (run_n == 0) return;
+            const uint32_t nb = static_cast<uint32_t>(run_n * row_bytes);
+            bulk_load(sk + run_i * row_bytes, p.k_cache + run_slot * p.slot_stride, nb, &full[s]);
+            bulk_load(sv + run_i * row_bytes, p.v_cache + run_slot * p.slot_stride, nb, &full[s]);
+            bytes += 2 * nb;
+            run_n = 0;
+          };
+          const bool packed = p.slot_stride == static_cast<int64_t>(p.hkv) * D;
+          // A stage inside one page of a packed pool is one run: two copies, no per-key work.
+          int i_begin = 0;
+          if (packed && ntok > 0) {
+            const int pg0 = pow2 ? (t0 >> pshift) : t0 / p.page_size;
+            const int pg1 = pow2 ? ((t0 + ntok - 1) >> pshift) : (t0 + ntok - 1) / p.page_size;
+            const int64_t slot0 = static_cast<int64_t>(s_pages[pg0 - p_first]) * p.page_size +
+                                  (t0 - pg0 * p.page_size);
+            if (pg0 == pg1 && slot0 >= 0 && slot0 + ntok <= p.num_slots) {
+              run_i = 0;
+              run_slot = slot0;
+              run_n = ntok;
+              valid = ntok == 32 ? 0xffffffffu : ((1u << ntok) - 1u);
+              i_begin = ntok;
+            }
+          }
+          for (int i = i_begin; i < ntok; ++i) {
+            const int t = t0 + i;
+            const int pg = pow2 ? (t >> pshift) : t / p.page_size;
+            const int64_t slot = static_cast<int64_t>(s_pages[pg - p_first]) * p.page_size +
+                                 (t - pg * p.page_size);
+            if (slot < 0 || slot >= p.num_slots) {
+              if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+              flush();
+              continue;
+            }
+            valid |= 1u << i;
+            if (run_n > 0 && packed && slot == run_slot + run_n && i == run_i + run_n) {
+              ++run_n;
+            } else {
+              flush();
+              run_i = i;
+              run_slot = slot;
+              run_n = 1;
+            }
+          }
+          flush();
+          StageHdr h;
+          h.row = row;
+          h.split = split;
+          h.nsplit = nsplit;
+          h.t0 = t0;
+          h.ntok = ntok;
+          h.flags = (t0 == k_begin ? kItemFirst : 0) | (t0 + T >= k_end ? kItemLast : 0);
+          h.qbuf = qb;
+          h.valid = valid;
+          hdr[s] = h;
+          mbar_expect_tx(&full[s], bytes);  // the producer's arrival (release) + the copies' bytes
+          t0 += T;
+          if (t0 >= k_end) break;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    }
+    if (lane == 0 && ok) {
+      const int s = gs % stages;
+      const uint32_t use = static_cast<uint32_t>(gs / stages);
+      if (mbar_wait(&empty[s], (use & 1u) ^ 1u, p.error_flag)) {
+        hdr[s].flags = kStreamExit;
+        mbar_arrive(&full[s]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- consumers --
+    const int cw = warp - 1;
+    const int g = lane / kLanes;
+    const int c = lane % kLanes;
+    const bool dim_ok = c < kVec;
+    const int group_base = lane & ~(kLanes - 1);
+    const int qpk = p.hq / p.hkv;
+    float qv[HPW][8], acc[HPW][8], m[HPW], l[HPW];
+    int gs = 0, nitem = 0;
+    while (true) {
+      const int s = gs % stages;
+      const uint32_t use = static_cast<uint32_t>(gs / stages);
+      ++gs;
+      if (!mbar_wait(&full[s], use & 1u, p.error_flag)) break;
+      const StageHdr hd = hdr[s];
+      if (hd.flags & kStreamExit) break;
+      if (hd.flags & kItemFirst) {
+        const uint32_t quse = static_cast<uint32_t>(nitem >> 1);
+        ++nitem;
+        if (!mbar_wait(&qfull[hd.qbuf], quse & 1u, p.error_flag)) break;
+        const uint8_t* qrow = sq + hd.qbuf * L.q_bytes;
+#pragma unroll
+        for (int j = 0; j < HPW; ++j) {
+          const int h = cw + kConsumerWarps * j;
+          if (h < p.hq && dim_ok) {
+            unpack8(*reinterpret_cast<const bf16x8*>(qrow + (h * D + 8 * c) * 2), qv[j]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qv[j][e] *= p.scale_log2;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) qv[j][e] = 0.f;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[j][e] = 0.f;
+          m[j] = kNegBig;
+          l[j] = 0.f;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&qempty[hd.qbuf]);
+      }
+      const uint8_t* sk = smem + s * L.stage_bytes;
+      const uint8_t* sv = sk + T * row_bytes;
+      bool kvalid[kStreamUnroll];
+#pragma unroll
+      for (int u = 0; u < kStreamUnroll; ++u) {
+        const int i = u * kGroups + g;
+        kvalid[u] = i < hd.ntok && ((hd.valid >> i) & 1u);
+      }
+#pragma unroll
+      for (int j = 0; j < HPW; ++j) {
+        const int h = cw + kConsumerWarps * j;
+        if (h >= p.hq) break;
+        const int off = (h / qpk) * D * 2 + 16 * c;
+        float part[kStreamUnroll];
+#pragma unroll
+        for (int u = 0; u < kStreamUnroll; ++u) {
+          part[u] = 0.f;
+          if (dim_ok) {
+            float kf[8];
+            unpack8(*reinterpret_cast<const bf16x8*>(sk + (u * kGroups + g) * row_bytes + off), kf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) part[u] = fmaf(qv[j][e], kf[e], part[u]);
+          }
+        }
+        const float red = butterfly4<kLanes>(part[0], part[1], part[2], part[3], lane);
+        float sc[kStreamUnroll];
+#pragma unroll
+        for (int u = 0; u < kStreamUnroll; ++u) {
+          const int src = group_base + (u >> 1) * (kLanes / 2) + (u & 1) * (kLanes / 4);
+          const float v = __shfl_sync(0xffffffffu, red, src);
+          sc[u] = kvalid[u] ? v : kNegBig;
+        }
+        float mx = m[j];
+#pragma unroll
+        for (int u = 0; u < kStreamUnroll; ++u) mx = fmaxf(mx, sc[u]);
+        const float corr = exp2f(m[j] - mx);
+        l[j] *= corr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[j][e] *= corr;
+#pragma unroll
+        for (int u = 0; u < kStreamUnroll; ++u) {
+          if (kvalid[u]) {
+            const float pr = exp2f(sc[u] - mx);
+            l[j] += pr;
+            if (dim_ok) {
+              float vf[8];
+              unpack8(*reinterpret_cast<const bf16x8*>(sv + (u * kGroups + g) * row_bytes + off), vf);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[j][e] = fmaf(pr, vf[e], acc[j][e]);
+            }
+          }
+        }
+        m[j] = mx;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (!(hd.flags & kItemLast)) continue;
+
+      // ---- end of an item: merge the lane groups, publish, maybe merge the row
+      const int64_t row = hd.row;
+#pragma unroll
+      for (int j = 0; j < HPW; ++j) {
+#pragma unroll
+        for (int o = kLanes; o < 32; o <<= 1) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, m[j], o);
+          const float l2 = __shfl_xor_sync(0xffffffffu, l[j], o);
+          const float mn = fmaxf(m[j], m2);
+          const float c1 = exp2f(m[j] - mn), c2 = exp2f(m2 - mn);
+          l[j] = l[j] * c1 + l2 * c2;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            acc[j][e] = acc[j][e] * c1 + __shfl_xor_sync(0xffffffffu, acc[j][e], o) * c2;
+          m[j] = mn;
+        }
+      }
+      const bool writer = g == 0 && dim_ok;
+      if (hd.nsplit == 1) {
+#pragma unroll
+        for (int j = 0; j < HPW; ++j) {
+          const int h = cw + kConsumerWarps * j;
+          if (h < p.hq && writer) {
+            const float inv = l[j] > 0.f ? 1.f / l[j] : 0.f;
+            float o8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o8[e] = acc[j][e] * inv;
+            *reinterpret_cast<bf16x8*>(p.out + row * p.out_stride + int64_t(h) * D + 8 * c) = pack8(o8);
+          }
+        }
+        continue;
+      }
+#pragma unroll
+      for (int j = 0; j < HPW; ++j) {
+        const int h = cw + kConsumerWarps * j;
+        if (h < p.hq && writer) {
+          const int64_t idx = (row * p.hq + h) * p.max_splits + hd.split;
+          float4* po = reinterpret_cast<float4*>(p.ws.partial_o + idx * D + 8 * c);
+          po[0] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+          po[1] = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
+          if (c == 0) *reinterpret_cast<float2*>(p.ws.partial_ml + idx * 2) = make_float2(m[j], l[j]);
+        }
+      }
+      // One arrival counter per (row, consumer warp): the warp that completes a row's
+      // set of splits merges its own heads, without waiting for the other warps.
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        int* counter = p.ws.counters + kRowCounterBase + row * kConsumerWarps + cw;
+        const int prev = atomicAdd(counter, 1);
+        last = prev == hd.nsplit - 1;
+        if (last) *counter = 0;  // every split has arrived: reset for the next launch
+      }
+      if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+      __threadfence();
+      constexpr int kQuads = D / 4;
+      for (int j = 0; j < HPW; ++j) {
+        const int h = cw + kConsumerWarps * j;
+        if (h >= p.hq) break;
+        const int64_t base_idx = (row * p.hq + h) * p.max_splits;
+        float mt = kNegBig, lt = 0.f;
+        float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s2 = 0; s2 < hd.nsplit; ++s2) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws.partial_ml + (base_idx + s2) * 2));
+          const float mn = fmaxf(mt, ml.x);
+          const float c1 = exp2f(mt - mn), c2 = exp2f(ml.x - mn);
+          lt = lt * c1 + ml.y * c2;
+          float4 po = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (lane < kQuads)
+            po = __ldcg(reinterpret_cast<const float4*>(p.ws.partial_o + (base_idx + s2) * D) + lane);
+          ot.x = ot.x * c1 + po.x * c2;
+          ot.y = ot.y * c1 + po.y * c2;
+          ot.z = ot.z * c1 + po.z * c2;
+          ot.w = ot.w * c1 + po.w * c2;
+          mt = mn;
+        }
+        if (lane < kQuads) {
+          const float inv = lt > 0.f ? 1.f / lt : 0.f;
+          bf162* dst = reinterpret_cast<bf162*>(p.out + row * p.out_stride + int64_t(h) * D + 4 * lane);
+          dst[0] = __floats2bfloat162_rn(ot.x * inv, ot.y * inv);
+          dst[1] = __floats2bfloat162_rn(ot.z * inv, ot.w * inv);
+        }
+      }
+    }
+  }
+  // Every CTA has drained the queue once the finished count reaches the grid: the
+  // last one resets both counters for the next launch.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(queue + 1, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      queue[0] = 0;
+      queue[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+int num_sms_attention() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+      cudaGetLastError();
+      sms = 148;
+    }
+  }
+  return sms;
+}
+
+// Keys per item for the streaming kernel: enough items for about 16 per SM (so the
+// queue balances rows of different lengths), at least one stage, at most 1024.
+int64_t stream_chunk_for(int64_t rows, int64_t max_seqlen, int d) {
+  const int64_t want = 16 * static_cast<int64_t>(num_sms_attention());
+  int64_t chunk = 1024;
+  const int64_t floor_chunk = stream_tokens(d) > 64 ? stream_tokens(d) : 64;
+  while (chunk > floor_chunk && rows * ((max_seqlen + chunk - 1) / chunk) < want) chunk >>= 1;
+  return chunk;
+}
+
+bool stream_eligible(int32_t hq, int32_t hkv, int32_t d) {
+  return hq <= kStreamMaxHeads && 2 * stream_tokens(d) * hkv * d * 2 <= kStreamStageBudget;
+}
+
 }  // namespace
 }  // namespace lsb
 
 using namespace lsb;
 
+// The streaming kernel runs when its stage fits and its per-(row, warp) counters fit
+// the counter region; otherwise the per-CTA kernel does.
+static bool use_stream(int64_t rows, int32_t hq, int32_t hkv, int32_t d) {
+  return stream_eligible(hq, hkv, d) &&
+         rows * kConsumerWarps <= kCounterCap - kRowCounterBase;
+}
+
 extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, int32_t head_dim,
                                                       int64_t max_seqlen) {
   if (rows <= 0 || hq <= 0 || head_dim <= 0 || max_seqlen <= 0) return 0;
+  // Sized for whichever kernel the call may take (the KV head count is not an argument).
   const int64_t chunk = chunk_for(rows, hq, max_seqlen);
   const int64_t splits = (max_seqlen + chunk - 1) / chunk;
-  return workspace_bytes_for(rows, hq, head_dim, splits);
+  int64_t bytes = workspace_bytes_for(rows, hq, head_dim, splits);
+  if (hq <= kStreamMaxHeads) {
+    const int64_t sc = stream_chunk_for(rows, max_seqlen, head_dim);
+    const int64_t b2 = workspace_bytes_for(rows, hq, head_dim, (max_seqlen + sc - 1) / sc);
+    if (b2 > bytes) bytes = b2;
+  }
+  return bytes;
 }
 
 extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
@@ -303,6 +810,65 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
               "paged_attention: strides must be multiples of 8 elements");
   LSB_REQUIRE(slot_stride >= (int64_t)hkv * head_dim, "paged_attention: slot stride too small");
   if (rows <= 0) return LSB_OK;
+  if (use_stream(rows, hq, hkv, head_dim)) {
+    const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim);
+    const int64_t splits = (max_seqlen + chunk - 1) / chunk;
+    LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
+                "paged_attention: max_seqlen too large");
+    const int64_t need = workspace_bytes_for(rows, hq, head_dim, splits);
+    LSB_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+                "paged_attention: workspace of %lld bytes needed", (long long)need);
+    StreamParams sp;
+    sp.out = static_cast<bf16*>(out);
+    sp.out_stride = out_stride;
+    sp.q = static_cast<const bf16*>(q);
+    sp.q_stride = q_stride;
+    sp.k_cache = static_cast<const bf16*>(k_cache);
+    sp.v_cache = static_cast<const bf16*>(v_cache);
+    sp.slot_stride = slot_stride;
+    sp.num_slots = num_slots;
+    sp.page_table = page_table;
+    sp.pt_stride = pt_stride;
+    sp.cache_seqlens = cache_seqlens;
+    sp.cu_seqlens_q = cu_seqlens_q;
+    sp.num_reqs = static_cast<int>(num_reqs);
+    sp.rows = static_cast<int>(rows);
+    sp.hq = hq;
+    sp.hkv = hkv;
+    sp.page_size = page_size;
+    sp.chunk = static_cast<int>(chunk);
+    sp.max_splits = static_cast<int>(splits);
+    sp.max_seqlen = max_seqlen;
+    sp.scale_log2 = scale * kLog2e;
+    sp.ws = carve(workspace, rows, hq, head_dim, splits);
+    sp.error_flag = lsb_device_error_flag();
+    const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0);
+    int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
+    if (stages > kMaxStreamStages) stages = kMaxStreamStages;
+    LSB_REQUIRE(stages >= 2, "paged_attention: stage of %d bytes too large", probe.stage_bytes);
+    sp.stages = stages;
+    const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages);
+    const int64_t items = rows * splits;
+    const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
+    const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
+    auto launch = [&](auto kernel) -> int {
+      LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    lay.total));
+      kernel<<<grid, kStreamThreads, lay.total, as_stream(stream)>>>(sp);
+      return check_launch("lsb_paged_attention");
+    };
+#define LSB_STREAM_DISPATCH(DIM)                                                  \
+    if (head_dim == DIM) {                                                        \
+      if (hpw == 1) return launch(paged_attention_stream_kernel<DIM, 1>);         \
+      if (hpw == 2) return launch(paged_attention_stream_kernel<DIM, 2>);         \
+      return launch(paged_attention_stream_kernel<DIM, 4>);                       \
+    }
+    LSB_STREAM_DISPATCH(32)
+    LSB_STREAM_DISPATCH(64)
+    LSB_STREAM_DISPATCH(96)
+    LSB_STREAM_DISPATCH(128)
+#undef LSB_STREAM_DISPATCH
+  }
   const int64_t chunk = chunk_for(rows, hq, max_seqlen);
   const int64_t splits = (max_seqlen + chunk - 1) / chunk;
   LSB_REQUIRE(splits <= 65535, "paged_attention: max_seqlen too large");
@@ -311,7 +877,7 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
               "paged_attention: workspace of %lld bytes needed", (long long)need);
   const int groups = (hq + kWarps - 1) / kWarps;
   LSB_REQUIRE(rows * groups < (int64_t(1) << 31), "paged_attention: too many rows");
-  LSB_REQUIRE(splits == 1 || rows * groups <= kCounterCap,
+  LSB_REQUIRE(splits == 1 || rows * groups <= kCounterCap - 2,
               "paged_attention: %lld rows x %d head groups exceed the %lld split counters",
               (long long)rows, groups, (long long)kCounterCap);
   Workspace ws = splits > 1 ? carve(workspace, rows, hq, head_dim, splits) : Workspace{};
@@ -322,8 +888,8 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
         static_cast<bf16*>(out), out_stride, static_cast<const bf16*>(q), q_stride,
         static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache), slot_stride,
         num_slots, page_table, pt_stride, cache_seqlens, cu_seqlens_q,
-        static_cast<int>(num_reqs), hq, hkv, page_size, chunk, splits, scale_log2, ws,
-        lsb_device_error_flag());
+        static_cast<int>(num_reqs), hq, hkv, page_size, chunk, splits, max_seqlen, scale_log2,
+        ws, lsb_device_error_flag());
   };
   if (head_dim == 32) launch(paged_attention_kernel<32>);
   else if (head_dim == 64) launch(paged_attention_kernel<64>);

@@ -30,6 +30,7 @@
 #include <tuple>
 
 #include "common.cuh"
+#include "mbarrier.cuh"
 
 extern int* lsb_device_error_flag();
 
@@ -43,7 +44,6 @@ constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kSmemPerSm = 228 * 1024;
-constexpr long long kTimeoutCycles = 4000000000LL;
 
 struct GemmParams {
   bf16* y;
@@ -54,46 +54,6 @@ struct GemmParams {
   uint32_t idesc;
   int* error_flag;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait: false (and the timeout bit set) if the phase never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(addr, parity)) {
-    if (clock64() - t0 > kTimeoutCycles) {
-      if (err) atomicOr(err, LSB_DEVERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {

@@ -156,6 +156,52 @@ def test_paged_attention(d: int, page: int, mode: str) -> None:
     no_device_errors()
 
 
+@pytest.mark.parametrize("hq,hkv,d,page", [
+    (55, 55, 96, 16),   # Huginn heads: a stage would exceed 64 KB -> per-CTA kernel
+    (40, 8, 64, 16),    # 3 heads per consumer warp (streaming kernel, 4-head variant)
+    (20, 4, 128, 1),    # 2 heads per consumer warp, one-token pages
+    (16, 16, 32, 16),   # 32 tokens per stage
+])
+@pytest.mark.parametrize("mode", ["decode", "long"])
+def test_paged_attention_heads(hq: int, hkv: int, d: int, page: int, mode: str) -> None:
+    """Head counts and widths on either side of the streaming kernel's limits."""
+    g = gen(hq * 13 + d + page)
+    if mode == "decode":
+        q_lens, kv_lens = [1, 1, 1], [7, 64, 300]
+    else:
+        q_lens, kv_lens = [1, 3], [2500, 1900]
+    q, kc, vc, table, seq, cu = _paged_case(g, hq, hkv, d, page, q_lens, kv_lens)
+    scale = d ** -0.5
+    ref = O.paged_attention(q, kc, vc, table, seq, cu, scale)
+    kd = kc.to(DEV).view(-1, hkv * d)
+    vd = vc.to(DEV).view(-1, hkv * d)
+    max_seq = int(table.shape[1] * page)
+    for _ in range(2):
+        got = ops.paged_attention(q.to(DEV), kd, vd, table.to(DEV), seq.to(DEV), cu.to(DEV), page,
+                                  max_seq, scale, hkv)
+        close(got, ref)
+    no_device_errors()
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(16, 16, 128), (55, 55, 96)])
+def test_paged_attention_bad_page_flagged(hq: int, hkv: int, d: int) -> None:
+    """A page id outside the pool is never read: its keys are skipped and the slot bit of
+    the device error word is set; rows that do not touch it are unaffected."""
+    g = gen(hq + d)
+    page = 16
+    q, kc, vc, table, seq, cu = _paged_case(g, hq, hkv, d, page, [1, 1], [40, 40])
+    ref = O.paged_attention(q, kc, vc, table, seq, cu, d ** -0.5)
+    num_pages = kc.shape[0]
+    bad = table.clone()
+    bad[1, 1] = num_pages + 5
+    got = ops.paged_attention(q.to(DEV), kc.to(DEV).view(-1, hkv * d), vc.to(DEV).view(-1, hkv * d),
+                              bad.to(DEV), seq.to(DEV), cu.to(DEV), page, int(bad.shape[1] * page),
+                              d ** -0.5, hkv)
+    assert ops.device_error_word(reset=True) & 2
+    close(got[:1], ref[:1])
+    assert torch.isfinite(got.float()).all()
+
+
 def test_paged_attention_full_size_property() -> None:
     """Ouro-1.4B decode shape at full context: with every V row equal to one vector the
     output is that vector whatever the scores (a size-independent check), and sampled
