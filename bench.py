@@ -51,7 +51,7 @@ SEED = 0
 
 # Measured DRAM traffic of the decode attention kernel per context token (K+V of 16
 # heads x 128 = 8192 algorithmic bytes), from the ncu capture in profiles/.
-ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8220.5
+ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8362.3
 
 
 def log(msg: str) -> None:
