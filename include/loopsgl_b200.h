@@ -217,6 +217,14 @@ int lsb_gather_rows(void* out, const void* src, const int64_t* index, int64_t ro
 int lsb_argmax(int32_t* out, const void* logits, int64_t rows, int64_t vocab, int64_t ld,
                void* stream);
 
+/* Greedy token over tensor-parallel LM-head logits gathered rank by rank:
+ * logits [shards][rows][cols] bf16 (rank r holds vocabulary entries
+ * r*cols .. r*cols+cols-1, layers/embedding.py:89-111); entries at or beyond
+ * `vocab` are padding. Same tie rule as lsb_argmax (smallest global index), so
+ * the result equals the argmax of the reference's all-gathered, permuted row. */
+int lsb_argmax_sharded(int32_t* out, const void* logits, int64_t shards, int64_t rows,
+                       int64_t cols, int64_t vocab, void* stream);
+
 /* silu(x[:, :I]) * x[:, I:] -> out[:, :I].  Replaces layers/activation.py:9-12. */
 int lsb_silu_and_mul(void* out, const void* x, int64_t rows, int64_t inter, void* stream);
 
@@ -284,6 +292,57 @@ int lsb_set_metadata(int32_t* cache_seqlens, int32_t* cu_seqlens_k, int32_t* cu_
                      const int32_t* seq_lens, const int32_t* extend_lens, int64_t bs,
                      int64_t max_seq_pages, int32_t page_size, int32_t seq_len_delta,
                      int32_t is_decode, void* stream);
+
+/* ------------------------------------------------- TP communicator --------
+ * Tensor parallelism over the GPUs of one node, one process per GPU, without
+ * NCCL on the data path. Every rank allocates one symmetric buffer of
+ * lsb_comm_buffer_bytes(max_elems) with lsb_comm_alloc (zeroed), exports it with
+ * lsb_ipc_handle, maps every peer's with lsb_ipc_open (the handles travel over
+ * the host process group), and builds a communicator from the world's mapped
+ * addresses (buffers[rank] = its own). max_elems bounds the bf16 elements of one
+ * all-reduce (rows x cols) and the bytes/2 of one all-gather contribution.
+ * Data moves with stores into peer memory over NVLink: each output region is
+ * owned by one rank, which sums every rank's bf16 partial in rank order (fp32,
+ * one rounding: all ranks receive identical bits) and writes the sum back to
+ * every rank. Flags carry per-call epochs, so no reset is needed between calls;
+ * every wait is bounded (LSB_DEVERR_TIMEOUT in the device error word). All ranks
+ * must make the same calls, with the same shapes, in the same order. Calls are
+ * stream-ordered and capturable in CUDA graphs. Replaces the PyNCCL communicator
+ * (python/loopsgl/distributed/impl.py:44-60, kernel/csrc/src/pynccl.cu:72-161,
+ * python/loopsgl/kernel/pynccl.py:59-92). */
+#define LSB_IPC_HANDLE_BYTES 64
+typedef struct lsb_comm lsb_comm;
+int64_t lsb_comm_buffer_bytes(int64_t max_elems);
+int lsb_comm_alloc(int64_t bytes, void** ptr);
+int lsb_comm_free(void* ptr);
+int lsb_ipc_handle(void* ptr, void* handle);
+int lsb_ipc_open(const void* handle, void** ptr);
+int lsb_ipc_close(void* ptr);
+int lsb_comm_create(int32_t rank, int32_t world, void* const* buffers, int64_t max_elems,
+                    lsb_comm** comm);
+int lsb_comm_destroy(lsb_comm* comm);
+
+/* In-place sum of x[rows, cols] (row stride ld) over the ranks: the reference's
+ * DistributedCommunicator.all_reduce (distributed/impl.py:63-67), used for the
+ * vocab-parallel embedding and by callers that keep their own GEMM. */
+int lsb_allreduce(lsb_comm* comm, void* x, int64_t rows, int64_t cols, int64_t ld, void* stream);
+
+/* out[world][bytes] = every rank's `in` (bytes a multiple of 16), the reference's
+ * all_gather along dim 0 (distributed/impl.py:68-70; LM-head logits,
+ * layers/embedding.py:99-111). */
+int lsb_allgather(lsb_comm* comm, void* out, const void* in, int64_t bytes, void* stream);
+
+/* Row-parallel linear fused with its all-reduce: y[M, N] = sum over ranks of
+ * x_r[M, K_r] . w_r[N, K_r]^T (+ bias on every rank, as the reference adds it
+ * before reducing), in ONE kernel: the tcgen05 GEMM's epilogue pushes each
+ * rank's bf16 tile to the tile's owner over NVLink, the owner reduces and
+ * broadcasts, and the kernel ends when y is complete on this rank. epilogue
+ * LSB_EPI_NONE or LSB_EPI_BIAS; M x N <= the communicator's max_elems. With one
+ * rank it is lsb_gemm. Replaces LinearOProj.forward / LinearRowParallel.forward
+ * (layers/linear.py:103-107, 124-128: F.linear then all_reduce). */
+int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x, int64_t ldx,
+                       const void* w, int64_t ldw, const void* bias, int64_t M, int64_t N,
+                       int64_t K, int32_t epilogue, void* stream);
 
 #ifdef __cplusplus
 }

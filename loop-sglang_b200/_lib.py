@@ -28,6 +28,8 @@ LSB_DEVERR_SLOT = 2
 LSB_DEVERR_SEQLEN = 4
 LSB_DEVERR_TIMEOUT = 8
 
+LSB_IPC_HANDLE_BYTES = 64
+
 P = c_void_p
 I64 = c_int64
 I32 = c_int32
@@ -58,6 +60,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_embedding": (ctypes.c_int, [P, P, P, I64, I64, I64, I64, F, P]),
     "lsb_gather_rows": (ctypes.c_int, [P, P, P, I64, I64, P]),
     "lsb_argmax": (ctypes.c_int, [P, P, I64, I64, I64, P]),
+    "lsb_argmax_sharded": (ctypes.c_int, [P, P, I64, I64, I64, I64, P]),
     "lsb_silu_and_mul": (ctypes.c_int, [P, P, I64, I64, P]),
     "lsb_last_exited_resolve": (ctypes.c_int, [P, I64, I64, P, I64, P, I64, P, I64, I64, P, P, P,
                                                P, I32, I64, I64, I32, P]),
@@ -66,6 +69,17 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                         P]),
     "lsb_last_exited_reserve": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
     "lsb_last_exited_release": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
+    "lsb_comm_buffer_bytes": (c_int64, [I64]),
+    "lsb_comm_alloc": (ctypes.c_int, [I64, P]),
+    "lsb_comm_free": (ctypes.c_int, [P]),
+    "lsb_ipc_handle": (ctypes.c_int, [P, P]),
+    "lsb_ipc_open": (ctypes.c_int, [P, P]),
+    "lsb_ipc_close": (ctypes.c_int, [P]),
+    "lsb_comm_create": (ctypes.c_int, [I32, I32, P, I64, P]),
+    "lsb_comm_destroy": (ctypes.c_int, [P]),
+    "lsb_allreduce": (ctypes.c_int, [P, P, I64, I64, I64, P]),
+    "lsb_allgather": (ctypes.c_int, [P, P, P, I64, P]),
+    "lsb_gemm_allreduce": (ctypes.c_int, [P, P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -103,7 +117,8 @@ def check(rc: int, what: str) -> None:
 
 
 _launches = 0
-_NOT_LAUNCHES = {"lsb_device_error_word"}
+_NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "lsb_ipc_handle",
+                 "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy"}
 
 
 def launch_count() -> int:

@@ -1,0 +1,210 @@
+// Tensor-parallel exchange over peer memory (NVLink), shared by the fused
+// row-parallel GEMM + all-reduce, the standalone all-reduce and the all-gather.
+//
+// Every rank of a node holds one symmetric buffer (same layout on every rank,
+// allocated with cudaMalloc and mapped into its peers with CUDA IPC). A call's
+// output is cut into regions (one per CTA, the same on every rank). The owner of
+// a region receives every rank's bf16 partial of it in recv[src], sums them in
+// rank order once every rank's flag shows this call's epoch, rounds once, writes
+// the sum to its own output and into every peer's result area, and raises the
+// peers' done flags; the other ranks copy the sum out of their result area. Flags
+// carry a per-operation epoch that every rank advances once per call (the last
+// CTA to finish stores it), so no flag is ever reset and a stale flag can never
+// match. Every wait is bounded and reports LSB_DEVERR_TIMEOUT instead of hanging.
+#pragma once
+
+#include "common.cuh"
+
+namespace lsb {
+
+constexpr int kCommMaxWorld = 8;
+constexpr int kCommMaxRegions = 16384;
+enum CommOp : int { kOpGemmAllReduce = 0, kOpAllReduce = 1, kOpAllGather = 2, kCommOps = 3 };
+
+// Byte offsets inside a rank's symmetric buffer.
+constexpr int64_t kCommCtlOff = 0;  // u32 [kCommOps][2]: epoch, CTAs finished
+constexpr int64_t kCommFlagsOff = 4096;
+constexpr int64_t kCommFlagBytes =
+    static_cast<int64_t>(kCommMaxRegions) * kCommMaxWorld * sizeof(uint32_t);
+constexpr int64_t kCommDoneBytes = static_cast<int64_t>(kCommMaxRegions) * sizeof(uint32_t);
+// per op: flags [regions][world] then done [regions]
+constexpr int64_t kCommOpBytes = kCommFlagBytes + kCommDoneBytes;
+constexpr int64_t kCommDataOff = kCommFlagsOff + kCommOps * kCommOpBytes;
+
+struct CommDev {
+  int rank, world;
+  int64_t max_elems;  // bf16 elements of one recv slot / the result area / one gather slot
+  uint8_t* base[kCommMaxWorld];
+
+  __device__ __forceinline__ uint32_t* ctl(int r) const {
+    return reinterpret_cast<uint32_t*>(base[r] + kCommCtlOff);
+  }
+  __device__ __forceinline__ uint32_t* flags(int r, int op) const {
+    return reinterpret_cast<uint32_t*>(base[r] + kCommFlagsOff + op * kCommOpBytes);
+  }
+  __device__ __forceinline__ uint32_t* done(int r, int op) const {
+    return reinterpret_cast<uint32_t*>(base[r] + kCommFlagsOff + op * kCommOpBytes +
+                                       kCommFlagBytes);
+  }
+  // recv slot `src` of rank r (partials sent to r by src)
+  __device__ __forceinline__ bf16* recv(int r, int src) const {
+    return reinterpret_cast<bf16*>(base[r] + kCommDataOff) + static_cast<int64_t>(src) * max_elems;
+  }
+  __device__ __forceinline__ bf16* result(int r) const {
+    return reinterpret_cast<bf16*>(base[r] + kCommDataOff) +
+           static_cast<int64_t>(kCommMaxWorld) * max_elems;
+  }
+  // all-gather slot `src` of rank r for calls of epoch parity `par`: a rank can run
+  // at most one all-gather ahead of a peer that is still copying out of its slots
+  __device__ __forceinline__ uint8_t* gather(int r, int src, int par) const {
+    return base[r] + kCommDataOff +
+           (static_cast<int64_t>(kCommMaxWorld + 1) + par * kCommMaxWorld + src) * max_elems * 2;
+  }
+};
+
+inline int64_t comm_buffer_bytes(int64_t max_elems) {
+  return kCommDataOff + (3 * static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 2;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr long long kCommTimeoutCycles = 4000000000LL;  // ~2 s
+
+// Bounded wait until *p == v (the flag of this call's epoch).
+__device__ __forceinline__ bool comm_wait(const uint32_t* p, uint32_t v, int* err) {
+  if (ld_acquire_sys(p) == v) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_sys(p) != v) {
+    if (clock64() - t0 > kCommTimeoutCycles) {
+      if (err) atomicOr(err, LSB_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
+// This call's epoch of `op` (read by one thread of every CTA before it finishes).
+__device__ __forceinline__ uint32_t comm_epoch(const CommDev& c, int op) {
+  return *reinterpret_cast<volatile uint32_t*>(c.ctl(c.rank) + 2 * op) + 1u;
+}
+
+// Called once per CTA (one thread) at its very end: the last CTA of the grid
+// stores the epoch, which the next call of `op` then advances.
+__device__ __forceinline__ void comm_finish(const CommDev& c, int op, uint32_t epoch,
+                                            unsigned ctas) {
+  uint32_t* ctl = c.ctl(c.rank) + 2 * op;
+  __threadfence();
+  const unsigned prev = atomicAdd(ctl + 1, 1u);
+  if (prev == ctas - 1) {
+    ctl[0] = epoch;
+    ctl[1] = 0;
+    __threadfence();
+  }
+}
+
+// Four consecutive bf16 of row m, columns col..col+3 (< ncols), as one 8-byte
+// store when aligned and whole, else element by element.
+__device__ __forceinline__ void put4(bf16* dst_row, int col, int ncols, const bf16 v[4]) {
+  bf16* d = dst_row + col;
+  if (col + 3 < ncols && (reinterpret_cast<uintptr_t>(d) & 7) == 0) {
+    uint2 u;
+    memcpy(&u, v, 8);
+    *reinterpret_cast<uint2*>(d) = u;
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (col + e < ncols) d[e] = v[e];
+}
+
+__device__ __forceinline__ void get4(const bf16* src_row, int col, int ncols, float f[4]) {
+  const bf16* s = src_row + col;
+  if (col + 3 < ncols && (reinterpret_cast<uintptr_t>(s) & 7) == 0) {
+    const uint2 u = __ldcg(reinterpret_cast<const uint2*>(s));
+    bf16 h[4];
+    memcpy(h, &u, 8);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f[e] = __bfloat162float(h[e]);
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f[e] = col + e < ncols ? __bfloat162float(s[e]) : 0.f;
+}
+
+// Second half of the exchange for one region (rows [r0, r1) x columns [c0, c0 + w)
+// of an output with `ncols` columns and row stride `ld`), after this CTA has pushed
+// its partial of the region to the owner's recv slot. Run by `nthreads` threads
+// (index t) that synchronise with `sync()`; thread 0 handles the flags.
+// recv/result rows use a row stride of `rs` elements.
+template <typename Sync>
+__device__ __forceinline__ void comm_complete(const CommDev& c, int op, int region, int owner,
+                                              uint32_t epoch, bf16* out, int64_t ld, int r0,
+                                              int r1, int c0, int w, int ncols, int64_t rs,
+                                              int t, int nthreads, Sync sync, int* err) {
+  const int me = c.rank, W = c.world;
+  sync();  // every push of this CTA is issued
+  if (t == 0) {
+    __threadfence_system();
+    st_release_sys(c.flags(owner, op) + region * kCommMaxWorld + me, epoch);
+  }
+  const int quads = (w + 3) >> 2;
+  const int count = (r1 - r0) * quads;
+  if (me == owner) {
+    if (t == 0)
+      for (int s = 0; s < W; ++s)
+        comm_wait(c.flags(me, op) + region * kCommMaxWorld + s, epoch, err);
+    sync();
+    for (int idx = t; idx < count; idx += nthreads) {
+      const int m = r0 + idx / quads;
+      const int col = c0 + 4 * (idx % quads);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < W; ++s) {  // rank order: every rank gets the same bits
+        float f[4];
+        get4(c.recv(me, s) + m * rs, col, ncols, f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += f[e];
+      }
+      bf16 v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(acc[e]);
+      put4(out + m * ld, col, ncols, v);
+      for (int r = 0; r < W; ++r)
+        if (r != me) put4(c.result(r) + m * rs, col, ncols, v);
+    }
+    sync();
+    if (t == 0) {
+      __threadfence_system();
+      for (int r = 0; r < W; ++r)
+        if (r != me) st_release_sys(c.done(r, op) + region, epoch);
+    }
+  } else {
+    if (t == 0) comm_wait(c.done(me, op) + region, epoch, err);
+    sync();
+    for (int idx = t; idx < count; idx += nthreads) {
+      const int m = r0 + idx / quads;
+      const int col = c0 + 4 * (idx % quads);
+      float f[4];
+      get4(c.result(me) + m * rs, col, ncols, f);
+      bf16 v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(f[e]);
+      put4(out + m * ld, col, ncols, v);
+    }
+  }
+}
+
+}  // namespace lsb
+
+// The communicator object behind the C ABI's opaque lsb_comm handle.
+struct lsb_comm {
+  lsb::CommDev dev;
+  int device;
+};

@@ -29,6 +29,7 @@
 #include <mutex>
 #include <tuple>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "mbarrier.cuh"
 
@@ -53,6 +54,7 @@ struct GemmParams {
   int bn, stages, splits, epilogue;
   uint32_t idesc;
   int* error_flag;
+  CommDev comm;  // row-parallel all-reduce (AR variants only)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -157,7 +159,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
-template <int EPI, bool CLUSTER>
+template <int EPI, bool CLUSTER, bool AR>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
@@ -389,12 +391,46 @@ __global__ void __launch_bounds__(kThreads, 2)
             o2 = round_bf16(o2) + b2; o3 = round_bf16(o3) + b3;
           }
         }
-        store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
+        if (AR) {
+          // this rank's partial (rounded to bf16, as the reference's local GEMM output)
+          // goes to the tile owner's recv slot, rows of N elements
+          const bf16 v4[4] = {__float2bfloat16_rn(o0), __float2bfloat16_rn(o1),
+                              __float2bfloat16_rn(o2), __float2bfloat16_rn(o3)};
+          put4(p.comm.recv(tile_n % p.comm.world, p.comm.rank) +
+                   static_cast<int64_t>(m0 + m) * p.N, col, ncols, v4);
+        } else {
+          store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
+        }
       }
       }
     }
   }
   if (CLUSTER) cluster_sync_all();  // peers may still be reading this CTA's tile
+  if (AR && warp >= 2) {
+    // Row-parallel all-reduce of this CTA's region (rows m0+tb..m0+te of the tile's
+    // 128 columns) with the same CTA of every rank, over NVLink.
+    const int t = threadIdx.x - 64;
+    const int tokens = p.M - m0 < p.bn ? p.M - m0 : p.bn;
+    int tb = 0, te = tokens;
+    if (CLUSTER) {
+      const int per = (tokens + S - 1) / S;
+      tb = split * per;
+      te = tb + per < tokens ? tb + per : tokens;
+      if (te < tb) te = tb;
+    }
+    uint32_t epoch = 0;
+    if (t == 0) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      epoch = comm_epoch(p.comm, kOpGemmAllReduce);
+    }
+    const int region = blockIdx.x + blockIdx.y * gridDim.x;
+    const int w = p.N - n0 < kBM ? p.N - n0 : kBM;
+    comm_complete(p.comm, kOpGemmAllReduce, region, tile_n % p.comm.world, epoch, p.y, p.ldy,
+                  m0 + tb, m0 + te, n0, w, p.N, p.N, t, 128, [] { epi_barrier(); },
+                  p.error_flag);
+    epi_barrier();
+    if (t == 0) comm_finish(p.comm, kOpGemmAllReduce, epoch, gridDim.x * gridDim.y);
+  }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
   if (warp == 1) {
@@ -460,12 +496,18 @@ int num_sms() {
 
 using Kernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
 
-Kernel kernel_for(bool cluster, int epilogue) {
+Kernel kernel_for(bool cluster, int epilogue, bool ar = false) {
   static const Kernel kernels[2][4] = {
-      {gemm_tcgen05_kernel<LSB_EPI_NONE, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false>,
-       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false>},
-      {gemm_tcgen05_kernel<LSB_EPI_NONE, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true>,
-       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true>, gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true>}};
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, false, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, false>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false, false>,
+       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false, false>},
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, true, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, false>,
+       gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true, false>,
+       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true, false>}};
+  static const Kernel ar_kernels[2][2] = {
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, false, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, true>},
+      {gemm_tcgen05_kernel<LSB_EPI_NONE, true, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, true>}};
+  if (ar) return ar_kernels[cluster ? 1 : 0][epilogue == LSB_EPI_BIAS ? 1 : 0];
   return kernels[cluster ? 1 : 0][epilogue];
 }
 
@@ -473,15 +515,15 @@ constexpr int kMaxSmem = 227 * 1024;
 
 // Raises a kernel's dynamic shared-memory limit once per device (needed before both
 // the launch and the occupancy queries below).
-int configure(bool cluster, int epilogue) {
+int configure(bool cluster, int epilogue, bool ar = false) {
   static std::mutex mu;
-  static uint64_t done[64] = {0};  // bit (cluster*4 + epilogue) per device
+  static uint64_t done[64] = {0};  // bit (ar*8 + cluster*4 + epilogue) per device
   int dev = 0;
   LSB_CUDA(cudaGetDevice(&dev));
-  const uint64_t bit = uint64_t(1) << ((cluster ? 4 : 0) + epilogue);
+  const uint64_t bit = uint64_t(1) << ((ar ? 8 : 0) + (cluster ? 4 : 0) + epilogue);
   std::lock_guard<std::mutex> lock(mu);
   if (dev < 64 && (done[dev] & bit)) return LSB_OK;
-  LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue),
+  LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue, ar),
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   if (dev < 64) done[dev] |= bit;
   return LSB_OK;
@@ -551,7 +593,7 @@ size_t smem_for(int stages, int stage_bytes) {
 // ingest of weight and activation tiles, not the pipeline depth, then limits the
 // main loop. A split is only used when all clusters of the grid run at once; a
 // cluster left for a second wave would double the kernel's time.
-Plan plan_for(int64_t M, int64_t N, int64_t K) {
+Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   Plan pl;
   int64_t bn = ((M + 15) / 16) * 16;
   if (bn > 256) bn = 256;
@@ -581,7 +623,7 @@ Plan plan_for(int64_t M, int64_t N, int64_t K) {
   pl.smem = smem_a;
 
   const size_t smem_b = smem_for(3, stage_bytes);
-  if (2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
+  if (!single_wave && 2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
     const int split_b = tiles < 2 * sms ? best_split(2 * sms / tiles, smem_b) : 1;
     if (static_cast<int64_t>(tiles) * split_b > sms) {
       pl.stages = 3;
@@ -612,12 +654,9 @@ extern "C" int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return 0;  // split-K partials are reduced in distributed shared memory
 }
 
-extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
-                        int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
-                        int32_t epilogue, void* workspace, int64_t workspace_bytes,
-                        void* stream) {
-  (void)workspace;
-  (void)workspace_bytes;
+static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
+                     int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
+                     int32_t epilogue, const lsb_comm* comm, void* stream) {
   LSB_REQUIRE(y && x && w, "gemm: null pointer");
   LSB_REQUIRE(N > 0 && K > 0, "gemm: empty N or K (N=%lld K=%lld)", (long long)N, (long long)K);
   LSB_REQUIRE(epilogue != LSB_EPI_SWIGLU || N % kBM == 0,
@@ -634,7 +673,9 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   const int64_t out_cols = epilogue == LSB_EPI_SWIGLU ? N / 2 : N;
   LSB_REQUIRE(ldy >= out_cols, "gemm: ldy too small");
   if (M <= 0) return LSB_OK;
-  Plan pl = plan_for(M, N, K);
+  // The all-reduce variant waits on the same CTA of every rank: its whole grid must be
+  // resident at once, so it keeps one CTA per SM and at most one wave.
+  Plan pl = plan_for(M, N, K, comm != nullptr);
   CUtensorMap tw, tx;
   if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
   if (int rc = make_tmap(&tx, x, M, K, ldx, pl.bn)) return rc;
@@ -651,9 +692,17 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   p.epilogue = epilogue;
   p.idesc = make_idesc(pl.bn);
   p.error_flag = lsb_device_error_flag();
+  const bool ar = comm != nullptr;
+  if (ar) {
+    p.comm = comm->dev;
+    LSB_REQUIRE(static_cast<int64_t>(pl.tiles_n) * pl.splits * pl.tiles_m <= kCommMaxRegions,
+                "gemm_allreduce: too many tiles");
+  } else {
+    memset(&p.comm, 0, sizeof(p.comm));
+  }
   const bool cluster = pl.splits > 1;
-  if (int rc = configure(cluster, epilogue)) return rc;
-  Kernel kernel = kernel_for(cluster, epilogue);
+  if (int rc = configure(cluster, epilogue, ar)) return rc;
+  Kernel kernel = kernel_for(cluster, epilogue, ar);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles_n * pl.splits, pl.tiles_m, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -675,4 +724,42 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   cfg.numAttrs = nattr;
   LSB_CUDA(cudaLaunchKernelEx(&cfg, kernel, tw, tx, p));
   return check_launch("lsb_gemm");
+}
+
+extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
+                        int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
+                        int32_t epilogue, void* workspace, int64_t workspace_bytes,
+                        void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  return gemm_impl(y, ldy, x, ldx, w, ldw, bias, M, N, K, epilogue, nullptr, stream);
+}
+
+extern "C" int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x,
+                                  int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                                  int64_t M, int64_t N, int64_t K, int32_t epilogue,
+                                  void* stream) {
+  LSB_REQUIRE(comm && y && x, "gemm_allreduce: null pointer");
+  LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_BIAS,
+              "gemm_allreduce: epilogue must be LSB_EPI_NONE or LSB_EPI_BIAS");
+  LSB_REQUIRE(M >= 0 && N > 0, "gemm_allreduce: bad shape");
+  if (comm->dev.world == 1)
+    return gemm_impl(y, ldy, x, ldx, w, ldw, bias, M, N, K, epilogue, nullptr, stream);
+  const int sms = num_sms();
+  const int64_t tiles_n = (N + kBM - 1) / kBM;
+  LSB_REQUIRE(tiles_n <= sms, "gemm_allreduce: N=%lld needs more tiles than SMs", (long long)N);
+  // One wave per launch: tokens beyond what the SMs hold in one wave go to further
+  // launches (each a complete all-reduce of its rows).
+  int64_t rows_per = (sms / tiles_n) * 256;
+  if (rows_per * N > comm->dev.max_elems) rows_per = (comm->dev.max_elems / N) / 16 * 16;
+  LSB_REQUIRE(rows_per > 0, "gemm_allreduce: N=%lld exceeds the communicator's %lld elements",
+              (long long)N, (long long)comm->dev.max_elems);
+  for (int64_t m0 = 0; m0 < M; m0 += rows_per) {
+    const int64_t mc = M - m0 < rows_per ? M - m0 : rows_per;
+    if (int rc = gemm_impl(static_cast<bf16*>(y) + m0 * ldy, ldy,
+                           static_cast<const bf16*>(x) + m0 * ldx, ldx, w, ldw, bias, mc, N, K,
+                           epilogue, comm, stream))
+      return rc;
+  }
+  return LSB_OK;
 }

@@ -37,26 +37,35 @@ __global__ void gather_rows_kernel(bf16* __restrict__ out, const bf16* __restric
   for (int64_t j = threadIdx.x; j < dim / 8; j += blockDim.x) d[j] = s[j];
 }
 
-// One CTA per row. Ties resolve to the smallest index, like torch.argmax.
+// One CTA per row. Ties resolve to the smallest index, like torch.argmax. The row
+// may be split into `shards` consecutive vocabulary ranges of `cols` entries
+// stored `shard_stride` elements apart (tensor-parallel LM-head logits gathered
+// rank by rank); global entries at or beyond `vocab` (padding) never win.
 __global__ void argmax_kernel(int32_t* __restrict__ out, const bf16* __restrict__ logits,
-                              int64_t vocab, int64_t ld) {
+                              int64_t vocab, int64_t ld, int64_t cols, int64_t shards,
+                              int64_t shard_stride) {
   const int64_t r = blockIdx.x;
-  const bf16* row = logits + r * ld;
   float best = -INFINITY;
   int64_t best_i = vocab;
-  const bool vec = (ld % 8 == 0) && (vocab % 8 == 0);
-  if (vec) {
-    for (int64_t j = threadIdx.x; j < vocab / 8; j += blockDim.x) {
-      float f[8];
-      unpack8(*reinterpret_cast<const bf16x8*>(row + 8 * j), f);
+  for (int64_t sh = 0; sh < shards; ++sh) {
+    const bf16* row = logits + sh * shard_stride + r * ld;
+    const int64_t g0 = sh * cols;
+    const int64_t n = vocab - g0 < cols ? vocab - g0 : cols;
+    if (n <= 0) break;
+    const bool vec = (ld % 8 == 0) && (n % 8 == 0) && (shard_stride % 8 == 0);
+    if (vec) {
+      for (int64_t j = threadIdx.x; j < n / 8; j += blockDim.x) {
+        float f[8];
+        unpack8(*reinterpret_cast<const bf16x8*>(row + 8 * j), f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (f[e] > best) { best = f[e]; best_i = 8 * j + e; }
-    }
-  } else {
-    for (int64_t j = threadIdx.x; j < vocab; j += blockDim.x) {
-      const float f = __bfloat162float(row[j]);
-      if (f > best) { best = f; best_i = j; }
+        for (int e = 0; e < 8; ++e)
+          if (f[e] > best) { best = f[e]; best_i = g0 + 8 * j + e; }
+      }
+    } else {
+      for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+        const float f = __bfloat162float(row[j]);
+        if (f > best) { best = f; best_i = g0 + j; }
+      }
     }
   }
   // NaN never wins; equal values keep the smaller index.
@@ -173,8 +182,19 @@ extern "C" int lsb_argmax(int32_t* out, const void* logits, int64_t rows, int64_
   LSB_REQUIRE(aligned(logits, 16), "argmax: logits must be 16-byte aligned");
   if (rows <= 0) return LSB_OK;
   argmax_kernel<<<rows, 512, 0, as_stream(stream)>>>(out, static_cast<const bf16*>(logits),
-                                                     vocab, ld);
+                                                     vocab, ld, vocab, 1, 0);
   return check_launch("lsb_argmax");
+}
+
+extern "C" int lsb_argmax_sharded(int32_t* out, const void* logits, int64_t shards, int64_t rows,
+                                  int64_t cols, int64_t vocab, void* stream) {
+  LSB_REQUIRE(out && logits && shards > 0 && cols > 0 && vocab > 0 && vocab <= shards * cols,
+              "argmax_sharded: bad arguments");
+  LSB_REQUIRE(aligned(logits, 16), "argmax_sharded: logits must be 16-byte aligned");
+  if (rows <= 0) return LSB_OK;
+  argmax_kernel<<<rows, 512, 0, as_stream(stream)>>>(out, static_cast<const bf16*>(logits),
+                                                     vocab, cols, cols, shards, rows * cols);
+  return check_launch("lsb_argmax_sharded");
 }
 
 extern "C" int lsb_silu_and_mul(void* out, const void* x, int64_t rows, int64_t inter,
