@@ -78,8 +78,7 @@ class DecodeEngine:
         h, inj = m.forward_prelude(b, self.kv)
         for step in range(m.cfg.loop_steps):
             h = m.core_step(h, step, inj, b, self.kv)
-        logits = m.lm_head(m.forward_coda(h, b, self.kv), b)
-        ops.argmax(logits, out=self.ids)
+        m.greedy(m.forward_coda(h, b, self.kv), b, out=self.ids)
 
     def capture(self) -> None:
         """Warm up (sizes every workspace), then capture one decode step."""

@@ -142,35 +142,85 @@ class LoopedDecoder:
     """A looped decoder under one looped-KV policy, weights resident in HBM (bf16)."""
 
     def __init__(self, cfg: LoopedConfig, weights: dict[str, torch.Tensor], policy: str,
-                 device: torch.device | str = "cuda") -> None:
+                 device: torch.device | str = "cuda", comm=None) -> None:
+        """``weights`` is the full (unsharded) state dict. With a ``comm``
+        (``comm.B200Communicator``) this rank keeps its tensor-parallel shard, split as
+        the reference's loader does (models/weight.py:38-56): q/k/v and gate/up rows,
+        o_proj and down_proj columns, vocabulary rows of the embedding and LM head."""
         if policy not in ("depth_indexed", "shared", "last_exited"):
             raise ValueError(f"unknown looped-KV policy {policy!r}")
         self.cfg, self.policy = cfg, policy
         self.device = torch.device(device)
+        self.comm = comm
+        self.rank, self.world = (comm.rank, comm.world) if comm is not None else (0, 1)
+        t, r = self.world, self.rank
+        if t > 1 and (cfg.arch != "ouro" or cfg.heads % t or cfg.intermediate % t):
+            raise ValueError(f"{cfg.arch} with {cfg.heads} heads does not shard over {t} ranks "
+                             "(Huginn runs as data-parallel replicas)")
+        self.hq = cfg.heads // t
+        self.hkv = max(cfg.kv_heads // t, 1)
+        self.inter = cfg.intermediate // t
+        d = cfg.head_dim
 
-        def bf(name: str) -> torch.Tensor:
-            return weights[name].to(device=self.device, dtype=BF16).contiguous()
+        def bf(x: torch.Tensor) -> torch.Tensor:
+            return x.to(device=self.device, dtype=BF16).contiguous()
 
-        def opt(name: str) -> torch.Tensor | None:
-            return bf(name) if name in weights else None
+        def rows(x: torch.Tensor) -> torch.Tensor:  # _SPLIT_DIM_0
+            return x.chunk(t, dim=0)[r]
+
+        def kv_rows(x: torch.Tensor) -> torch.Tensor:  # k/v: replicated below one head per rank
+            if cfg.kv_heads < t:
+                h = r * cfg.kv_heads // t
+                return x[h * d:(h + 1) * d]
+            return rows(x)
+
+        def qkv_shard(x: torch.Tensor) -> torch.Tensor:
+            q, k, v = x.split([cfg.heads * d, cfg.kv_heads * d, cfg.kv_heads * d], dim=0)
+            return torch.cat([rows(q), kv_rows(k), kv_rows(v)], dim=0)
+
+        def gate_up_shard(x: torch.Tensor) -> torch.Tensor:
+            g, u = x.chunk(2, dim=0)
+            return torch.cat([rows(g), rows(u)], dim=0)
+
+        def cols(x: torch.Tensor) -> torch.Tensor:  # _SPLIT_DIM_1
+            return x.chunk(t, dim=1)[r]
+
+        def opt(name: str, fn=lambda x: x) -> torch.Tensor | None:
+            return bf(fn(weights[name])) if name in weights else None
 
         self.layers: dict[str, _Layer] = {}
         for p in cfg.layer_names():
-            gu = bf(f"{p}.mlp.gate_up_proj.weight")
+            gu = bf(gate_up_shard(weights[f"{p}.mlp.gate_up_proj.weight"]))
             self.layers[p] = _Layer(
-                qkv=bf(f"{p}.self_attn.qkv_proj.weight"),
-                qkv_bias=opt(f"{p}.self_attn.qkv_proj.bias"),
-                o=bf(f"{p}.self_attn.o_proj.weight"),
+                qkv=bf(qkv_shard(weights[f"{p}.self_attn.qkv_proj.weight"])),
+                qkv_bias=opt(f"{p}.self_attn.qkv_proj.bias", qkv_shard),
+                o=bf(cols(weights[f"{p}.self_attn.o_proj.weight"])),
                 gate_up=ops.swiglu_interleave(gu),
-                down=bf(f"{p}.mlp.down_proj.weight"),
-                norms=[bf(f"{p}.{n}.weight") for n in (
+                down=bf(cols(weights[f"{p}.mlp.down_proj.weight"])),
+                norms=[bf(weights[f"{p}.{n}.weight"]) for n in (
                     "input_layernorm", "input_layernorm_2", "post_attention_layernorm",
                     "post_attention_layernorm_2")],
             )
             del gu
-        self.embed = bf("model.embed_tokens.weight")
-        self.lm_head_w = self.embed if cfg.tie_word_embeddings else bf("lm_head.weight")
-        self.norm = bf("model.norm.weight")
+        # vocabulary partition (ParallelLMHead / VocabParallelEmbedding): ceil(V/t) rows per
+        # rank; the LM head is zero-padded to that size so every rank's logits gather alike
+        self.vocab_local = -(-cfg.vocab // t)
+        self.vocab_start = r * self.vocab_local
+        vlen = max(0, min(self.vocab_local, cfg.vocab - self.vocab_start))
+        self.vocab_len = vlen
+
+        def vocab_rows(x: torch.Tensor, pad: bool) -> torch.Tensor:
+            part = x[self.vocab_start:self.vocab_start + vlen]
+            if pad and vlen < self.vocab_local:
+                part = torch.cat([part, part.new_zeros(self.vocab_local - vlen, x.shape[1])])
+            return part
+
+        embed_full = weights["model.embed_tokens.weight"]
+        self.embed = bf(vocab_rows(embed_full, False)) if t > 1 else bf(embed_full)
+        head_full = embed_full if cfg.tie_word_embeddings else weights["lm_head.weight"]
+        self.lm_head_w = bf(vocab_rows(head_full, True)) if t > 1 else (
+            self.embed if cfg.tie_word_embeddings else bf(head_full))
+        self.norm = bf(weights["model.norm.weight"])
         self.gate_w = opt("model.early_exit_gate.weight")
         self.gate_b = opt("model.early_exit_gate.bias")
         self.adapter = opt("model.adapter.weight")
@@ -180,6 +230,13 @@ class LoopedDecoder:
         self.scale = cfg.head_dim ** -0.5
         self.core_names = [f"model.layers.{i}" for i in range(cfg.num_core_layers)]
 
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """LinearOProj / LinearRowParallel (layers/linear.py:103-107, 124-128): the local
+        GEMM and the all-reduce in one kernel over NVLink when sharded."""
+        if self.world > 1:
+            return self.comm.gemm_allreduce(x, w)
+        return ops.gemm(x, w)
+
     # ------------------------------------------------------------------ KV --
     @property
     def num_kv_layers(self) -> int:
@@ -188,11 +245,11 @@ class LoopedDecoder:
     def make_kv_cache(self, num_pages: int, page_size: int, zero: bool = True):
         c = self.cfg
         if self.policy == "last_exited":
-            return LastExitedKVCache(c.kv_heads, self.num_kv_layers, c.head_dim, num_pages,
+            return LastExitedKVCache(self.hkv, self.num_kv_layers, c.head_dim, num_pages,
                                      c.num_prelude_layers,
                                      c.num_prelude_layers + c.num_core_layers, c.loop_steps,
                                      self.device, zero=zero)
-        return MHAKVCache(c.kv_heads, self.num_kv_layers, c.head_dim, num_pages, page_size,
+        return MHAKVCache(self.hkv, self.num_kv_layers, c.head_dim, num_pages, page_size,
                           self.device, zero=zero)
 
     def resolve_core(self, batch: DeviceBatch, kv: LastExitedKVCache, depths) -> None:
@@ -239,16 +296,16 @@ class LoopedDecoder:
             else:
                 out_loc, table = batch.fixed_out_loc[group], batch.fixed_page_table[group]
         kc, vc = kv.slots(cache_layer)
-        ops.rope_store_kv(qkv, batch.positions, self.cos_sin, c.heads, c.kv_heads, c.head_dim,
+        ops.rope_store_kv(qkv, batch.positions, self.cos_sin, self.hq, self.hkv, c.head_dim,
                           kc, vc, out_loc)
-        q = qkv[:, : c.heads * c.head_dim].view(-1, c.heads, c.head_dim)
+        q = qkv[:, : self.hq * c.head_dim].view(-1, self.hq, c.head_dim)
         o = ops.paged_attention(q, kc, vc, table, batch.cache_seqlens, batch.cu_seqlens_q, page,
-                                batch.max_seqlen, self.scale, c.kv_heads)
-        return ops.gemm(o.view(-1, c.heads * c.head_dim), lw.o)
+                                batch.max_seqlen, self.scale, self.hkv)
+        return self._row_parallel(o.view(-1, self.hq * c.head_dim), lw.o)
 
     def _mlp(self, lw: _Layer, x: torch.Tensor) -> torch.Tensor:
         """GatedMLP (models/utils.py:45-50) with the SwiGLU epilogue."""
-        return ops.gemm(ops.gemm(x, lw.gate_up, epilogue=ops.LSB_EPI_SWIGLU), lw.down)
+        return self._row_parallel(ops.gemm(x, lw.gate_up, epilogue=ops.LSB_EPI_SWIGLU), lw.down)
 
     def _ouro_core(self, hidden: torch.Tensor, loop_step, batch: DeviceBatch, kv):
         """All core layers of one Ouro step up to the last MLP output (ouro.py:119-135).
@@ -291,7 +348,13 @@ class LoopedDecoder:
         layers, with a zero recurrent state (huginn.py:146-160)."""
         c = self.cfg
         if c.arch == "ouro":
-            return ops.embedding(batch.input_ids, self.embed), None
+            if self.world == 1:
+                return ops.embedding(batch.input_ids, self.embed), None
+            # VocabParallelEmbedding (layers/embedding.py:34-43): local rows, zeros elsewhere,
+            # summed over the ranks
+            h = ops.embedding(batch.input_ids, self.embed, vocab_start=self.vocab_start,
+                              vocab_len=self.vocab_len)
+            return self.comm.all_reduce(h), None
         inj = ops.embedding(batch.input_ids, self.embed, scale=c.embed_scale)
         for i in range(c.num_prelude_layers):
             inj = self._huginn_layer(self.layers[f"model.prelude.{i}"], inj, i, batch, kv)
@@ -355,14 +418,35 @@ class LoopedDecoder:
             x = self._huginn_layer(self.layers[f"model.coda.{i}"], x, layer, batch, kv)
         return ops.rmsnorm(x, self.norm, c.rms_eps)
 
-    def lm_head(self, hidden: torch.Tensor, batch: DeviceBatch | None) -> torch.Tensor:
-        """ParallelLMHead at TP=1 (layers/embedding.py:89-111)."""
+    def _lm_rows(self, hidden: torch.Tensor, batch: DeviceBatch | None) -> torch.Tensor:
         if batch is not None and batch.is_prefill:
             idx = batch.last_indices
             if idx is None:
                 idx = (batch.cu_seqlens_q[1:] - 1).long()
             hidden = ops.gather_rows(hidden, idx)
-        return ops.gemm(hidden, self.lm_head_w)
+        return hidden
+
+    def lm_head(self, hidden: torch.Tensor, batch: DeviceBatch | None) -> torch.Tensor:
+        """ParallelLMHead (layers/embedding.py:89-111): logits [B, V] (all-gathered and
+        put in vocabulary order when sharded)."""
+        logits = ops.gemm(self._lm_rows(hidden, batch), self.lm_head_w)
+        if self.world == 1:
+            return logits
+        g = self.comm.all_gather(logits)  # [t*B, V/t] rank by rank
+        bs = logits.shape[0]
+        g = g.view(self.world, bs, self.vocab_local).permute(1, 0, 2).reshape(bs, -1)
+        return g[:, : self.cfg.vocab]
+
+    def greedy(self, hidden: torch.Tensor, batch: DeviceBatch | None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """LM head + greedy sampling (sample.py:108-112) into int32 ``out``: with shards,
+        the local logits are all-gathered over NVLink and reduced by one sharded argmax."""
+        logits = ops.gemm(self._lm_rows(hidden, batch), self.lm_head_w)
+        if self.world == 1:
+            return ops.argmax(logits, out=out)
+        g = self.comm.all_gather(logits)
+        return ops.argmax_sharded(g, self.world, logits.shape[0], self.vocab_local,
+                                  self.cfg.vocab, out=out)
 
     def forward(self, batch: DeviceBatch, kv) -> torch.Tensor:
         """Full-depth pass (base.py:148-164)."""

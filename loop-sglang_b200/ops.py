@@ -27,7 +27,7 @@ __all__ = [
     "rmsnorm", "fused_add_rmsnorm", "sandwich_norm", "rope_store_kv", "rope_only", "store_kv",
     "paged_attention",
     "gemm", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
-    "gather_rows", "argmax", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
+    "gather_rows", "argmax", "argmax_sharded", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
     "last_exited_release", "device_error_word", "Workspace", "prepare_batch_inputs",
     "set_metadata",
     "LSB_EPI_NONE", "LSB_EPI_BIAS", "LSB_EPI_BIAS_AFTER_ROUND", "LSB_EPI_SWIGLU",
@@ -299,6 +299,19 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device) if out is None else out
     call("lsb_argmax", out.data_ptr(), logits.data_ptr(), logits.shape[0], logits.shape[1],
          _row_stride(logits, "logits"), _stream())
+    return out
+
+
+def argmax_sharded(gathered: torch.Tensor, shards: int, rows: int, cols: int, vocab: int,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy token over tensor-parallel logits gathered rank by rank ``[shards*rows, cols]``
+    (rank r holds vocabulary entries r*cols ..), entries >= ``vocab`` being padding."""
+    _need(gathered, BF16, "gathered")
+    if gathered.numel() != shards * rows * cols:
+        raise ValueError("argmax_sharded: gathered logits have the wrong size")
+    out = torch.empty(rows, dtype=torch.int32, device=gathered.device) if out is None else out
+    call("lsb_argmax_sharded", out.data_ptr(), gathered.data_ptr(), shards, rows, cols, vocab,
+         _stream())
     return out
 
 

@@ -154,14 +154,16 @@ def replay_cdb(name: str, dtype=torch.float32) -> tuple[dict, dict[str, torch.Te
 # ---------------------------------------------------------------------------
 
 
-def gpu_model(cfg: LoopedConfig, weights, policy: str):
+def gpu_model(cfg: LoopedConfig, weights, policy: str, comm=None):
+    """The CUDA-path model; with ``comm`` this rank's tensor-parallel shard of it."""
     from __graft_entry__ import load_package
 
     load_package()
     from loop_sglang_b200.model import LoopedConfig as GpuConfig
     from loop_sglang_b200.model import LoopedDecoder
 
-    return LoopedDecoder(GpuConfig(**cfg.__dict__), weights, policy, torch.device("cuda"))
+    return LoopedDecoder(GpuConfig(**cfg.__dict__), weights, policy, torch.device("cuda"),
+                         comm=comm)
 
 
 def device_batch(fx: dict, prefix: str, ids, is_prefill: bool, page_size: int):
@@ -175,12 +177,13 @@ def device_batch(fx: dict, prefix: str, ids, is_prefill: bool, page_size: int):
                        max_seqlen=int(b.page_table.shape[1]) * page_size)
 
 
-def gpu_replay_cb(name: str) -> tuple[dict, dict[str, torch.Tensor]]:
-    """CUDA-path logits for every step of a CB fixture (bf16 weights)."""
+def gpu_replay_cb(name: str, comm=None) -> tuple[dict, dict[str, torch.Tensor]]:
+    """CUDA-path logits for every step of a CB fixture (bf16 weights; sharded over
+    ``comm``'s ranks when given)."""
     cfg, policy = CB_CASES[name]
     fx = load(name)
     weights = make_weights(cfg, int(fx["seed"]), dtype=torch.float32, gate_bias=0.0)
-    model = gpu_model(cfg, weights, policy)
+    model = gpu_model(cfg, weights, policy, comm)
     page = int(fx["page_size"])
     kv = model.make_kv_cache(NUM_PAGES, page)
     out = {}
@@ -192,12 +195,13 @@ def gpu_replay_cb(name: str) -> tuple[dict, dict[str, torch.Tensor]]:
     return fx, out
 
 
-def gpu_replay_cdb(name: str) -> tuple[dict, dict[str, torch.Tensor]]:
-    """CUDA-path prefill, prelude, mixed-depth fused core phases and coda of a CDB fixture."""
+def gpu_replay_cdb(name: str, comm=None) -> tuple[dict, dict[str, torch.Tensor]]:
+    """CUDA-path prefill, prelude, mixed-depth fused core phases and coda of a CDB fixture
+    (sharded over ``comm``'s ranks when given)."""
     cfg, policy = CDB_CASES[name]
     fx = load(name)
     weights = make_weights(cfg, int(fx["seed"]), dtype=torch.float32, gate_bias=0.3)
-    model = gpu_model(cfg, weights, policy)
+    model = gpu_model(cfg, weights, policy, comm)
     dev = torch.device("cuda")
     kv = model.make_kv_cache(CDB_NUM_PAGES, 1)
     res: dict[str, torch.Tensor] = {}

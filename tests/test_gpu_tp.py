@@ -1,5 +1,7 @@
-"""Tensor-parallel exchange on two GPUs: all-reduce, all-gather and the fused
-row-parallel GEMM + all-reduce, each against an exact host-side restatement.
+"""Tensor parallelism on two GPUs: all-reduce, all-gather and the fused
+row-parallel GEMM + all-reduce, each against an exact host-side restatement, and
+the Ouro looped decoder sharded over both ranks (CB under all three KV policies,
+CDB phases) against the oracle.
 
 Every rank generates every rank's inputs from per-rank seeds, so each can build
 the expected result itself: the sum of the ranks' bf16 partials in rank order in
@@ -98,6 +100,33 @@ def _worker(rank: int, world: int, port: int, errq) -> None:
                 # with the largest output, not with each element
                 scale = float(ref.abs().max())
                 torch.testing.assert_close(got.float().cpu(), ref, rtol=2e-2, atol=1e-2 * scale)
+        torch.cuda.synchronize()
+        assert ops.device_error_word(reset=True) == 0
+
+        # the whole looped decoder sharded over the two ranks, against the oracle
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from replay import gpu_replay_cb, gpu_replay_cdb, replay_cb, replay_cdb
+        from test_gpu_model import greedy_agrees, rel_err
+
+        for name in ("ouro_cb_depth_indexed", "ouro_cb_shared", "ouro_cb_last_exited"):
+            _, got = gpu_replay_cb(name, comm=cm)
+            _, ref, _ = replay_cb(name, dtype=torch.bfloat16)
+            for prefix, logits in got.items():
+                assert rel_err(logits, ref[prefix]) < 2e-2, (name, prefix)
+                assert greedy_agrees(logits, ref[prefix]), (name, prefix)
+        for name in ("ouro_cdb_last_exited", "ouro_cdb_shared"):
+            fx, got = gpu_replay_cdb(name, comm=cm)
+            _, ref = replay_cdb(name, dtype=torch.bfloat16)
+            assert rel_err(got["prefill_logits"], ref["prefill_logits"]) < 2e-2, name
+            k = 0
+            while f"core{k}_rows" in fx:
+                assert rel_err(got[f"core{k}_hidden"], ref[f"core{k}_hidden"]) < 2e-2, (name, k)
+                p = ref[f"core{k}_exit"]
+                sure = (p - 0.5).abs() > 1e-3
+                assert torch.equal(got[f"core{k}_gates"][sure], ref[f"core{k}_gates"][sure])
+                k += 1
+            assert rel_err(got["coda_logits"], ref["coda_logits"]) < 2e-2, name
+            assert greedy_agrees(got["coda_logits"], ref["coda_logits"]), name
         torch.cuda.synchronize()
         assert ops.device_error_word(reset=True) == 0
         cm.close()
