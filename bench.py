@@ -17,7 +17,11 @@ ids are synthetic (seeded random), as are the weights.
 per-step call with host buffers (H2D of the scheduler inputs, D2H of the tokens).
 ``--impl reference`` times the CPU oracle restatement of the same decode step
 (the reference's own code path restated on the host cores) on a bounded sample.
-With N > 1 (torchrun) every rank runs an independent replica (weak scaling).
+With N > 1 (torchrun, one process per GPU) the model runs tensor-parallel over the
+N GPUs (the reference's TP split; o_proj and down_proj fused with their NVLink
+all-reduce): every rank holds 1/N of the weights and KV heads, so the KV pool
+admits more of the 256 requests and the whole job's tokens per second is the
+running batch's (strong scaling on the fixed 256-request workload).
 """
 
 from __future__ import annotations
@@ -47,6 +51,7 @@ PROMPT_RANGE = (512, 2048)
 OUT_TOKENS = 256
 MID = 128  # decode position inside the generation when timing starts
 SEED = 0
+NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction on this pool's B200s
 
 
 # Measured DRAM traffic of the decode attention kernel per context token (K+V of 16
@@ -229,6 +234,7 @@ def run_b200(args) -> None:
 
     load_package()
     from loop_sglang_b200 import _lib, ops
+    from loop_sglang_b200.comm import B200Communicator
     from loop_sglang_b200.engine import DecodeEngine
     from loop_sglang_b200.model import LoopedConfig, LoopedDecoder
 
@@ -244,12 +250,16 @@ def run_b200(args) -> None:
                                              device_id=dev)
     cfg = LoopedConfig(**OURO_14B)
     t0 = time.perf_counter()
-    weights = gpu_weights(cfg, dev, SEED)
-    model = LoopedDecoder(cfg, weights, "depth_indexed", dev)
+    comm = None
+    if world > 1:  # symmetric buffer: the largest all-reduce / LM-head gather of a step
+        vocab_local = -(-cfg.vocab // world)
+        comm = B200Communicator(rank, world, NUM_REQS * max(cfg.hidden, vocab_local))
+    weights = gpu_weights(cfg, dev, SEED)  # same seed on every rank: the same full model
+    model = LoopedDecoder(cfg, weights, "depth_indexed", dev, comm=comm)
     del weights
     torch.cuda.empty_cache()
     prompts = request_lengths()
-    page_bytes = 2 * model.num_kv_layers * PAGE * cfg.kv_heads * cfg.head_dim * 2
+    page_bytes = 2 * model.num_kv_layers * PAGE * model.hkv * cfg.head_dim * 2
     free, _ = torch.cuda.mem_get_info(dev)
     pool_pages = int((free - 8 * 2**30) // page_bytes)
     if args.batch:
@@ -321,9 +331,9 @@ def run_b200(args) -> None:
 
     # roofline of the dominant kernel: layer-0 attention of the same batch, timed alone
     ctx = (sched[args.warmup + args.steps - 1]).to(torch.int64)
-    attn_bytes = int(ctx.sum().item()) * cfg.kv_heads * cfg.head_dim * 2 * 2 \
-        + 2 * bs * cfg.heads * cfg.head_dim * 2
-    q = torch.randn(bs, cfg.heads, cfg.head_dim, device=dev).to(torch.bfloat16)
+    attn_bytes = int(ctx.sum().item()) * model.hkv * cfg.head_dim * 2 * 2 \
+        + 2 * bs * model.hq * cfg.head_dim * 2
+    q = torch.randn(bs, model.hq, cfg.head_dim, device=dev).to(torch.bfloat16)
     kc, vc = kv.slots(0)
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 20
@@ -331,11 +341,11 @@ def run_b200(args) -> None:
         out = torch.empty_like(q)
         for _ in range(3):
             ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, cfg.kv_heads, out=out)
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
         a0.record(s)
         for _ in range(reps):
             ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, cfg.kv_heads, out=out)
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
         a1.record(s)
         s.synchronize()
     attn_s = a0.elapsed_time(a1) / 1000.0 / reps
@@ -346,39 +356,50 @@ def run_b200(args) -> None:
         t = torch.tensor([total_ms, e2e_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         t_max, e2e_max = float(t[0]), float(t[1])
-    tokens = bs * args.steps * world
+    tokens = bs * args.steps  # tensor parallel: every rank decodes the same batch
     value = tokens / (t_max / 1000.0)
     mean_ctx = float(ctx.float().mean())
     weight_bytes = sum(t.numel() * 2 for lw in model.layers.values()
                        for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) * cfg.loop_steps \
         + model.lm_head_w.numel() * 2 + bs * cfg.hidden * 2
-    kv_bytes = int(ctx.sum().item()) * model.num_kv_layers * cfg.kv_heads * cfg.head_dim * 4
+    kv_bytes = int(ctx.sum().item()) * model.num_kv_layers * model.hkv * cfg.head_dim * 4
     step_bytes = weight_bytes + kv_bytes
     peak, peak_kind = peaks()
+    # NVLink bytes each rank sends per step: 2 fused all-reduces per layer and loop step
+    # (a bf16 [bs, hidden] output: partials to the owners, sums back, each (t-1)/t of
+    # it), the embedding all-reduce and the LM-head gather of bs x V/t logits.
+    nvlink_bytes = 0
+    if world > 1:
+        ar = 2 * (world - 1) / world * bs * cfg.hidden * 2
+        nvlink_bytes = int(ar * (2 * cfg.num_core_layers * cfg.loop_steps + 1)
+                           + (world - 1) * bs * model.vocab_local * 2)
+    step_s = t_max / 1000.0 / args.steps
+    ideal_s = max(step_bytes / (peak * 1e9), nvlink_bytes / (NVLINK_GBS * 1e9))
     achieved = attn_bytes / attn_s / 1e9
     # DRAM bytes per launch: ncu's dram__bytes_read.sum + dram__bytes_write.sum of one
     # launch of the same kernel on a one-layer case (profiles/paged_attention_*.md),
     # per context token, scaled by this batch's context tokens (traffic grows with them).
-    traffic = ATTN_DRAM_BYTES_PER_CTX_TOKEN * int(ctx.sum().item())
+    traffic = ATTN_DRAM_BYTES_PER_CTX_TOKEN * model.hkv / cfg.kv_heads * int(ctx.sum().item())
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_max / args.steps,
-        "p50_tpot_ms": statistics.median(step_ms), "higher_is_better": True, "scaling": "weak",
+        "p50_tpot_ms": statistics.median(step_ms), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded random-init weights, random KV contents and token ids",
         "config": {"workload": WORKLOAD, "model": "Ouro-1.4B architecture (random init)",
-                   "global_batch": bs * world, "running_batch_per_gpu": bs,
+                   "global_batch": bs, "running_batch_per_gpu": bs,
                    "mean_context": round(mean_ctx, 1), "kv_pool_pages": num_pages,
-                   "page_size": PAGE, "parallelism": f"dp{world}" if world > 1 else "tp1",
+                   "page_size": PAGE, "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2 (each step streams the KV pool, ~%d GB)"
                          % (step_bytes // 10**9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": round(traffic),
                      "kernel": "paged_attention (layer-0 decode, whole running batch)",
                      "peak_kind": peak_kind,
-                     "step_frac": round(step_bytes / (t_max / 1000.0 / args.steps) / 1e9 / peak
-                                        * (1 if world == 1 else 1), 4),
-                     "step_bytes": step_bytes},
+                     "step_frac": round(step_bytes / step_s / 1e9 / peak, 4),
+                     "step_bytes": step_bytes, "nvlink_bytes_per_step": nvlink_bytes,
+                     "combined_step_frac": round(ideal_s / step_s, 4)},
         "e2e": {"value": tokens / (e2e_max / 1000.0), "unit": "tok/s",
                 "h2d_bytes_per_step": 2 * bs * 4, "d2h_bytes_per_step": bs * 4},
         "gpu_launches": eng.launches_per_step * args.steps,
@@ -394,6 +415,8 @@ def run_b200(args) -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     eng.graph = None
+    if comm is not None:
+        comm.close()
     if world > 1:
         torch.distributed.destroy_process_group()
     _ = _lib

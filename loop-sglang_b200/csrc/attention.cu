@@ -296,14 +296,15 @@ constexpr int kStreamMaxHeads = 4 * kConsumerWarps;
 constexpr int kStreamUnroll = 4;             // keys per lane group per stage
 constexpr int kStreamStageBudget = 64 * 1024;  // bytes of K + V per stage
 constexpr int kStreamSmemBudget = 220 * 1024;
-constexpr int kMaxStreamStages = 8;
+constexpr int kMaxStreamStages = 16;
+constexpr int kMaxStageTokens = 64;  // bits of the per-stage valid mask
 constexpr int kRowCounterBase = 2;  // counters[0]: next item, [1]: CTAs finished
 
 enum : int { kItemFirst = 1, kItemLast = 2, kStreamExit = 4 };
 
 struct StageHdr {
-  int row, split, nsplit, t0, ntok, flags, qbuf;
-  uint32_t valid;  // bit i: key t0 + i has a slot inside the pool
+  int row, split, nsplit, t0, ntok, flags, qbuf, pad;
+  uint64_t valid;  // bit i: key t0 + i has a slot inside the pool
 };
 
 struct StreamParams {
@@ -320,6 +321,8 @@ struct StreamParams {
   const int32_t* cu_seqlens_q;
   int num_reqs, rows, hq, hkv, page_size;
   int chunk, max_splits, stages;
+  int sub;              // blocks of stream_tokens(D) keys per stage
+  int warps_per_head;   // consumer warps sharing a query head (1 when hq >= 16)
   int64_t max_seqlen;
   float scale_log2;
   Workspace ws;
@@ -334,10 +337,10 @@ struct StreamLayout {
 };
 
 __host__ __device__ inline StreamLayout stream_layout(int d, int hq, int hkv, int chunk,
-                                                      int page_size, int stages) {
+                                                      int page_size, int stages, int sub) {
   StreamLayout L;
   const int row_bytes = hkv * d * 2;
-  L.stage_bytes = 2 * stream_tokens(d) * row_bytes;
+  L.stage_bytes = 2 * stream_tokens(d) * sub * row_bytes;
   L.q_bytes = (hq * d * 2 + 127) & ~127;
   L.pages_cap = chunk / page_size + 2;
   L.off_q = stages * L.stage_bytes;
@@ -373,9 +376,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
   constexpr int kLanes = lanes_for(D);
   constexpr int kGroups = 32 / kLanes;
   constexpr int kVec = D / 8;
-  constexpr int T = stream_tokens(D);
+  constexpr int TB = stream_tokens(D);  // keys per block: kStreamUnroll per lane group
+  const int T = TB * p.sub;             // keys per stage
   extern __shared__ __align__(128) uint8_t smem[];
-  const StreamLayout L = stream_layout(D, p.hq, p.hkv, p.chunk, p.page_size, p.stages);
+  const StreamLayout L = stream_layout(D, p.hq, p.hkv, p.chunk, p.page_size, p.stages, p.sub);
   const int row_bytes = p.hkv * D * 2;
   uint8_t* const sq = smem + L.off_q;
   int32_t* const s_pages = reinterpret_cast<int32_t*>(smem + L.off_pages);
@@ -409,19 +413,26 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
     const int q_copy = p.hq * D * 2;
     int gs = 0, nitem = 0;
     bool ok = true;
+    // (claiming the next item ahead of time was measured to hurt: a CTA that holds two
+    // items unbalances the tail of the queue)
+    int next = 0;
+    const bool one_row_per_req = p.rows == p.num_reqs;  // decode: row r is request r
     while (ok) {
-      int item = 0;
-      if (lane == 0) item = atomicAdd(queue, 1);
-      item = __shfl_sync(0xffffffffu, item, 0);
+      if (lane == 0) next = atomicAdd(queue, 1);
+      next = __shfl_sync(0xffffffffu, next, 0);
+      const int item = next;
       if (item >= total) break;
       const int split = item / p.rows;
       const int row = item - split * p.rows;
-      int lo = 0, hi = p.num_reqs - 1;  // request of the row
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (p.cu_seqlens_q[mid] <= row) lo = mid; else hi = mid - 1;
+      int b = row;
+      if (!one_row_per_req) {
+        int lo = 0, hi = p.num_reqs - 1;  // request of the row
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (p.cu_seqlens_q[mid] <= row) lo = mid; else hi = mid - 1;
+        }
+        b = lo;
       }
-      const int b = lo;
       int64_t kv_len = static_cast<int64_t>(p.cache_seqlens[b]) - (p.cu_seqlens_q[b + 1] - 1 - row);
       // a context longer than max_seqlen is cut there (and flagged): the page table of
       // the row has no entries beyond it
@@ -463,7 +474,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
           }
           uint8_t* const sk = smem + s * L.stage_bytes;
           uint8_t* const sv = sk + T * row_bytes;
-          uint32_t valid = 0, bytes = 0;
+          uint64_t valid = 0;
+          uint32_t bytes = 0;
           int run_i = 0, run_n = 0;
           int64_t run_slot = 0;
           auto flush = [&]() {
@@ -475,40 +487,45 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
             run_n = 0;
           };
           const bool packed = p.slot_stride == static_cast<int64_t>(p.hkv) * D;
-          // A stage inside one page of a packed pool is one run: two copies, no per-key work.
-          int i_begin = 0;
-          if (packed && ntok > 0) {
-            const int pg0 = pow2 ? (t0 >> pshift) : t0 / p.page_size;
-            const int pg1 = pow2 ? ((t0 + ntok - 1) >> pshift) : (t0 + ntok - 1) / p.page_size;
-            const int64_t slot0 = static_cast<int64_t>(s_pages[pg0 - p_first]) * p.page_size +
-                                  (t0 - pg0 * p.page_size);
-            if (pg0 == pg1 && slot0 >= 0 && slot0 + ntok <= p.num_slots) {
-              run_i = 0;
-              run_slot = slot0;
-              run_n = ntok;
-              valid = ntok == 32 ? 0xffffffffu : ((1u << ntok) - 1u);
-              i_begin = ntok;
-            }
-          }
-          for (int i = i_begin; i < ntok; ++i) {
+          // Page by page: the keys of a page are consecutive slots, one run when the
+          // pool is packed (runs merge across pages that happen to be adjacent).
+          for (int i = 0; i < ntok;) {
             const int t = t0 + i;
-            const int pg = pow2 ? (t >> pshift) : t / p.page_size;
-            const int64_t slot = static_cast<int64_t>(s_pages[pg - p_first]) * p.page_size +
-                                 (t - pg * p.page_size);
-            if (slot < 0 || slot >= p.num_slots) {
+            int pg, off;
+            if (pow2) {
+              pg = t >> pshift;
+              off = t & (p.page_size - 1);
+            } else {
+              pg = t / p.page_size;
+              off = t - pg * p.page_size;
+            }
+            const int n = p.page_size - off < ntok - i ? p.page_size - off : ntok - i;
+            const int64_t slot0 = static_cast<int64_t>(s_pages[pg - p_first]) * p.page_size + off;
+            if (slot0 < 0 || slot0 + n > p.num_slots) {  // outside the pool: skipped, flagged
               if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
               flush();
+              i += n;
               continue;
             }
-            valid |= 1u << i;
-            if (run_n > 0 && packed && slot == run_slot + run_n && i == run_i + run_n) {
-              ++run_n;
+            valid |= (n >= 64 ? ~0ull : ((1ull << n) - 1ull)) << i;
+            if (packed) {
+              if (run_n > 0 && slot0 == run_slot + run_n && i == run_i + run_n) {
+                run_n += n;
+              } else {
+                flush();
+                run_i = i;
+                run_slot = slot0;
+                run_n = n;
+              }
             } else {
-              flush();
-              run_i = i;
-              run_slot = slot;
-              run_n = 1;
+              for (int j = 0; j < n; ++j) {
+                flush();
+                run_i = i + j;
+                run_slot = slot0 + j;
+                run_n = 1;
+              }
             }
+            i += n;
           }
           flush();
           StageHdr h;
@@ -538,12 +555,30 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
     }
   } else {
     // ---------------------------------------------------------- consumers --
+    // With fewer query heads than warps, the warps of a head split the blocks of every
+    // stage (warp sub-index wsub takes blocks wsub, wsub + G, ...) and each keeps its own
+    // softmax state; their partials are merged like the splits of a long row.
     const int cw = warp - 1;
+    const int G = p.warps_per_head;
+    const int h_first = G == 1 ? cw : cw / G;
+    const int wsub = G == 1 ? 0 : cw % G;
+    const bool active = h_first < p.hq;
     const int g = lane / kLanes;
     const int c = lane % kLanes;
     const bool dim_ok = c < kVec;
     const int group_base = lane & ~(kLanes - 1);
     const int qpk = p.hq / p.hkv;
+    const int64_t parts = static_cast<int64_t>(p.max_splits) * G;  // partials per (row, head)
+    int heads[HPW];     // this warp's query heads (p.hq: none)
+    int head_off[HPW];  // byte offset of the head's KV head and 8-dim vector in a key row
+#pragma unroll
+    for (int j = 0; j < HPW; ++j) {
+      heads[j] = G == 1 ? cw + kConsumerWarps * j : (j == 0 ? h_first : p.hq);
+      if (heads[j] > p.hq) heads[j] = p.hq;
+      head_off[j] = (heads[j] < p.hq ? heads[j] / qpk : 0) * D * 2 + 16 * c;
+    }
+    auto head_of = [&](int j) { return heads[j]; };
+    const int key_off = (g * row_bytes);  // this lane group's first key in a block
     float qv[HPW][8], acc[HPW][8], m[HPW], l[HPW];
     int gs = 0, nitem = 0;
     while (true) {
@@ -560,7 +595,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         const uint8_t* qrow = sq + hd.qbuf * L.q_bytes;
 #pragma unroll
         for (int j = 0; j < HPW; ++j) {
-          const int h = cw + kConsumerWarps * j;
+          const int h = head_of(j);
           if (h < p.hq && dim_ok) {
             unpack8(*reinterpret_cast<const bf16x8*>(qrow + (h * D + 8 * c) * 2), qv[j]);
 #pragma unroll
@@ -577,63 +612,69 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         __syncwarp();
         if (lane == 0) mbar_arrive(&qempty[hd.qbuf]);
       }
-      const uint8_t* sk = smem + s * L.stage_bytes;
-      const uint8_t* sv = sk + T * row_bytes;
-      bool kvalid[kStreamUnroll];
+      if (active) {
+        const uint8_t* stage_k = smem + s * L.stage_bytes + key_off;
+        const int v_off = T * row_bytes;
+        for (int blk = wsub; blk * TB < hd.ntok; blk += G) {
+          const uint8_t* sk = stage_k + blk * TB * row_bytes;
+          const uint8_t* sv = sk + v_off;
+          // this block's bits of the valid mask, lane group g's key of step u at bit u*kGroups
+          const uint32_t vb = static_cast<uint32_t>(hd.valid >> (blk * TB)) >> g;
+          const int left = hd.ntok - blk * TB - g;  // keys of this block left for group g
+          bool kvalid[kStreamUnroll];
 #pragma unroll
-      for (int u = 0; u < kStreamUnroll; ++u) {
-        const int i = u * kGroups + g;
-        kvalid[u] = i < hd.ntok && ((hd.valid >> i) & 1u);
-      }
+          for (int u = 0; u < kStreamUnroll; ++u)
+            kvalid[u] = u * kGroups < left && ((vb >> (u * kGroups)) & 1u);
 #pragma unroll
-      for (int j = 0; j < HPW; ++j) {
-        const int h = cw + kConsumerWarps * j;
-        if (h >= p.hq) break;
-        const int off = (h / qpk) * D * 2 + 16 * c;
-        float part[kStreamUnroll];
+          for (int j = 0; j < HPW; ++j) {
+            if (heads[j] >= p.hq) break;
+            const int off = head_off[j];
+            float part[kStreamUnroll];
 #pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) {
-          part[u] = 0.f;
-          if (dim_ok) {
-            float kf[8];
-            unpack8(*reinterpret_cast<const bf16x8*>(sk + (u * kGroups + g) * row_bytes + off), kf);
+            for (int u = 0; u < kStreamUnroll; ++u) {
+              part[u] = 0.f;
+              if (dim_ok) {
+                float kf[8];
+                unpack8(*reinterpret_cast<const bf16x8*>(sk + u * kGroups * row_bytes + off), kf);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) part[u] = fmaf(qv[j][e], kf[e], part[u]);
-          }
-        }
-        const float red = butterfly4<kLanes>(part[0], part[1], part[2], part[3], lane);
-        float sc[kStreamUnroll];
-#pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) {
-          const int src = group_base + (u >> 1) * (kLanes / 2) + (u & 1) * (kLanes / 4);
-          const float v = __shfl_sync(0xffffffffu, red, src);
-          sc[u] = kvalid[u] ? v : kNegBig;
-        }
-        float mx = m[j];
-#pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) mx = fmaxf(mx, sc[u]);
-        const float corr = exp2f(m[j] - mx);
-        l[j] *= corr;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[j][e] *= corr;
-#pragma unroll
-        for (int u = 0; u < kStreamUnroll; ++u) {
-          if (kvalid[u]) {
-            const float pr = exp2f(sc[u] - mx);
-            l[j] += pr;
-            if (dim_ok) {
-              float vf[8];
-              unpack8(*reinterpret_cast<const bf16x8*>(sv + (u * kGroups + g) * row_bytes + off), vf);
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc[j][e] = fmaf(pr, vf[e], acc[j][e]);
+                for (int e = 0; e < 8; ++e) part[u] = fmaf(qv[j][e], kf[e], part[u]);
+              }
             }
+            const float red = butterfly4<kLanes>(part[0], part[1], part[2], part[3], lane);
+            float sc[kStreamUnroll];
+#pragma unroll
+            for (int u = 0; u < kStreamUnroll; ++u) {
+              const int src = group_base + (u >> 1) * (kLanes / 2) + (u & 1) * (kLanes / 4);
+              const float v = __shfl_sync(0xffffffffu, red, src);
+              sc[u] = kvalid[u] ? v : kNegBig;
+            }
+            float mx = m[j];
+#pragma unroll
+            for (int u = 0; u < kStreamUnroll; ++u) mx = fmaxf(mx, sc[u]);
+            const float corr = exp2f(m[j] - mx);
+            l[j] *= corr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[j][e] *= corr;
+#pragma unroll
+            for (int u = 0; u < kStreamUnroll; ++u) {
+              if (kvalid[u]) {
+                const float pr = exp2f(sc[u] - mx);
+                l[j] += pr;
+                if (dim_ok) {
+                  float vf[8];
+                  unpack8(*reinterpret_cast<const bf16x8*>(sv + u * kGroups * row_bytes + off), vf);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) acc[j][e] = fmaf(pr, vf[e], acc[j][e]);
+                }
+              }
+            }
+            m[j] = mx;
           }
         }
-        m[j] = mx;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
-      if (!(hd.flags & kItemLast)) continue;
+      if (!(hd.flags & kItemLast) || !active) continue;
 
       // ---- end of an item: merge the lane groups, publish, maybe merge the row
       const int64_t row = hd.row;
@@ -653,10 +694,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         }
       }
       const bool writer = g == 0 && dim_ok;
-      if (hd.nsplit == 1) {
+      if (hd.nsplit == 1 && G == 1) {
 #pragma unroll
         for (int j = 0; j < HPW; ++j) {
-          const int h = cw + kConsumerWarps * j;
+          const int h = head_of(j);
           if (h < p.hq && writer) {
             const float inv = l[j] > 0.f ? 1.f / l[j] : 0.f;
             float o8[8];
@@ -667,50 +708,65 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         }
         continue;
       }
+      const int64_t nparts = static_cast<int64_t>(hd.nsplit) * G;
 #pragma unroll
       for (int j = 0; j < HPW; ++j) {
-        const int h = cw + kConsumerWarps * j;
+        const int h = head_of(j);
         if (h < p.hq && writer) {
-          const int64_t idx = (row * p.hq + h) * p.max_splits + hd.split;
+          const int64_t idx = (row * p.hq + h) * parts + static_cast<int64_t>(hd.split) * G + wsub;
           float4* po = reinterpret_cast<float4*>(p.ws.partial_o + idx * D + 8 * c);
           po[0] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
           po[1] = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
           if (c == 0) *reinterpret_cast<float2*>(p.ws.partial_ml + idx * 2) = make_float2(m[j], l[j]);
         }
       }
-      // One arrival counter per (row, consumer warp): the warp that completes a row's
-      // set of splits merges its own heads, without waiting for the other warps.
+      // One arrival counter per (row, head): whichever warp delivers a head's last
+      // partial merges that head, without waiting for any other warp.
       __threadfence();
       __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        int* counter = p.ws.counters + kRowCounterBase + row * kConsumerWarps + cw;
-        const int prev = atomicAdd(counter, 1);
-        last = prev == hd.nsplit - 1;
-        if (last) *counter = 0;  // every split has arrived: reset for the next launch
-      }
-      if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-      __threadfence();
       constexpr int kQuads = D / 4;
       for (int j = 0; j < HPW; ++j) {
-        const int h = cw + kConsumerWarps * j;
+        const int h = head_of(j);
         if (h >= p.hq) break;
-        const int64_t base_idx = (row * p.hq + h) * p.max_splits;
+        int last = 0;
+        if (lane == 0) {
+          int* counter = p.ws.counters + kRowCounterBase + row * p.hq + h;
+          const int prev = atomicAdd(counter, 1);
+          last = prev == nparts - 1;
+          if (last) *counter = 0;  // every partial has arrived: reset for the next launch
+        }
+        if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+        __threadfence();
+        const int64_t base_idx = (row * p.hq + h) * parts;
         float mt = kNegBig, lt = 0.f;
         float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s2 = 0; s2 < hd.nsplit; ++s2) {
-          const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws.partial_ml + (base_idx + s2) * 2));
-          const float mn = fmaxf(mt, ml.x);
-          const float c1 = exp2f(mt - mn), c2 = exp2f(ml.x - mn);
-          lt = lt * c1 + ml.y * c2;
-          float4 po = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (lane < kQuads)
-            po = __ldcg(reinterpret_cast<const float4*>(p.ws.partial_o + (base_idx + s2) * D) + lane);
-          ot.x = ot.x * c1 + po.x * c2;
-          ot.y = ot.y * c1 + po.y * c2;
-          ot.z = ot.z * c1 + po.z * c2;
-          ot.w = ot.w * c1 + po.w * c2;
-          mt = mn;
+        // 8 partials per batch: all their loads are in flight before the first is used
+        constexpr int kBatch = 8;
+        for (int64_t s0 = 0; s0 < nparts; s0 += kBatch) {
+          float2 ml[kBatch];
+          float4 po[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            ml[u] = make_float2(kNegBig, 0.f);
+            po[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (s0 + u < nparts) {
+              ml[u] = __ldcg(reinterpret_cast<const float2*>(p.ws.partial_ml + (base_idx + s0 + u) * 2));
+              if (lane < kQuads)
+                po[u] = __ldcg(reinterpret_cast<const float4*>(p.ws.partial_o + (base_idx + s0 + u) * D) + lane);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            if (s0 + u >= nparts) break;
+            const float mn = fmaxf(mt, ml[u].x);
+            const float c1 = exp2f(mt - mn), c2 = exp2f(ml[u].x - mn);
+            lt = lt * c1 + ml[u].y * c2;
+            ot.x = ot.x * c1 + po[u].x * c2;
+            ot.y = ot.y * c1 + po[u].y * c2;
+            ot.z = ot.z * c1 + po[u].z * c2;
+            ot.w = ot.w * c1 + po[u].w * c2;
+            mt = mn;
+          }
         }
         if (lane < kQuads) {
           const float inv = lt > 0.f ? 1.f / lt : 0.f;
@@ -749,13 +805,16 @@ int num_sms_attention() {
 }
 
 // Keys per item for the streaming kernel: enough items for about 16 per SM (so the
-// queue balances rows of different lengths), at least one stage, at most 1024.
-int64_t stream_chunk_for(int64_t rows, int64_t max_seqlen, int d) {
+// queue balances rows of different lengths), at least 64 keys, at most 1024.
+int64_t stream_chunk_for(int64_t rows, int64_t max_seqlen) {
   const int64_t want = 16 * static_cast<int64_t>(num_sms_attention());
   int64_t chunk = 1024;
-  const int64_t floor_chunk = stream_tokens(d) > 64 ? stream_tokens(d) : 64;
-  while (chunk > floor_chunk && rows * ((max_seqlen + chunk - 1) / chunk) < want) chunk >>= 1;
+  while (chunk > 64 && rows * ((max_seqlen + chunk - 1) / chunk) < want) chunk >>= 1;
   return chunk;
+}
+
+int stream_warps_per_head(int32_t hq) {
+  return hq >= kConsumerWarps ? 1 : kConsumerWarps / hq;
 }
 
 bool stream_eligible(int32_t hq, int32_t hkv, int32_t d) {
@@ -770,8 +829,7 @@ using namespace lsb;
 // The streaming kernel runs when its stage fits and its per-(row, warp) counters fit
 // the counter region; otherwise the per-CTA kernel does.
 static bool use_stream(int64_t rows, int32_t hq, int32_t hkv, int32_t d) {
-  return stream_eligible(hq, hkv, d) &&
-         rows * kConsumerWarps <= kCounterCap - kRowCounterBase;
+  return stream_eligible(hq, hkv, d) && rows * hq <= kCounterCap - kRowCounterBase;
 }
 
 extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, int32_t head_dim,
@@ -782,8 +840,9 @@ extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, 
   const int64_t splits = (max_seqlen + chunk - 1) / chunk;
   int64_t bytes = workspace_bytes_for(rows, hq, head_dim, splits);
   if (hq <= kStreamMaxHeads) {
-    const int64_t sc = stream_chunk_for(rows, max_seqlen, head_dim);
-    const int64_t b2 = workspace_bytes_for(rows, hq, head_dim, (max_seqlen + sc - 1) / sc);
+    const int64_t sc = stream_chunk_for(rows, max_seqlen);
+    const int64_t b2 = workspace_bytes_for(rows, hq, head_dim,
+                                           (max_seqlen + sc - 1) / sc * stream_warps_per_head(hq));
     if (b2 > bytes) bytes = b2;
   }
   return bytes;
@@ -811,11 +870,12 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
   LSB_REQUIRE(slot_stride >= (int64_t)hkv * head_dim, "paged_attention: slot stride too small");
   if (rows <= 0) return LSB_OK;
   if (use_stream(rows, hq, hkv, head_dim)) {
-    const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim);
+    const int64_t chunk = stream_chunk_for(rows, max_seqlen);
     const int64_t splits = (max_seqlen + chunk - 1) / chunk;
     LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
                 "paged_attention: max_seqlen too large");
-    const int64_t need = workspace_bytes_for(rows, hq, head_dim, splits);
+    const int wph = stream_warps_per_head(hq);
+    const int64_t need = workspace_bytes_for(rows, hq, head_dim, splits * wph);
     LSB_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
                 "paged_attention: workspace of %lld bytes needed", (long long)need);
     StreamParams sp;
@@ -840,14 +900,21 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
     sp.max_splits = static_cast<int>(splits);
     sp.max_seqlen = max_seqlen;
     sp.scale_log2 = scale * kLog2e;
-    sp.ws = carve(workspace, rows, hq, head_dim, splits);
+    sp.ws = carve(workspace, rows, hq, head_dim, splits * wph);
+    sp.warps_per_head = wph;
     sp.error_flag = lsb_device_error_flag();
-    const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0);
+    // blocks per stage: about 64 KB of K+V per stage, at most 64 keys
+    const int tb = stream_tokens(head_dim);
+    int sub = kStreamStageBudget / (2 * tb * hkv * head_dim * 2);
+    if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
+    if (sub < 1) sub = 1;
+    sp.sub = sub;
+    const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0, sub);
     int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
     if (stages > kMaxStreamStages) stages = kMaxStreamStages;
     LSB_REQUIRE(stages >= 2, "paged_attention: stage of %d bytes too large", probe.stage_bytes);
     sp.stages = stages;
-    const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages);
+    const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages, sub);
     const int64_t items = rows * splits;
     const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
     const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
