@@ -221,7 +221,7 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-METRIC = "decode output tok/s, Ouro-1.4B CB full depth (configs[1]), TP1 per replica"
+METRIC = "decode output tok/s, Ouro-1.4B CB full depth (configs[1]), TP over the job's GPUs"
 WORKLOAD = ("configs[1]: Ouro-1.4B random-init bf16, full-depth CB decode, depth-indexed KV, "
             "16-token pages, 256 requests prompt U[512,2048] + 256 outputs, capacity-limited "
             "running batch decoding at prompt+128")

@@ -14,7 +14,6 @@ constexpr int kCommThreads = 128;
 __global__ void __launch_bounds__(kCommThreads)
     allreduce_kernel(CommDev c, bf16* x, int64_t ld, int rows, int cols, int row_tile,
                      int* err) {
-  __shared__ uint32_t s_epoch;
   const int t = threadIdx.x;
   const int region = blockIdx.x + blockIdx.y * gridDim.x;
   const int c0 = blockIdx.x * 128;
@@ -22,10 +21,10 @@ __global__ void __launch_bounds__(kCommThreads)
   const int r0 = blockIdx.y * row_tile;
   const int r1 = r0 + row_tile < rows ? r0 + row_tile : rows;
   const int owner = region % c.world;
-  if (t == 0) s_epoch = comm_epoch(c, kOpAllReduce);
-  // this rank's partial of the region -> the owner's recv slot (dense rows of `cols`)
+  const uint32_t epoch = comm_epoch(c, kOpAllReduce);
+  // this rank's partial of the region -> the owner's recv slot (tagged words)
   const int quads = (w + 3) >> 2;
-  bf16* dst = c.recv(owner, c.rank);
+  uint64_t* dst = c.recv(owner, c.rank);
   for (int idx = t; idx < (r1 - r0) * quads; idx += kCommThreads) {
     const int m = r0 + idx / quads;
     const int col = c0 + 4 * (idx % quads);
@@ -34,12 +33,9 @@ __global__ void __launch_bounds__(kCommThreads)
     bf16 v[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(f[e]);
-    put4(dst + static_cast<int64_t>(m) * cols, col, cols, v);
+    tag_put4(dst, static_cast<int64_t>(m) * cols + col, v, epoch);
   }
-  __syncthreads();
-  const uint32_t epoch = s_epoch;
-  comm_complete(c, kOpAllReduce, region, owner, epoch, x, ld, r0, r1, c0, w, cols, cols, t,
-                kCommThreads, [] { __syncthreads(); }, err);
+  comm_complete(c, owner, epoch, x, ld, r0, r1, c0, w, cols, t, kCommThreads, err);
   __syncthreads();
   if (t == 0) comm_finish(c, kOpAllReduce, epoch, gridDim.x * gridDim.y);
 }
@@ -159,7 +155,8 @@ extern "C" int lsb_comm_destroy(lsb_comm* comm) {
 extern "C" int lsb_allreduce(lsb_comm* comm, void* x, int64_t rows, int64_t cols, int64_t ld,
                              void* stream) {
   LSB_REQUIRE(comm && x, "allreduce: null pointer");
-  LSB_REQUIRE(rows >= 0 && cols > 0 && ld >= cols, "allreduce: bad shape");
+  LSB_REQUIRE(rows >= 0 && cols > 0 && cols % 4 == 0 && ld >= cols,
+              "allreduce: cols must be a positive multiple of 4 and ld >= cols");
   LSB_REQUIRE(rows * cols <= comm->dev.max_elems, "allreduce: %lld elements exceed the buffer's %lld",
               (long long)(rows * cols), (long long)comm->dev.max_elems);
   if (rows == 0 || comm->dev.world == 1) return LSB_OK;

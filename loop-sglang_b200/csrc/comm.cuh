@@ -3,14 +3,18 @@
 //
 // Every rank of a node holds one symmetric buffer (same layout on every rank,
 // allocated with cudaMalloc and mapped into its peers with CUDA IPC). A call's
-// output is cut into regions (one per CTA, the same on every rank). The owner of
-// a region receives every rank's bf16 partial of it in recv[src], sums them in
-// rank order once every rank's flag shows this call's epoch, rounds once, writes
-// the sum to its own output and into every peer's result area, and raises the
-// peers' done flags; the other ranks copy the sum out of their result area. Flags
-// carry a per-operation epoch that every rank advances once per call (the last
-// CTA to finish stores it), so no flag is ever reset and a stale flag can never
-// match. Every wait is bounded and reports LSB_DEVERR_TIMEOUT instead of hanging.
+// output is cut into regions (one per CTA, the same on every rank) and every
+// region has an owner rank. The all-reduce moves data in "tagged words": 8-byte
+// stores carrying two bf16 values and the call's epoch, so a reader knows a word
+// is current by its tag alone -- no flag, no memory fence, one NVLink crossing per
+// hop. Each rank stores its bf16 partial of a region into the owner's recv slot;
+// the owner waits for every rank's words, sums them in rank order in fp32, rounds
+// once, writes the sum to its output and as tagged words into every peer's result
+// area; the peers copy it out. A rank can be at most one call ahead of a peer (it
+// needs that peer's words of the next call to finish it), and the epoch that every
+// rank advances once per call (the last CTA to finish stores it) tells the calls
+// apart. The all-gather keeps per-region flags (release/acquire at system scope).
+// Every wait is bounded and reports LSB_DEVERR_TIMEOUT instead of hanging.
 #pragma once
 
 #include "common.cuh"
@@ -46,24 +50,26 @@ struct CommDev {
     return reinterpret_cast<uint32_t*>(base[r] + kCommFlagsOff + op * kCommOpBytes +
                                        kCommFlagBytes);
   }
-  // recv slot `src` of rank r (partials sent to r by src)
-  __device__ __forceinline__ bf16* recv(int r, int src) const {
-    return reinterpret_cast<bf16*>(base[r] + kCommDataOff) + static_cast<int64_t>(src) * max_elems;
+  // recv slot `src` of rank r: tagged words (2 bf16 + epoch) of src's partials, one
+  // word per element pair of a [rows, cols] output
+  __device__ __forceinline__ uint64_t* recv(int r, int src) const {
+    return reinterpret_cast<uint64_t*>(base[r] + kCommDataOff) + static_cast<int64_t>(src) * (max_elems / 2);
   }
-  __device__ __forceinline__ bf16* result(int r) const {
-    return reinterpret_cast<bf16*>(base[r] + kCommDataOff) +
-           static_cast<int64_t>(kCommMaxWorld) * max_elems;
+  __device__ __forceinline__ uint64_t* result(int r) const {
+    return reinterpret_cast<uint64_t*>(base[r] + kCommDataOff) +
+           static_cast<int64_t>(kCommMaxWorld) * (max_elems / 2);
   }
   // all-gather slot `src` of rank r for calls of epoch parity `par`: a rank can run
   // at most one all-gather ahead of a peer that is still copying out of its slots
   __device__ __forceinline__ uint8_t* gather(int r, int src, int par) const {
-    return base[r] + kCommDataOff +
-           (static_cast<int64_t>(kCommMaxWorld + 1) + par * kCommMaxWorld + src) * max_elems * 2;
+    return base[r] + kCommDataOff + (static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 4 +
+           static_cast<int64_t>(par * kCommMaxWorld + src) * max_elems * 2;
   }
 };
 
 inline int64_t comm_buffer_bytes(int64_t max_elems) {
-  return kCommDataOff + (3 * static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 2;
+  return kCommDataOff + (static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 4 +
+         2 * static_cast<int64_t>(kCommMaxWorld) * max_elems * 2;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -139,65 +145,84 @@ __device__ __forceinline__ void get4(const bf16* src_row, int col, int ncols, fl
   for (int e = 0; e < 4; ++e) f[e] = col + e < ncols ? __bfloat162float(s[e]) : 0.f;
 }
 
-// Second half of the exchange for one region (rows [r0, r1) x columns [c0, c0 + w)
-// of an output with `ncols` columns and row stride `ld`), after this CTA has pushed
-// its partial of the region to the owner's recv slot. Run by `nthreads` threads
-// (index t) that synchronise with `sync()`; thread 0 handles the flags.
-// recv/result rows use a row stride of `rs` elements.
-template <typename Sync>
-__device__ __forceinline__ void comm_complete(const CommDev& c, int op, int region, int owner,
-                                              uint32_t epoch, bf16* out, int64_t ld, int r0,
-                                              int r1, int c0, int w, int ncols, int64_t rs,
-                                              int t, int nthreads, Sync sync, int* err) {
-  const int me = c.rank, W = c.world;
-  sync();  // every push of this CTA is issued
-  if (t == 0) {
-    __threadfence_system();
-    st_release_sys(c.flags(owner, op) + region * kCommMaxWorld + me, epoch);
+// Tagged-word store of four bf16 (columns col..col+3, col a multiple of 4) at
+// element offset `e` (a multiple of 4) of a tagged array: two 8-byte words, each
+// single-copy atomic, each carrying its own tag.
+__device__ __forceinline__ void tag_put4(uint64_t* words, int64_t e, const bf16 v[4],
+                                         uint32_t epoch) {
+  uint32_t lo, hi;
+  memcpy(&lo, v, 4);
+  memcpy(&hi, v + 2, 4);
+  const uint64_t w0 = (static_cast<uint64_t>(epoch) << 32) | lo;
+  const uint64_t w1 = (static_cast<uint64_t>(epoch) << 32) | hi;
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(words + e / 2), "l"(w0),
+               "l"(w1)
+               : "memory");
+}
+
+// Bounded poll until both words of four bf16 carry `epoch`; false (and the timeout bit)
+// if they never do.
+__device__ __forceinline__ bool tag_get4(const uint64_t* words, int64_t e, uint32_t epoch,
+                                         float f[4], int* err) {
+  const uint64_t* p = words + e / 2;
+  uint64_t w0, w1;
+  long long t0 = 0;
+  bool waited = false;
+  while (true) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p)
+                 : "memory");
+    if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch) break;
+    if (!waited) {
+      waited = true;
+      t0 = clock64();
+    } else if (clock64() - t0 > kCommTimeoutCycles) {
+      if (err) atomicOr(err, LSB_DEVERR_TIMEOUT);
+      return false;
+    }
   }
+  const uint32_t lo = static_cast<uint32_t>(w0), hi = static_cast<uint32_t>(w1);
+  bf16 h[4];
+  memcpy(h, &lo, 4);
+  memcpy(h + 2, &hi, 4);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) f[k] = __bfloat162float(h[k]);
+  return true;
+}
+
+// Second half of the all-reduce for one region (rows [r0, r1) x columns [c0, c0 + w)
+// of an output with `ncols` columns, a multiple of 4, and row stride `ld`), after this
+// CTA has stored its partial of the region as tagged words into the owner's recv slot
+// (element (m, col) at m * ncols + col). Run by `nthreads` threads (index t).
+__device__ __forceinline__ void comm_complete(const CommDev& c, int owner, uint32_t epoch,
+                                              bf16* out, int64_t ld, int r0, int r1, int c0,
+                                              int w, int ncols, int t, int nthreads, int* err) {
+  const int me = c.rank, W = c.world;
   const int quads = (w + 3) >> 2;
   const int count = (r1 - r0) * quads;
-  if (me == owner) {
-    if (t == 0)
-      for (int s = 0; s < W; ++s)
-        comm_wait(c.flags(me, op) + region * kCommMaxWorld + s, epoch, err);
-    sync();
-    for (int idx = t; idx < count; idx += nthreads) {
-      const int m = r0 + idx / quads;
-      const int col = c0 + 4 * (idx % quads);
+  for (int idx = t; idx < count; idx += nthreads) {
+    const int m = r0 + idx / quads;
+    const int col = c0 + 4 * (idx % quads);
+    const int64_t e = static_cast<int64_t>(m) * ncols + col;
+    bf16 v[4];
+    if (me == owner) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int s = 0; s < W; ++s) {  // rank order: every rank gets the same bits
-        float f[4];
-        get4(c.recv(me, s) + m * rs, col, ncols, f);
+        float f[4] = {0.f, 0.f, 0.f, 0.f};
+        tag_get4(c.recv(me, s), e, epoch, f, err);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] += f[e];
+        for (int k = 0; k < 4; ++k) acc[k] += f[k];
       }
-      bf16 v[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(acc[e]);
-      put4(out + m * ld, col, ncols, v);
+      for (int k = 0; k < 4; ++k) v[k] = __float2bfloat16_rn(acc[k]);
       for (int r = 0; r < W; ++r)
-        if (r != me) put4(c.result(r) + m * rs, col, ncols, v);
-    }
-    sync();
-    if (t == 0) {
-      __threadfence_system();
-      for (int r = 0; r < W; ++r)
-        if (r != me) st_release_sys(c.done(r, op) + region, epoch);
-    }
-  } else {
-    if (t == 0) comm_wait(c.done(me, op) + region, epoch, err);
-    sync();
-    for (int idx = t; idx < count; idx += nthreads) {
-      const int m = r0 + idx / quads;
-      const int col = c0 + 4 * (idx % quads);
-      float f[4];
-      get4(c.result(me) + m * rs, col, ncols, f);
-      bf16 v[4];
+        if (r != me) tag_put4(c.result(r), e, v, epoch);
+    } else {
+      float f[4] = {0.f, 0.f, 0.f, 0.f};
+      tag_get4(c.result(me), e, epoch, f, err);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(f[e]);
-      put4(out + m * ld, col, ncols, v);
+      for (int k = 0; k < 4; ++k) v[k] = __float2bfloat16_rn(f[k]);
     }
+    put4(out + m * ld, col, ncols, v);
   }
 }
 

@@ -317,6 +317,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     const int count = te > tb ? (te - tb) << kQuadShift : 0;
     const uint32_t red_addr = smem_u32(red);
+    uint32_t ar_epoch = 0;  // this call's all-reduce epoch (AR variants)
+    if (AR) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      ar_epoch = comm_epoch(p.comm, kOpGemmAllReduce);
+    }
     // kU quads per thread and pass: with every split's loads of all of them issued
     // before the sums, kU x S distributed-shared-memory loads are in flight.
     constexpr int kU = kSwiglu ? 1 : 2;
@@ -393,11 +398,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         if (AR) {
           // this rank's partial (rounded to bf16, as the reference's local GEMM output)
-          // goes to the tile owner's recv slot, rows of N elements
+          // goes to the tile owner's recv slot as tagged words, rows of N elements
           const bf16 v4[4] = {__float2bfloat16_rn(o0), __float2bfloat16_rn(o1),
                               __float2bfloat16_rn(o2), __float2bfloat16_rn(o3)};
-          put4(p.comm.recv(tile_n % p.comm.world, p.comm.rank) +
-                   static_cast<int64_t>(m0 + m) * p.N, col, ncols, v4);
+          tag_put4(p.comm.recv(tile_n % p.comm.world, p.comm.rank),
+                   static_cast<int64_t>(m0 + m) * p.N + col, v4, ar_epoch);
         } else {
           store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
         }
@@ -418,16 +423,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       te = tb + per < tokens ? tb + per : tokens;
       if (te < tb) te = tb;
     }
-    uint32_t epoch = 0;
-    if (t == 0) {
-      asm volatile("griddepcontrol.wait;" ::: "memory");
-      epoch = comm_epoch(p.comm, kOpGemmAllReduce);
-    }
-    const int region = blockIdx.x + blockIdx.y * gridDim.x;
+    const uint32_t epoch = comm_epoch(p.comm, kOpGemmAllReduce);
     const int w = p.N - n0 < kBM ? p.N - n0 : kBM;
-    comm_complete(p.comm, kOpGemmAllReduce, region, tile_n % p.comm.world, epoch, p.y, p.ldy,
-                  m0 + tb, m0 + te, n0, w, p.N, p.N, t, 128, [] { epi_barrier(); },
-                  p.error_flag);
+    comm_complete(p.comm, tile_n % p.comm.world, epoch, p.y, p.ldy, m0 + tb, m0 + te, n0, w,
+                  p.N, t, 128, p.error_flag);
     epi_barrier();
     if (t == 0) comm_finish(p.comm, kOpGemmAllReduce, epoch, gridDim.x * gridDim.y);
   }
@@ -742,7 +741,7 @@ extern "C" int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const vo
   LSB_REQUIRE(comm && y && x, "gemm_allreduce: null pointer");
   LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_BIAS,
               "gemm_allreduce: epilogue must be LSB_EPI_NONE or LSB_EPI_BIAS");
-  LSB_REQUIRE(M >= 0 && N > 0, "gemm_allreduce: bad shape");
+  LSB_REQUIRE(M >= 0 && N > 0 && N % 4 == 0, "gemm_allreduce: N must be a multiple of 4");
   if (comm->dev.world == 1)
     return gemm_impl(y, ldy, x, ldx, w, ldw, bias, M, N, K, epilogue, nullptr, stream);
   const int sms = num_sms();

@@ -8,6 +8,8 @@ CUDA events on the capturing stream after warm-up replays.
 
     python loop-sglang_b200/kernel_bench.py attention --rows 143 --ctx 1448
     python loop-sglang_b200/kernel_bench.py gemm --tokens 143 --shape qkv o gate_up down
+    python -m torch.distributed.run --nproc-per-node 2 loop-sglang_b200/kernel_bench.py \
+        gemm_ar --tokens 256     # row-parallel GEMM fused with its all-reduce, per rank
 
 It is also the small case for profiler captures of one kernel (one KV layer of a
 few GB instead of the whole pool that the decode benchmark holds).
@@ -118,10 +120,18 @@ def bench_attention(args, ops) -> dict:
             "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}
 
 
+def tp_shape(name: str, tp: int) -> tuple[int, int, bool]:
+    """Per-rank GEMM shape under the reference's tensor-parallel split."""
+    n, k, swiglu = OURO_GEMMS[name]
+    if name in ("qkv", "gate_up", "lm_head"):
+        return n // tp, k, swiglu  # column-parallel: output rows split
+    return n, k // tp, swiglu  # row-parallel: reduction split
+
+
 def bench_gemm(args, ops, name: str) -> dict:
     """One ``y = x . w^T`` launch with the weight streamed from HBM (rotating copies)."""
-    dev = torch.device("cuda", 0)
-    n, k, swiglu = OURO_GEMMS[name]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n, k, swiglu = tp_shape(name, args.tp)
     m = args.tokens
     w_bytes = n * k * 2
     copies = max(2, math.ceil(2 * L2_BYTES / w_bytes))
@@ -137,9 +147,41 @@ def bench_gemm(args, ops, name: str) -> dict:
     us = _time_graph(launch, args.reps)
     nbytes = w_bytes + m * k * 2 + m * cols * 2
     flops = 2.0 * m * n * k
-    return {"kernel": "gemm", "shape": name, "tokens": m, "N": n, "K": k, "swiglu": swiglu,
+    return {"kernel": "gemm", "shape": name, "tp": args.tp, "tokens": m, "N": n, "K": k,
+            "swiglu": swiglu,
             "weight_copies": copies, "algorithmic_bytes": nbytes, "us": round(us, 2),
             "GBps": round(nbytes / us / 1e3, 1), "TFLOPs": round(flops / us / 1e6, 1)}
+
+
+def bench_gemm_ar(args, ops, comm, name: str) -> dict:
+    """One row-parallel shard GEMM fused with its NVLink all-reduce (every rank runs it),
+    next to the same local GEMM alone; the max over ranks of the per-launch time."""
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tp = comm.world
+    n, k, _ = tp_shape(name, tp)
+    m = args.tokens
+    w_bytes = n * k * 2
+    copies = max(2, math.ceil(2 * L2_BYTES / w_bytes))
+    ws = [torch.randn(n, k, dtype=torch.bfloat16, device=dev).mul_(0.02) for _ in range(copies)]
+    x = torch.randn(m, k, dtype=torch.bfloat16, device=dev)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    dist.barrier()
+    us_ar = _time_graph(lambda i: comm.gemm_allreduce(x, ws[i % copies], out=y), args.reps)
+    dist.barrier()
+    us_local = _time_graph(lambda i: ops.gemm(x, ws[i % copies], out=y), args.reps)
+    dist.barrier()
+    us_allreduce = _time_graph(lambda i: comm.all_reduce(y), args.reps)
+    t = torch.tensor([us_ar, us_local, us_allreduce], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us_ar, us_local, us_allreduce = float(t[0]), float(t[1]), float(t[2])
+    link = 2 * (tp - 1) / tp * m * n * 2  # bytes each rank sends: partials + sums
+    return {"kernel": "gemm_allreduce", "shape": name, "tp": tp, "tokens": m, "N": n, "K": k,
+            "us": round(us_ar, 2), "us_local_gemm": round(us_local, 2),
+            "us_allreduce_alone": round(us_allreduce, 2),
+            "weight_GBps": round(w_bytes / us_ar / 1e3, 1),
+            "nvlink_bytes": int(link), "nvlink_GBps": round(link / us_ar / 1e3, 1)}
 
 
 def main(argv=None) -> None:
@@ -161,12 +203,35 @@ def main(argv=None) -> None:
     gm.add_argument("--shape", nargs="+", default=["qkv", "o", "gate_up", "down"],
                     choices=sorted(OURO_GEMMS))
     gm.add_argument("--reps", type=int, default=60)
+    gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
+    ga = sub.add_parser("gemm_ar")
+    ga.add_argument("--tokens", type=int, default=256)
+    ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
+    ga.add_argument("--reps", type=int, default=60)
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("kernel_bench needs a CUDA device")
     _package()
     import importlib
     ops = importlib.import_module("loop_sglang_b200.ops")
+    if args.kernel == "gemm_ar":
+        import datetime
+        import os
+
+        import torch.distributed as dist
+
+        C = importlib.import_module("loop_sglang_b200.comm")
+        rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        comm = C.B200Communicator(rank, world, args.tokens * 8192)
+        for name in args.shape:
+            line = bench_gemm_ar(args, ops, comm, name)
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+        comm.close()
+        dist.destroy_process_group()
+        return
     torch.cuda.set_device(0)
     if args.kernel == "attention":
         print(json.dumps(bench_attention(args, ops)), flush=True)
