@@ -251,8 +251,10 @@ int lsb_last_exited_resolve(int32_t* physical_table, int64_t pt_group_stride, in
  * token t pops fixed_groups + d_t * core_groups slots (d_t = steps, or
  * restore_depths[t] when not NULL) and depths it did not compute alias the
  * last computed version. slot_map [fixed + steps*core, width] int32,
- * completed_depth [width], free_slots stack, free_count [1] (device).
- * Replaces kvcache/last_exited.py:15-47 and :181-202, :269-290. */
+ * completed_depth [width], free_slots stack, free_count [1] (device). A
+ * negative handle reserves nothing (rows of a fixed-shape batch that have
+ * nothing to reserve). Replaces kvcache/last_exited.py:15-47 and :181-202,
+ * :269-290. */
 int lsb_last_exited_reserve(int32_t* slot_map, int32_t* completed_depth, int64_t width,
                             int32_t* free_slots, int32_t* free_count, const int32_t* handles,
                             const int32_t* restore_depths, int64_t n, int32_t steps,
@@ -261,8 +263,8 @@ int lsb_last_exited_reserve(int32_t* slot_map, int32_t* completed_depth, int64_t
 /* Release versions back to the stack in handle order (the reference's
  * _release_versions): with exits (alias) the versions at depths >= exits[t]
  * are freed and alias the final computed version; with exits == NULL every
- * version of the token is freed.  Replaces kvcache/last_exited.py:50-84,
- * :204-248. */
+ * version of the token is freed; a negative handle releases nothing.
+ * Replaces kvcache/last_exited.py:50-84, :204-248. */
 int lsb_last_exited_release(int32_t* slot_map, int32_t* completed_depth, int64_t width,
                             int32_t* free_slots, int32_t* free_count, const int32_t* handles,
                             const int32_t* exits, int64_t n, int32_t steps, int32_t fixed_groups,
@@ -292,6 +294,36 @@ int lsb_set_metadata(int32_t* cache_seqlens, int32_t* cu_seqlens_k, int32_t* cu_
                      const int32_t* seq_lens, const int32_t* extend_lens, int64_t bs,
                      int64_t max_seq_pages, int32_t page_size, int32_t seq_len_delta,
                      int32_t is_decode, void* stream);
+
+/* ------------------------------------------- device-side CDB routing -------
+ * One core step of continuous-depth batching routed on the device
+ * (CDBScheduler._run_core / _consume_gate / _run_coda, managers/cdb_scheduler.py:
+ * 189-267, with disable_lookahead_exit timing), so a decode iteration needs no
+ * host round trip. Per row r, after the step at depth[r]: d = depth[r] + 1; the
+ * row exits when d >= max_depth or its gate fired (signal[r] != 0) -- or, when
+ * replay_depths [rows, out_stride] is given, when d reaches the prescribed exit
+ * depth of its next output (the reference's replay_exit_depths). An exiting row
+ * takes its greedy token sampled[r] (or forced_ids[r, k] when given: teacher
+ * forcing) as the next input, records sampled[r] and d in out_tokens / out_depths
+ * [rows, out_stride] at k = out_count[r] (optional), advances seq_lens[r] and sets
+ * depth[r] = 0; alias_handle[r] /
+ * alias_depth[r] then name its KV versions to alias (else -1) and reserve_handle[r]
+ * the successor position to reserve (else -1), ready for lsb_last_exited_release /
+ * lsb_last_exited_reserve, which skip negative handles. *produced (optional)
+ * counts the outputs. No counterpart kernel in the reference (host logic there). */
+int lsb_cdb_route(int32_t* depth, int32_t* seq_lens, int32_t* ids, const int32_t* sampled,
+                  const uint8_t* signal, const int32_t* replay_depths, const int32_t* forced_ids,
+                  int64_t out_stride, int32_t* out_count, int32_t* out_tokens, int32_t* out_depths,
+                  int32_t* alias_handle, int32_t* alias_depth, int32_t* reserve_handle,
+                  uint8_t* exited, const int32_t* req_to_token, int64_t r2t_stride,
+                  const int32_t* req_pool_indices, int64_t rows, int32_t max_depth,
+                  int32_t max_seq_len, int32_t* produced, void* stream);
+
+/* Re-admission of the rows that exited: hidden[slots[r]] = emb[r] (the successor's
+ * prelude output) and exit_state[slots[r]] = 0 (optional) where exited[r]; the
+ * prelude phase's state writes (cdb_model_runner.py:84-91). */
+int lsb_cdb_admit(void* hidden, int64_t ld, float* exit_state, const int64_t* slots,
+                  const uint8_t* exited, const void* emb, int64_t rows, int64_t dim, void* stream);
 
 /* ------------------------------------------------- TP communicator --------
  * Tensor parallelism over the GPUs of one node, one process per GPU, without

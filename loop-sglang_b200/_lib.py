@@ -69,6 +69,9 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                         P]),
     "lsb_last_exited_reserve": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
     "lsb_last_exited_release": (ctypes.c_int, [P, P, I64, P, P, P, P, I64, I32, I32, I32, P]),
+    "lsb_cdb_route": (ctypes.c_int, [P, P, P, P, P, P, P, I64, P, P, P, P, P, P, P, P, I64, P, I64,
+                                     I32, I32, P, P]),
+    "lsb_cdb_admit": (ctypes.c_int, [P, I64, P, P, P, P, I64, I64, P]),
     "lsb_comm_buffer_bytes": (c_int64, [I64]),
     "lsb_comm_alloc": (ctypes.c_int, [I64, P]),
     "lsb_comm_free": (ctypes.c_int, [P]),

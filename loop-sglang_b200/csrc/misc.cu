@@ -3,6 +3,8 @@
 // last-exited address resolution.
 #include "common.cuh"
 
+extern int* lsb_device_error_flag();
+
 namespace lsb {
 namespace {
 
@@ -290,12 +292,12 @@ __global__ void __launch_bounds__(kScanThreads)
   const int total = fixed + steps * core;
   for (int64_t c0 = 0; c0 < n; c0 += kScanThreads) {
     const int64_t t = c0 + threadIdx.x;
-    const int depth = t < n ? (restore ? restore[t] : steps) : 0;
-    const int cnt = t < n ? fixed + depth * core : 0;
+    const int64_t h = t < n ? handles[t] : -1;  // a negative handle reserves nothing
+    const int depth = h >= 0 ? (restore ? restore[t] : steps) : 0;
+    const int cnt = h >= 0 ? fixed + depth * core : 0;
     const int incl = block_inclusive_scan(cnt, warp_tot);
-    if (t < n && base - incl >= 0) {  // the host keeps the pool from running dry
+    if (h >= 0 && base - incl >= 0) {  // the host keeps the pool from running dry
       const int start = base - incl;
-      const int64_t h = handles[t];
       for (int slot = 0; slot < total; ++slot) {
         int src = slot;
         if (slot >= fixed) {
@@ -327,10 +329,9 @@ __global__ void __launch_bounds__(kScanThreads)
   const int total = fixed + steps * core;
   for (int64_t c0 = 0; c0 < n; c0 += kScanThreads) {
     const int64_t t = c0 + threadIdx.x;
-    int64_t h = 0;
+    int64_t h = t < n ? handles[t] : -1;  // a negative handle releases nothing
     int depth = 0, begin = 0, end = 0;
-    if (t < n) {
-      h = handles[t];
+    if (h >= 0) {
       const int old_depth = depths[h];
       depth = alias ? exits[t] : 0;
       end = fixed + old_depth * core;
@@ -338,7 +339,7 @@ __global__ void __launch_bounds__(kScanThreads)
     }
     const int cnt = end > begin ? end - begin : 0;
     const int incl = block_inclusive_scan(cnt, warp_tot);
-    if (t < n) {
+    if (h >= 0) {
       const int start = base + incl - cnt;
       for (int slot = begin; slot < end; ++slot) stack[start + slot - begin] = vmap[slot * width + h];
       if (alias) {
@@ -389,6 +390,138 @@ extern "C" int lsb_last_exited_release(int32_t* slot_map, int32_t* completed_dep
       slot_map, completed_depth, width, free_slots, free_count, handles, exits, n, steps,
       fixed_groups, core_groups);
   return check_launch("lsb_last_exited_release");
+}
+
+// ---------------------------------------------------------------------------
+// Device-side continuous-depth batching: the exit routing of one core step and the
+// re-admission of exited rows, with no host round trip.
+// ---------------------------------------------------------------------------
+namespace lsb {
+namespace {
+
+struct CdbRoute {
+  int32_t* depth;
+  int32_t* seq_lens;
+  int32_t* ids;
+  const int32_t* sampled;
+  const uint8_t* signal;
+  const int32_t* replay_depths;
+  const int32_t* forced_ids;
+  int64_t out_stride;
+  int32_t* out_count;
+  int32_t* out_tokens;
+  int32_t* out_depths;
+  int32_t* alias_handle;
+  int32_t* alias_depth;
+  int32_t* reserve_handle;
+  uint8_t* exited;
+  const int32_t* req_to_token;
+  int64_t r2t_stride;
+  const int32_t* rpi;
+  int64_t rows;
+  int32_t max_depth, max_seq_len;
+  int32_t* produced;
+  int* error_flag;
+};
+
+// One thread per row. A row that just ran loop step depth[r] exits when it reached
+// full depth, or its gate fired (or, replaying, it reached its prescribed depth):
+// its greedy token becomes the next input, its KV versions are aliased at the exit
+// depth, the successor position gets fresh versions and the row restarts at depth 0.
+__global__ void cdb_route_kernel(CdbRoute a) {
+  const int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (r >= a.rows) return;
+  const int d1 = a.depth[r] + 1;
+  const int k = a.out_count[r];
+  const bool in_range = k < a.out_stride;
+  bool fire;
+  if (a.replay_depths) fire = in_range && d1 >= a.replay_depths[r * a.out_stride + k];
+  else fire = a.signal != nullptr && a.signal[r] != 0;
+  const bool ex = d1 >= a.max_depth || fire;
+  const int32_t* row = a.req_to_token + static_cast<int64_t>(a.rpi[r]) * a.r2t_stride;
+  const int seq = a.seq_lens[r];
+  a.exited[r] = ex ? 1 : 0;
+  if (!ex) {
+    a.depth[r] = d1;
+    a.alias_handle[r] = -1;
+    a.reserve_handle[r] = -1;
+    return;
+  }
+  const int32_t tok = (a.forced_ids && in_range) ? a.forced_ids[r * a.out_stride + k] : a.sampled[r];
+  a.alias_handle[r] = row[seq - 1];
+  a.alias_depth[r] = d1;
+  if (in_range) {
+    if (a.out_tokens) a.out_tokens[r * a.out_stride + k] = a.sampled[r];
+    if (a.out_depths) a.out_depths[r * a.out_stride + k] = d1;
+  }
+  a.out_count[r] = k + 1;
+  a.ids[r] = tok;
+  a.depth[r] = 0;
+  if (a.produced) atomicAdd(a.produced, 1);
+  if (seq < a.max_seq_len) {
+    a.seq_lens[r] = seq + 1;
+    a.reserve_handle[r] = row[seq];
+  } else {  // the request table has no room for another token: stay, flagged
+    a.reserve_handle[r] = -1;
+    if (a.error_flag) atomicOr(a.error_flag, LSB_DEVERR_SEQLEN);
+  }
+}
+
+// One CTA per row: an exited row's state slot takes the successor token's prelude
+// output (the embedding) and a zero exit state.
+__global__ void cdb_admit_kernel(bf16* __restrict__ hidden, int64_t ld, float* __restrict__ exit_state,
+                                 const int64_t* __restrict__ slots, const uint8_t* __restrict__ exited,
+                                 const bf16* __restrict__ emb, int64_t dim) {
+  const int64_t r = blockIdx.x;
+  if (!exited[r]) return;
+  const int64_t slot = slots[r];
+  const bf16x8* s = reinterpret_cast<const bf16x8*>(emb + r * dim);
+  bf16x8* d = reinterpret_cast<bf16x8*>(hidden + slot * ld);
+  for (int64_t j = threadIdx.x; j < dim / 8; j += blockDim.x) d[j] = s[j];
+  if (exit_state && threadIdx.x == 0) exit_state[slot] = 0.f;
+}
+
+}  // namespace
+}  // namespace lsb
+
+extern "C" int lsb_cdb_route(int32_t* depth, int32_t* seq_lens, int32_t* ids, const int32_t* sampled,
+                             const uint8_t* signal, const int32_t* replay_depths,
+                             const int32_t* forced_ids, int64_t out_stride, int32_t* out_count,
+                             int32_t* out_tokens, int32_t* out_depths, int32_t* alias_handle,
+                             int32_t* alias_depth, int32_t* reserve_handle, uint8_t* exited,
+                             const int32_t* req_to_token, int64_t r2t_stride,
+                             const int32_t* req_pool_indices, int64_t rows, int32_t max_depth,
+                             int32_t max_seq_len, int32_t* produced, void* stream) {
+  LSB_REQUIRE(depth && seq_lens && ids && sampled && out_count && alias_handle && alias_depth &&
+                  reserve_handle && exited && req_to_token && req_pool_indices,
+              "cdb_route: null pointer");
+  LSB_REQUIRE(signal || replay_depths || max_depth >= 1, "cdb_route: no exit rule");
+  LSB_REQUIRE(max_depth >= 1 && max_seq_len >= 1 && r2t_stride >= max_seq_len,
+              "cdb_route: bad limits");
+  LSB_REQUIRE(!(replay_depths || forced_ids || out_tokens || out_depths) || out_stride > 0,
+              "cdb_route: per-output arrays need out_stride > 0");
+  if (rows <= 0) return LSB_OK;
+  CdbRoute a{depth, seq_lens, ids, sampled, signal, replay_depths, forced_ids, out_stride,
+             out_count, out_tokens, out_depths, alias_handle, alias_depth, reserve_handle, exited,
+             req_to_token, r2t_stride, req_pool_indices, rows, max_depth, max_seq_len, produced,
+             lsb_device_error_flag()};
+  const int threads = 128;
+  cdb_route_kernel<<<static_cast<unsigned>((rows + threads - 1) / threads), threads, 0,
+                     as_stream(stream)>>>(a);
+  return check_launch("lsb_cdb_route");
+}
+
+extern "C" int lsb_cdb_admit(void* hidden, int64_t ld, float* exit_state, const int64_t* slots,
+                             const uint8_t* exited, const void* emb, int64_t rows, int64_t dim,
+                             void* stream) {
+  LSB_REQUIRE(hidden && slots && exited && emb && dim > 0 && dim % 8 == 0 && ld % 8 == 0,
+              "cdb_admit: bad arguments");
+  LSB_REQUIRE(aligned(hidden, 16) && aligned(emb, 16), "cdb_admit: misaligned");
+  if (rows <= 0) return LSB_OK;
+  cdb_admit_kernel<<<static_cast<unsigned>(rows), 128, 0, as_stream(stream)>>>(
+      static_cast<bf16*>(hidden), ld, exit_state, slots, exited, static_cast<const bf16*>(emb),
+      dim);
+  return check_launch("lsb_cdb_admit");
 }
 
 // ---------------------------------------------------------------------------

@@ -360,6 +360,15 @@ class LoopedDecoder:
             inj = self._huginn_layer(self.layers[f"model.prelude.{i}"], inj, i, batch, kv)
         return torch.zeros_like(inj), inj
 
+    def embed_tokens(self, ids: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Ouro's prelude (ouro.py:117): the token embedding, vocab-parallel when sharded
+        (layers/embedding.py:34-43)."""
+        if self.world == 1:
+            return ops.embedding(ids, self.embed, out=out)
+        h = ops.embedding(ids, self.embed, vocab_start=self.vocab_start,
+                          vocab_len=self.vocab_len, out=out)
+        return self.comm.all_reduce(h)
+
     def core_step(self, hidden: torch.Tensor, loop_step, injection, batch: DeviceBatch, kv,
                   out: torch.Tensor | None = None) -> torch.Tensor:
         """One loop step (ouro.py:119-136, huginn.py:162-178); ``hidden`` may be consumed."""

@@ -28,7 +28,7 @@ __all__ = [
     "paged_attention",
     "gemm", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
     "gather_rows", "argmax", "argmax_sharded", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
-    "last_exited_release", "device_error_word", "Workspace", "prepare_batch_inputs",
+    "last_exited_release", "cdb_route", "cdb_admit", "device_error_word", "Workspace", "prepare_batch_inputs",
     "set_metadata",
     "LSB_EPI_NONE", "LSB_EPI_BIAS", "LSB_EPI_BIAS_AFTER_ROUND", "LSB_EPI_SWIGLU",
 ]
@@ -361,6 +361,32 @@ def last_exited_release(slot_map, completed, free_slots, free_count, handles, st
          free_slots.data_ptr(), free_count.data_ptr(), handles.data_ptr(), _p(exits),
          handles.numel(), steps, fixed, core, _stream())
 
+
+
+def cdb_route(depth, seq_lens, ids, sampled, signal, out_count, alias_handle, alias_depth,
+              reserve_handle, exited, req_to_token, req_pool_indices, max_depth: int,
+              max_seq_len: int, replay_depths=None, forced_ids=None, out_tokens=None,
+              out_depths=None, produced=None) -> None:
+    """Device-side exit routing of one CDB core step (cdb_scheduler.py:189-267); see
+    ``lsb_cdb_route``. Per-output arrays are ``[rows, out_stride]`` int32."""
+    outs = [t for t in (replay_depths, forced_ids, out_tokens, out_depths) if t is not None]
+    stride = outs[0].shape[1] if outs else 0
+    if any(t.shape[1] != stride or t.stride(1) != 1 or t.stride(0) != stride for t in outs):
+        raise ValueError("cdb_route: per-output arrays must share one contiguous [rows, n] shape")
+    call("lsb_cdb_route", depth.data_ptr(), seq_lens.data_ptr(), ids.data_ptr(), sampled.data_ptr(),
+         _p(signal), _p(replay_depths), _p(forced_ids), stride, out_count.data_ptr(),
+         _p(out_tokens), _p(out_depths), alias_handle.data_ptr(), alias_depth.data_ptr(),
+         reserve_handle.data_ptr(), exited.data_ptr(), req_to_token.data_ptr(),
+         req_to_token.stride(0), req_pool_indices.data_ptr(), depth.numel(), max_depth,
+         max_seq_len, _p(produced), _stream())
+
+
+def cdb_admit(hidden: torch.Tensor, exit_state: torch.Tensor | None, slots: torch.Tensor,
+              exited: torch.Tensor, emb: torch.Tensor) -> None:
+    """Exited rows take their successor's prelude state (cdb_model_runner.py:84-91)."""
+    _need(slots, torch.int64, "slots")
+    call("lsb_cdb_admit", hidden.data_ptr(), hidden.stride(0), _p(exit_state), slots.data_ptr(),
+         exited.data_ptr(), emb.data_ptr(), slots.numel(), hidden.shape[1], _stream())
 
 
 # -------------------------------------------------------- batch metadata --
