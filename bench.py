@@ -1,27 +1,32 @@
 """Decode throughput of the looped-decoder hot path on B200 (one JSON line on stdout).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload cdb|cb]
 
-Workload: Ouro-1.4B architecture (24 shared layers x 4 loop
-steps, hidden 2048, 16 MHA heads x 128, SwiGLU 5632, vocab 49152), random-init bf16,
-full-depth CB decode, depth-indexed KV with 16-token pages, TP=1. 256 requests with
-uniform-random prompt lengths in [512, 2048] and 256 output tokens; the requests
-are admitted in order while their full length fits the KV pool (768 KiB per token:
-the running batch is capacity-limited) and every admitted request decodes from the
-middle of its generation (prompt + 128). A step is one decode step of the running
-batch: batch metadata, embedding, 4 x 24 layers, LM head and greedy sampling, all
-from this repository's kernels, replayed as one CUDA graph. KV contents and token
-ids are synthetic (seeded random), as are the weights.
+Default workload (the metric's): Ouro-1.4B architecture (24 shared
+layers x 4 loop steps, hidden 2048, 16 MHA heads x 128, SwiGLU 5632, vocab 49152),
+random-init bf16, early exit under continuous-depth batching (CDB) with the last-exited
+KV policy and exit threshold 0.2. 512 requests with uniform-random prompt lengths in
+[256, 1024] and 512 outputs; the running batch is capacity-limited (version slots of
+192 KiB) and decodes from the middle of its generation. Exit steps are prescribed per
+output token at 15/25/30/30% for loop steps 1-4 (the reference's replay depths; the
+gate is still evaluated every step). A step is one core step of every running row at
+its own depth plus the device-side routing: exit decisions, greedy sampling of the rows
+that exit, KV version alias/reserve and the successors' prelude, all from this
+repository's kernels, replayed as one CUDA graph; ``value`` = output tokens / time.
 
-``value`` times K device-resident steps; ``e2e`` times K steps through the public
-per-step call with host buffers (H2D of the scheduler inputs, D2H of the tokens).
-``--impl reference`` times the CPU oracle restatement of the same decode step
-(the reference's own code path restated on the host cores) on a bounded sample.
-With N > 1 (torchrun, one process per GPU) the model runs tensor-parallel over the
-N GPUs (the reference's TP split; o_proj and down_proj fused with their NVLink
-all-reduce): every rank holds 1/N of the weights and KV heads, so the KV pool
-admits more of the 256 requests and the whole job's tokens per second is the
-running batch's (strong scaling on the fixed 256-request workload).
+``--workload cb``: full-depth CB decode with depth-indexed KV and
+16-token pages, 256 requests with prompts U[512, 2048] + 256 outputs; a step is one
+decode step of the running batch (4 x 24 layers, LM head, sampling).
+
+KV contents and token ids are synthetic (seeded random), as are the weights. ``value``
+times K device-resident steps; ``e2e`` times K steps through the host (H2D of the
+step's scheduler inputs, D2H of its outputs). ``--impl reference`` times the CPU oracle
+restatement of the same work on a bounded sample. With N > 1 (torchrun, one process per
+GPU) the model runs tensor-parallel over the N GPUs (the reference's TP split; o_proj
+and down_proj fused with their NVLink all-reduce): every rank holds 1/N of the weights
+and KV heads, so the KV pool admits more requests (strong scaling on the fixed
+workload).
 """
 
 from __future__ import annotations
@@ -206,14 +211,19 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    base = cpu_decode_sample(max(1, args.steps), args.cpu_batch, threads)
+    if args.workload == "cdb":
+        base = cpu_cdb_sample(max(1, args.steps), args.cpu_batch, threads)
+        metric, workload = CDB_METRIC, CDB_WORKLOAD
+    else:
+        base = cpu_decode_sample(max(1, args.steps), args.cpu_batch, threads)
+        metric, workload = METRIC, WORKLOAD
     line = {
-        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "tok/s",
+        "impl": "reference", "metric": metric, "value": base["value"], "unit": "tok/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * base["p50_step_s"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random weights, KV and token ids)",
-        "config": {"workload": WORKLOAD, "sample_batch": args.cpu_batch},
+        "config": {"workload": workload, "sample_batch": args.cpu_batch},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -422,6 +432,281 @@ def run_b200(args) -> None:
     _ = _lib
 
 
+# ------------------------------------------------------- CDB workload --
+# Ouro-1.4B with early exit under continuous-depth batching, exit
+# threshold 0.2, last-exited KV; 512 requests, prompt U[256, 1024], 512 outputs. The exit
+# steps follow 15/25/30/30% at loop steps 1-4, prescribed per output token (the reference's
+# replay_exit_depths, cdb_scheduler.py:207-213) -- the gate is still evaluated every step.
+CDB_NUM_REQS = 512
+CDB_PROMPT_RANGE = (256, 1024)
+CDB_OUT_TOKENS = 512
+CDB_MID = 256
+CDB_EXIT_P = (0.15, 0.25, 0.30, 0.30)
+CDB_METRIC = ("decode output tok/s, Ouro-1.4B CDB (configs[2]), last-exited KV, TP over the "
+              "job's GPUs")
+CDB_WORKLOAD = ("configs[2]: Ouro-1.4B random-init bf16, continuous-depth batching with the "
+                "routing on the device, last-exited KV, exit threshold 0.2, exit steps "
+                "prescribed 15/25/30/30% at loop steps 1-4 (replay depths), 512 requests with "
+                "prompt U[256,1024] + 512 outputs, capacity-limited running batch decoding "
+                "from prompt+256")
+
+
+def cdb_depths(n: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return rng.choice(np.arange(1, 5), size=n, p=CDB_EXIT_P).astype(np.int32)
+
+
+def cpu_cdb_sample(tokens: int, batch: int, threads: int) -> dict:
+    """The oracle on a bounded CDB sample: ``batch`` requests at mean context, each output
+    token = prelude, its prescribed number of loop steps, LM head (shared-KV addressing;
+    the per-token arithmetic is the last-exited policy's)."""
+    from oracle import model as om
+
+    torch.set_num_threads(threads)
+    cfg = om.LoopedConfig(**{**OURO_14B, "exit_threshold": 0.2})
+    t0 = time.perf_counter()
+    w = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
+    mdl = om.LoopedModel(cfg, w, "shared")
+    rng = np.random.default_rng(SEED)
+    ctx = rng.integers(CDB_PROMPT_RANGE[0], CDB_PROMPT_RANGE[1] + 1, batch) + CDB_MID
+    pages_per = [(int(c) + tokens + PAGE) // PAGE for c in ctx]
+    num_pages = sum(pages_per) + 1
+    pool = om.PagedKVPool(mdl.num_kv_layers, num_pages, PAGE, cfg.kv_heads, cfg.head_dim,
+                          torch.bfloat16)
+    pool.buf.normal_(generator=torch.Generator().manual_seed(1))
+    table = torch.zeros(batch, max(pages_per), dtype=torch.int32)
+    nxt = 1
+    for b, n in enumerate(pages_per):
+        table[b, :n] = torch.arange(nxt, nxt + n, dtype=torch.int32)
+        nxt += n
+    setup = time.perf_counter() - t0
+    depths = cdb_depths(batch * tokens, SEED + 7).reshape(batch, tokens)
+    ids = torch.randint(0, cfg.vocab, (batch,), generator=torch.Generator().manual_seed(2),
+                        dtype=torch.int32)
+    t = time.perf_counter()
+    steps = 0
+    for k in range(tokens):
+        for b in range(batch):
+            pos = torch.tensor([int(ctx[b]) + k], dtype=torch.int32)
+            loc = table[b, pos.long() // PAGE] * PAGE + pos % PAGE
+            bt = om.Batch(ids[b:b + 1], pos, loc.to(torch.int32), table[b:b + 1], pos + 1,
+                          torch.arange(2, dtype=torch.int32), False)
+            h, _ = mdl.forward_prelude(bt, pool)
+            for step in range(int(depths[b, k])):
+                h = mdl.core_step(h, step, None, bt, pool)
+                steps += 1
+            ids[b] = mdl.lm_head(h, None).float().argmax(-1).to(torch.int32)[0]
+    total = time.perf_counter() - t
+    return {"value": batch * tokens / total, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"{batch} requests at context {int(ctx.mean())} (mean), {tokens} output "
+                       f"tokens each ({steps} loop steps at the prescribed exit depths) of "
+                       f"Ouro-1.4B through the CPU oracle in torch bf16/fp32, {threads} "
+                       f"threads; setup {setup:.0f}s untimed"),
+            "p50_step_s": total / max(1, steps)}
+
+
+def run_b200_cdb(args) -> None:
+    from __graft_entry__ import load_package
+
+    load_package()
+    from loop_sglang_b200 import ops
+    from loop_sglang_b200.comm import B200Communicator
+    from loop_sglang_b200.engine import CDBDecodeEngine
+    from loop_sglang_b200.model import LoopedConfig, LoopedDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = LoopedConfig(**{**OURO_14B, "exit_threshold": 0.2})
+    t0 = time.perf_counter()
+    comm = None
+    if world > 1:
+        vocab_local = -(-cfg.vocab // world)
+        comm = B200Communicator(rank, world, CDB_NUM_REQS * max(cfg.hidden, vocab_local))
+    weights = gpu_weights(cfg, dev, SEED)
+    model = LoopedDecoder(cfg, weights, "last_exited", dev, comm=comm)
+    del weights
+    torch.cuda.empty_cache()
+    rng = np.random.default_rng(SEED)
+    prompts = rng.integers(CDB_PROMPT_RANGE[0], CDB_PROMPT_RANGE[1] + 1, CDB_NUM_REQS)
+    steps_total = args.warmup + args.steps + 1 + (args.steps if not args.no_e2e else 0) + 1
+    ctx = prompts + CDB_MID  # tokens before the one being decoded
+    gen_depth = cdb_depths(CDB_NUM_REQS * CDB_MID, SEED + 1).reshape(CDB_NUM_REQS, CDB_MID)
+    # version slots a request holds: prompt tokens keep every loop step (prefill runs at full
+    # depth), generated ones their exit depth; plus the token being decoded and the steps
+    # to come (at most a fresh full-depth token per step)
+    need = prompts * 4 + gen_depth.sum(1) + 4 * (steps_total + 1)
+    max_len = int(ctx.max()) + steps_total + 2
+    slot_bytes = 2 * cfg.num_core_layers * model.hkv * cfg.head_dim * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    max_slots = int((free - 8 * 2**30) // slot_bytes)
+    if args.batch:
+        bs = args.batch
+    else:
+        fit = np.cumsum(np.maximum(need, max_len)) + 1
+        bs = int(min(np.searchsorted(fit, max_slots, side="right"), CDB_NUM_REQS))
+    num_pages = int(max(np.maximum(need, max_len)[:bs].sum() + 1, bs * max_len + 1))
+    kv = model.make_kv_cache(num_pages, 1, zero=False)
+    kv._kv_buffer.normal_(generator=torch.Generator(device=dev).manual_seed(SEED + 1))
+    kv._kv_buffer[:, :, 0].zero_()
+    handles = (1 + torch.arange(bs, device=dev).view(-1, 1) * max_len
+               + torch.arange(max_len, device=dev)).to(torch.int32)
+    # context versions, request by request (prompt at full depth, outputs at their exit depth)
+    ctx_b = torch.as_tensor(ctx[:bs], device=dev)
+    pos = torch.arange(max_len, device=dev).view(1, -1)
+    live = pos < ctx_b.view(-1, 1)
+    restore = torch.full((bs, max_len), 4, dtype=torch.int32, device=dev)
+    gen = torch.as_tensor(gen_depth[:bs], device=dev)
+    gpos = pos - torch.as_tensor(prompts[:bs], device=dev).view(-1, 1)
+    is_gen = live & (gpos >= 0)
+    restore[is_gen] = gen.gather(1, gpos.clamp(0, CDB_MID - 1))[is_gen].to(torch.int32)
+    ops.last_exited_reserve(kv.slot_map, kv.completed_depth, kv._free_slots, kv._free_count,
+                            handles[live].contiguous(), kv.loop_steps, kv.fixed_groups,
+                            kv.core_groups, restore_depths=restore[live].contiguous())
+    kv.available_slots -= int(restore[live].sum().item()) * kv.core_groups
+    out_cap = steps_total + 8
+    future = torch.as_tensor(cdb_depths(bs * out_cap, SEED + 2).reshape(bs, out_cap),
+                             device=dev).contiguous()
+    eng = CDBDecodeEngine(model, kv, bs, max_len, out_cap, replay_depths=future)
+    ids0 = torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32)
+    eng.start(handles, (ctx_b + 1).to(torch.int32), ids0)
+    eng.capture()
+    setup_s = time.perf_counter() - t0
+    log(f"[bench] rank {rank}: CDB batch {bs}, {num_pages} version slots, setup {setup_s:.1f}s, "
+        f"{eng.launches_per_step} kernels/step")
+    s = eng.stream
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            eng.replay()
+    barrier()
+    p0 = int(eng.produced.item())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(dev) as clocks, torch.cuda.stream(s):
+        ev[0].record(s)
+        for k in range(args.steps):
+            eng.replay()
+            ev[k + 1].record(s)
+        s.synchronize()
+    barrier()
+    produced = int(eng.produced.item()) - p0
+    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    clk = clocks.summary()
+
+    # e2e: each step through the host -- H2D of the running rows (the scheduler's batch),
+    # one step, D2H of which rows exited and their tokens
+    host_rows = torch.arange(1, bs + 1, dtype=torch.int32).pin_memory()
+    host_exit = torch.zeros(bs, dtype=torch.uint8).pin_memory()
+    host_ids = torch.zeros(bs, dtype=torch.int32).pin_memory()
+    e2e_ms, e2e_tokens = 0.0, 0
+    if not args.no_e2e:
+        barrier()
+        p1 = int(eng.produced.item())
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            with torch.cuda.stream(s):
+                eng.rpi.copy_(host_rows, non_blocking=True)
+                eng.replay()
+                host_exit.copy_(eng.exited, non_blocking=True)
+                host_ids.copy_(eng.ids, non_blocking=True)
+            s.synchronize()
+        e1.record(s)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        e2e_tokens = int(eng.produced.item()) - p1
+
+    # roofline of the dominant kernel: layer-0 attention over the rows' current depths
+    seq = eng.cache_seqlens.to(torch.int64)
+    ctx_tokens = int(seq.sum().item())
+    attn_bytes = ctx_tokens * model.hkv * cfg.head_dim * 4 + 2 * bs * model.hq * cfg.head_dim * 2
+    q = torch.randn(bs, model.hq, cfg.head_dim, device=dev).to(torch.bfloat16)
+    kc, vc = kv.slots(0)
+    table = eng.batch.core_page_table[0]
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    with torch.cuda.stream(s):
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_attention(q, kc, vc, table, eng.cache_seqlens, eng.cu_q, 1, max_len,
+                                cfg.head_dim ** -0.5, model.hkv, out=out)
+        a0.record(s)
+        for _ in range(reps):
+            ops.paged_attention(q, kc, vc, table, eng.cache_seqlens, eng.cu_q, 1, max_len,
+                                cfg.head_dim ** -0.5, model.hkv, out=out)
+        a1.record(s)
+        s.synchronize()
+    attn_s = a0.elapsed_time(a1) / 1000.0 / reps
+
+    t_max, e2e_max = total_ms, e2e_ms
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_max, e2e_max = float(t[0]), float(t[1])
+    value = produced / (t_max / 1000.0)
+    weight_bytes = sum(t.numel() * 2 for lw in model.layers.values()
+                       for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) \
+        + model.lm_head_w.numel() * 2
+    kv_bytes = ctx_tokens * cfg.num_core_layers * model.hkv * cfg.head_dim * 4
+    step_bytes = weight_bytes + kv_bytes
+    peak, peak_kind = peaks()
+    achieved = attn_bytes / attn_s / 1e9
+    step_s = t_max / 1000.0 / args.steps
+    line = {
+        "metric": CDB_METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_max / args.steps,
+        "p50_tpot_ms": statistics.median(step_ms) * bs / max(1.0, produced / args.steps),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded random-init weights, random KV contents and token ids",
+        "config": {"workload": CDB_WORKLOAD, "model": "Ouro-1.4B architecture (random init)",
+                   "global_batch": bs, "running_batch_per_gpu": bs,
+                   "mean_context": round(ctx_tokens / bs, 1), "version_slots": num_pages,
+                   "outputs_per_step": round(produced / args.steps, 2),
+                   "step": "one loop step of every running row at its own depth + routing",
+                   "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (each step streams ~%d GB)" % (step_bytes // 10**9)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "paged_attention (layer-0 core step, rows at their own depths)",
+                     "peak_kind": peak_kind,
+                     "step_frac": round(step_bytes / step_s / 1e9 / peak, 4),
+                     "step_bytes": step_bytes},
+        "e2e": ({"value": e2e_tokens / (e2e_max / 1000.0), "unit": "tok/s",
+                 "h2d_bytes_per_step": bs * 4, "d2h_bytes_per_step": bs * 5}
+                if not args.no_e2e else None),
+        "gpu_launches": eng.launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_cdb_sample(args.cpu_steps, args.cpu_batch,
+                                                  os.cpu_count() or 1)
+            line["cpu_baseline"].pop("p50_step_s", None)
+        except Exception as exc:  # reported, never silently dropped
+            line["cpu_baseline"] = {"value": None, "error": repr(exc)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.graph = None
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -432,11 +717,16 @@ def main() -> None:
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--cpu-batch", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--workload", choices=["cdb", "cb"], default="cdb",
+                    help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cdb":
+        run_b200_cdb(args)
     else:
         run_b200(args)
 

@@ -462,18 +462,69 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
           bulk_load(sq + qb * L.q_bytes, p.q + static_cast<int64_t>(row) * p.q_stride,
                     static_cast<uint32_t>(q_copy), &qfull[qb]);
         }
-        int t0 = k_begin;
-        while (ok) {
-          const int ntok = k_end - t0 < T ? (k_end - t0 > 0 ? k_end - t0 : 0) : T;
-          const int s = gs % stages;
-          const uint32_t use = static_cast<uint32_t>(gs / stages);
-          ++gs;
-          if (!mbar_wait(&empty[s], (use & 1u) ^ 1u, p.error_flag)) {
-            ok = false;
-            break;
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      const bool packed = p.slot_stride == static_cast<int64_t>(p.hkv) * D;
+      // Keys whose slots are scattered (one-token pages: the last-exited pool's versions,
+      // or an unpacked pool) go one copy pair per key, issued by one lane per key.
+      const bool scatter = p.page_size < 8 || !packed;
+      int t0 = k_begin;
+      while (ok) {
+        const int ntok = k_end - t0 < T ? (k_end - t0 > 0 ? k_end - t0 : 0) : T;
+        const int s = gs % stages;
+        const uint32_t use = static_cast<uint32_t>(gs / stages);
+        ++gs;
+        int free_ok = 1;
+        if (lane == 0) free_ok = mbar_wait(&empty[s], (use & 1u) ^ 1u, p.error_flag) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, free_ok, 0)) {
+          ok = false;
+          break;
+        }
+        uint8_t* const sk = smem + s * L.stage_bytes;
+        uint8_t* const sv = sk + T * row_bytes;
+        StageHdr h;
+        h.row = row;
+        h.split = split;
+        h.nsplit = nsplit;
+        h.t0 = t0;
+        h.ntok = ntok;
+        h.flags = (t0 == k_begin ? kItemFirst : 0) | (t0 + T >= k_end ? kItemLast : 0);
+        h.qbuf = qb;
+        if (scatter) {
+          int64_t slot[kMaxStageTokens / 32];
+          uint64_t valid = 0;
+#pragma unroll
+          for (int j = 0; j < kMaxStageTokens / 32; ++j) {
+            const int i = lane + 32 * j;
+            bool in = false;
+            slot[j] = 0;
+            if (i < ntok) {
+              const int t = t0 + i;
+              const int pg = pow2 ? (t >> pshift) : t / p.page_size;
+              slot[j] = static_cast<int64_t>(s_pages[pg - p_first]) * p.page_size +
+                        (t - pg * p.page_size);
+              in = slot[j] >= 0 && slot[j] < p.num_slots;
+              if (!in && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+            }
+            valid |= static_cast<uint64_t>(__ballot_sync(0xffffffffu, in)) << (32 * j);
           }
-          uint8_t* const sk = smem + s * L.stage_bytes;
-          uint8_t* const sv = sk + T * row_bytes;
+          if (lane == 0) {  // header, then the arrival carrying every copy's bytes
+            h.valid = valid;
+            hdr[s] = h;
+            mbar_expect_tx(&full[s], static_cast<uint32_t>(__popcll(valid)) * 2u * row_bytes);
+          }
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < kMaxStageTokens / 32; ++j) {
+            const int i = lane + 32 * j;
+            if (i < ntok && ((valid >> i) & 1ull)) {
+              bulk_load(sk + i * row_bytes, p.k_cache + slot[j] * p.slot_stride,
+                        static_cast<uint32_t>(row_bytes), &full[s]);
+              bulk_load(sv + i * row_bytes, p.v_cache + slot[j] * p.slot_stride,
+                        static_cast<uint32_t>(row_bytes), &full[s]);
+            }
+          }
+        } else if (lane == 0) {
           uint64_t valid = 0;
           uint32_t bytes = 0;
           int run_i = 0, run_n = 0;
@@ -486,9 +537,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
             bytes += 2 * nb;
             run_n = 0;
           };
-          const bool packed = p.slot_stride == static_cast<int64_t>(p.hkv) * D;
-          // Page by page: the keys of a page are consecutive slots, one run when the
-          // pool is packed (runs merge across pages that happen to be adjacent).
+          // Page by page: the keys of a page are consecutive slots, one run per page
+          // (runs merge across pages that happen to be adjacent).
           for (int i = 0; i < ntok;) {
             const int t = t0 + i;
             int pg, off;
@@ -508,40 +558,24 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
               continue;
             }
             valid |= (n >= 64 ? ~0ull : ((1ull << n) - 1ull)) << i;
-            if (packed) {
-              if (run_n > 0 && slot0 == run_slot + run_n && i == run_i + run_n) {
-                run_n += n;
-              } else {
-                flush();
-                run_i = i;
-                run_slot = slot0;
-                run_n = n;
-              }
+            if (run_n > 0 && slot0 == run_slot + run_n && i == run_i + run_n) {
+              run_n += n;
             } else {
-              for (int j = 0; j < n; ++j) {
-                flush();
-                run_i = i + j;
-                run_slot = slot0 + j;
-                run_n = 1;
-              }
+              flush();
+              run_i = i;
+              run_slot = slot0;
+              run_n = n;
             }
             i += n;
           }
           flush();
-          StageHdr h;
-          h.row = row;
-          h.split = split;
-          h.nsplit = nsplit;
-          h.t0 = t0;
-          h.ntok = ntok;
-          h.flags = (t0 == k_begin ? kItemFirst : 0) | (t0 + T >= k_end ? kItemLast : 0);
-          h.qbuf = qb;
           h.valid = valid;
           hdr[s] = h;
           mbar_expect_tx(&full[s], bytes);  // the producer's arrival (release) + the copies' bytes
-          t0 += T;
-          if (t0 >= k_end) break;
         }
+        __syncwarp();
+        t0 += T;
+        if (t0 >= k_end) break;
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
