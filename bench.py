@@ -64,6 +64,15 @@ NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction on this pool's 
 ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8362.3
 
 
+def agree_min(n: int, world: int, dev) -> int:
+    """The smallest of the ranks' values (batch sizes derived from each GPU's free memory)."""
+    if world == 1:
+        return n
+    t = torch.tensor([n], dtype=torch.int64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+    return int(t.item())
+
+
 def log(msg: str) -> None:
     print(msg, file=sys.stderr, flush=True)
 
@@ -276,6 +285,7 @@ def run_b200(args) -> None:
         bs = args.batch
     else:
         bs = min(admit(prompts, pool_pages - 1), NUM_REQS)
+    bs = agree_min(bs, world, dev)  # tensor parallel: every rank runs the same batch
     prompts = prompts[:bs]
     full = prompts + OUT_TOKENS
     pages_per = (full + PAGE - 1) // PAGE
@@ -415,6 +425,9 @@ def run_b200(args) -> None:
         "gpu_launches": eng.launches_per_step * args.steps,
         "clocks": clk,
     }
+    err = ops.device_error_word(reset=False)
+    if err:
+        line["device_error_word"] = err  # a bounded in-kernel wait gave up or an index was bad
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
             line["cpu_baseline"] = cpu_decode_sample(args.cpu_steps, args.cpu_batch,
@@ -552,6 +565,7 @@ def run_b200_cdb(args) -> None:
     else:
         fit = np.cumsum(np.maximum(need, max_len)) + 1
         bs = int(min(np.searchsorted(fit, max_slots, side="right"), CDB_NUM_REQS))
+    bs = agree_min(bs, world, dev)  # tensor parallel: every rank runs the same batch
     num_pages = int(max(np.maximum(need, max_len)[:bs].sum() + 1, bs * max_len + 1))
     kv = model.make_kv_cache(num_pages, 1, zero=False)
     kv._kv_buffer.normal_(generator=torch.Generator(device=dev).manual_seed(SEED + 1))
@@ -691,6 +705,9 @@ def run_b200_cdb(args) -> None:
         "gpu_launches": eng.launches_per_step * args.steps,
         "clocks": clk,
     }
+    err = ops.device_error_word(reset=False)
+    if err:
+        line["device_error_word"] = err  # a bounded in-kernel wait gave up or an index was bad
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
             line["cpu_baseline"] = cpu_cdb_sample(args.cpu_steps, args.cpu_batch,

@@ -39,6 +39,7 @@ int lsb_abi_version(void);
 #define LSB_DEVERR_SLOT 2     /* a KV slot outside the pool */
 #define LSB_DEVERR_SEQLEN 4   /* a sequence longer than the max_seqlen bound */
 #define LSB_DEVERR_TIMEOUT 8  /* a bounded in-kernel wait gave up */
+#define LSB_DEVERR_COMM_TIMEOUT 16 /* a bounded wait for a peer GPU's data gave up */
 int lsb_device_error_word(int32_t* out, int32_t reset, void* stream);
 
 /* ---------------------------------------------------------------- norms --
@@ -337,7 +338,7 @@ int lsb_cdb_admit(void* hidden, int64_t ld, float* exit_state, const int64_t* sl
  * owned by one rank, which sums every rank's bf16 partial in rank order (fp32,
  * one rounding: all ranks receive identical bits) and writes the sum back to
  * every rank. Flags carry per-call epochs, so no reset is needed between calls;
- * every wait is bounded (LSB_DEVERR_TIMEOUT in the device error word). All ranks
+ * every wait is bounded (LSB_DEVERR_COMM_TIMEOUT in the device error word). All ranks
  * must make the same calls, with the same shapes, in the same order. Calls are
  * stream-ordered and capturable in CUDA graphs. Replaces the PyNCCL communicator
  * (python/loopsgl/distributed/impl.py:44-60, kernel/csrc/src/pynccl.cu:72-161,

@@ -27,6 +27,7 @@ LSB_DEVERR_POSITION = 1
 LSB_DEVERR_SLOT = 2
 LSB_DEVERR_SEQLEN = 4
 LSB_DEVERR_TIMEOUT = 8
+LSB_DEVERR_COMM_TIMEOUT = 16
 
 LSB_IPC_HANDLE_BYTES = 64
 

@@ -13,8 +13,9 @@
 // area; the peers copy it out. A rank can be at most one call ahead of a peer (it
 // needs that peer's words of the next call to finish it), and the epoch that every
 // rank advances once per call (the last CTA to finish stores it) tells the calls
-// apart. The all-gather keeps per-region flags (release/acquire at system scope).
-// Every wait is bounded and reports LSB_DEVERR_TIMEOUT instead of hanging.
+// apart: one epoch counter serves every operation, so tags of different operations
+// never coincide. The all-gather keeps per-region flags (release/acquire at system
+// scope). Every wait is bounded and reports LSB_DEVERR_COMM_TIMEOUT instead of hanging.
 #pragma once
 
 #include "common.cuh"
@@ -26,7 +27,7 @@ constexpr int kCommMaxRegions = 16384;
 enum CommOp : int { kOpGemmAllReduce = 0, kOpAllReduce = 1, kOpAllGather = 2, kCommOps = 3 };
 
 // Byte offsets inside a rank's symmetric buffer.
-constexpr int64_t kCommCtlOff = 0;  // u32 [kCommOps][2]: epoch, CTAs finished
+constexpr int64_t kCommCtlOff = 0;  // u32 [2]: epoch of the last call, CTAs finished
 constexpr int64_t kCommFlagsOff = 4096;
 constexpr int64_t kCommFlagBytes =
     static_cast<int64_t>(kCommMaxRegions) * kCommMaxWorld * sizeof(uint32_t);
@@ -84,29 +85,41 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 constexpr long long kCommTimeoutCycles = 4000000000LL;  // ~2 s
 
+// True once any bounded wait for a peer on this GPU has given up: later waits then fail
+// at once (a peer that stopped answering would otherwise cost every wait its full bound).
+__device__ __forceinline__ bool comm_failed(const int* err) {
+  return err && (*reinterpret_cast<const volatile int*>(err) & LSB_DEVERR_COMM_TIMEOUT);
+}
+
 // Bounded wait until *p == v (the flag of this call's epoch).
 __device__ __forceinline__ bool comm_wait(const uint32_t* p, uint32_t v, int* err) {
   if (ld_acquire_sys(p) == v) return true;
+  if (comm_failed(err)) return false;
   const long long t0 = clock64();
   while (ld_acquire_sys(p) != v) {
     if (clock64() - t0 > kCommTimeoutCycles) {
-      if (err) atomicOr(err, LSB_DEVERR_TIMEOUT);
+      if (err) atomicOr(err, LSB_DEVERR_COMM_TIMEOUT);
       return false;
     }
   }
   return true;
 }
 
-// This call's epoch of `op` (read by one thread of every CTA before it finishes).
+// This call's epoch: one counter for every operation of the communicator (tags and flags
+// of different operations share buffers, so their epochs must never coincide). Read by
+// one thread of every CTA before it finishes.
 __device__ __forceinline__ uint32_t comm_epoch(const CommDev& c, int op) {
-  return *reinterpret_cast<volatile uint32_t*>(c.ctl(c.rank) + 2 * op) + 1u;
+  (void)op;
+  return *reinterpret_cast<volatile uint32_t*>(c.ctl(c.rank)) + 1u;
 }
 
-// Called once per CTA (one thread) at its very end: the last CTA of the grid
-// stores the epoch, which the next call of `op` then advances.
+// Called once per CTA (one thread) at its very end: the last CTA of the grid stores the
+// epoch, which the next call then advances. Calls are stream-ordered on every rank, so
+// no two of them are in flight at once.
 __device__ __forceinline__ void comm_finish(const CommDev& c, int op, uint32_t epoch,
                                             unsigned ctas) {
-  uint32_t* ctl = c.ctl(c.rank) + 2 * op;
+  (void)op;
+  uint32_t* ctl = c.ctl(c.rank);
   __threadfence();
   const unsigned prev = atomicAdd(ctl + 1, 1u);
   if (prev == ctas - 1) {
@@ -173,10 +186,11 @@ __device__ __forceinline__ bool tag_get4(const uint64_t* words, int64_t e, uint3
                  : "memory");
     if (static_cast<uint32_t>(w0 >> 32) == epoch && static_cast<uint32_t>(w1 >> 32) == epoch) break;
     if (!waited) {
+      if (comm_failed(err)) return false;
       waited = true;
       t0 = clock64();
     } else if (clock64() - t0 > kCommTimeoutCycles) {
-      if (err) atomicOr(err, LSB_DEVERR_TIMEOUT);
+      if (err) atomicOr(err, LSB_DEVERR_COMM_TIMEOUT);
       return false;
     }
   }

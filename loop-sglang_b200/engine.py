@@ -83,6 +83,7 @@ class DecodeEngine:
 
     def capture(self) -> None:
         """Warm up (sizes every workspace), then capture one decode step."""
+        self.stream.wait_stream(torch.cuda.current_stream())  # set-up work comes first
         with torch.cuda.stream(self.stream):
             before = _lib.launch_count()
             self._body()
@@ -176,15 +177,18 @@ class CDBDecodeEngine:
         about to be decoded, and that token's id: its versions are reserved (full depth)
         and its prelude written, at depth 0."""
         n = handles.shape[1]
-        self.req_to_token[1:, :n].copy_(handles)
-        self.seq_lens.copy_(seq_lens)
-        self.ids.copy_(ids)
-        self.depth.zero_()
-        cur = self.req_to_token[1:].gather(1, (self.seq_lens - 1).long().view(-1, 1)).view(-1)
-        self.kv.reserve_versions(cur)
-        self.model.embed_tokens(self.ids, out=self.emb)
-        self.exited.fill_(1)
-        ops.cdb_admit(self.state["hidden"], self.state["exit"], self.slots, self.exited, self.emb)
+        self.stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.stream):  # the engine's stream orders every step after it
+            self.req_to_token[1:, :n].copy_(handles)
+            self.seq_lens.copy_(seq_lens)
+            self.ids.copy_(ids)
+            self.depth.zero_()
+            cur = self.req_to_token[1:].gather(1, (self.seq_lens - 1).long().view(-1, 1)).view(-1)
+            self.kv.reserve_versions(cur)
+            self.model.embed_tokens(self.ids, out=self.emb)
+            self.exited.fill_(1)
+            ops.cdb_admit(self.state["hidden"], self.state["exit"], self.slots, self.exited,
+                          self.emb)
 
     # ------------------------------------------------------------------- step --
     def _body(self) -> None:
@@ -214,12 +218,14 @@ class CDBDecodeEngine:
 
     def step(self) -> None:
         """One core step, eagerly (no graph)."""
+        self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             self._body()
 
     def capture(self) -> None:
         """One warm-up step (sizes every workspace), then capture one step. The warm-up is a
         real step: it advances the rows."""
+        self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
             before = _lib.launch_count()
             self._body()
