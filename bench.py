@@ -455,6 +455,9 @@ CDB_PROMPT_RANGE = (256, 1024)
 CDB_OUT_TOKENS = 512
 CDB_MID = 256
 CDB_EXIT_P = (0.15, 0.25, 0.30, 0.30)
+# DRAM bytes per context key of the attention kernel over last-exited versions (scattered
+# 4 KB K and V rows), from the ncu capture in profiles/cdb_step_launches_*.md
+CDB_ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8216.1
 CDB_METRIC = ("decode output tok/s, Ouro-1.4B CDB (configs[2]), last-exited KV, TP over the "
               "job's GPUs")
 CDB_WORKLOAD = ("configs[2]: Ouro-1.4B random-init bf16, continuous-depth batching with the "
@@ -694,7 +697,9 @@ def run_b200_cdb(args) -> None:
                    "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2 (each step streams ~%d GB)" % (step_bytes // 10**9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": round(CDB_ATTN_DRAM_BYTES_PER_CTX_TOKEN * model.hkv
+                                      / cfg.kv_heads * ctx_tokens),
                      "kernel": "paged_attention (layer-0 core step, rows at their own depths)",
                      "peak_kind": peak_kind,
                      "step_frac": round(step_bytes / step_s / 1e9 / peak, 4),
