@@ -594,7 +594,10 @@ size_t smem_for(int stages, int stage_bytes) {
 // cluster left for a second wave would double the kernel's time.
 Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   Plan pl;
-  int64_t bn = ((M + 15) / 16) * 16;
+  // tokens per tile: balanced over the fewest tiles of at most 256 (263 tokens -> 2 x 144,
+  // not 256 + 7: a second weight pass is paid either way, the narrower tiles are cheaper)
+  const int64_t m_tiles = (M + 255) / 256;
+  int64_t bn = (((M + m_tiles - 1) / m_tiles + 15) / 16) * 16;
   if (bn > 256) bn = 256;
   if (bn < 16) bn = 16;
   pl.bn = static_cast<int>(bn);
