@@ -839,11 +839,15 @@ int num_sms_attention() {
 }
 
 // Keys per item for the streaming kernel: enough items for about 16 per SM (so the
-// queue balances rows of different lengths), at least 64 keys, at most 1024.
-int64_t stream_chunk_for(int64_t rows, int64_t max_seqlen) {
+// queue balances rows of different lengths), but at least 512 KB of K+V per item (with
+// few KV heads a short item would cost the producer as much per-item work as it has
+// data to stream), at least 64 and at most 1024 keys.
+int64_t stream_chunk_for(int64_t rows, int64_t max_seqlen, int d, int hkv) {
   const int64_t want = 16 * static_cast<int64_t>(num_sms_attention());
+  int64_t floor_chunk = 64;
+  while (floor_chunk < 1024 && floor_chunk * 2 * hkv * d * 2 < 512 * 1024) floor_chunk <<= 1;
   int64_t chunk = 1024;
-  while (chunk > 64 && rows * ((max_seqlen + chunk - 1) / chunk) < want) chunk >>= 1;
+  while (chunk > floor_chunk && rows * ((max_seqlen + chunk - 1) / chunk) < want) chunk >>= 1;
   return chunk;
 }
 
@@ -874,7 +878,7 @@ extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, 
   const int64_t splits = (max_seqlen + chunk - 1) / chunk;
   int64_t bytes = workspace_bytes_for(rows, hq, head_dim, splits);
   if (hq <= kStreamMaxHeads) {
-    const int64_t sc = stream_chunk_for(rows, max_seqlen);
+    const int64_t sc = stream_chunk_for(rows, max_seqlen, head_dim, hq);  // most splits
     const int64_t b2 = workspace_bytes_for(rows, hq, head_dim,
                                            (max_seqlen + sc - 1) / sc * stream_warps_per_head(hq));
     if (b2 > bytes) bytes = b2;
@@ -904,7 +908,7 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
   LSB_REQUIRE(slot_stride >= (int64_t)hkv * head_dim, "paged_attention: slot stride too small");
   if (rows <= 0) return LSB_OK;
   if (use_stream(rows, hq, hkv, head_dim)) {
-    const int64_t chunk = stream_chunk_for(rows, max_seqlen);
+    const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
     const int64_t splits = (max_seqlen + chunk - 1) / chunk;
     LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
                 "paged_attention: max_seqlen too large");
