@@ -161,6 +161,7 @@ def test_paged_attention(d: int, page: int, mode: str) -> None:
     (40, 8, 64, 16),    # 3 heads per consumer warp (streaming kernel, 4-head variant)
     (20, 4, 128, 1),    # 2 heads per consumer warp, one-token pages
     (16, 16, 32, 16),   # 32 tokens per stage
+    (16, 8, 128, 1),    # scattered 2 KB rows: streaming kernel, one bulk copy pair per key
 ])
 @pytest.mark.parametrize("mode", ["decode", "long"])
 def test_paged_attention_heads(hq: int, hkv: int, d: int, page: int, mode: str) -> None:
