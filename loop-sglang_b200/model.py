@@ -138,6 +138,56 @@ class _Layer:
     norms: list[torch.Tensor]  # input, input_2, post_attention, post_attention_2
 
 
+def shard_weights(cfg: LoopedConfig, weights: dict[str, torch.Tensor], rank: int,
+                  world: int) -> dict[str, torch.Tensor]:
+    """This rank's tensor-parallel shard of a full state dict with merged ``qkv_proj`` and
+    ``gate_up_proj``, as the reference's loader splits (models/weight.py:38-56) and merges
+    (:106-115) it: q/k/v and gate/up rows chunked per rank (k/v replicated when there are
+    fewer KV heads than ranks), o_proj/down_proj columns chunked, the embedding and LM head
+    cut into ceil(V/t)-row vocabulary ranges; everything else replicated. The LM head
+    shard is zero-padded to ceil(V/t) rows so every rank's logits gather alike."""
+    t, r = world, rank
+    if t == 1:
+        return dict(weights)
+    d = cfg.head_dim
+
+    def rows(x: torch.Tensor) -> torch.Tensor:
+        return x.chunk(t, dim=0)[r]
+
+    def kv_rows(x: torch.Tensor) -> torch.Tensor:
+        if cfg.kv_heads < t:
+            h = r * cfg.kv_heads // t
+            return x[h * d:(h + 1) * d]
+        return rows(x)
+
+    vocab_local = -(-cfg.vocab // t)
+    start = r * vocab_local
+    vlen = max(0, min(vocab_local, cfg.vocab - start))
+    out: dict[str, torch.Tensor] = {}
+    for name, x in weights.items():
+        if name.endswith("self_attn.qkv_proj.weight") or name.endswith("self_attn.qkv_proj.bias"):
+            q, k, v = x.split([cfg.heads * d, cfg.kv_heads * d, cfg.kv_heads * d], dim=0)
+            out[name] = torch.cat([rows(q), kv_rows(k), kv_rows(v)], dim=0).contiguous()
+        elif name.endswith("mlp.gate_up_proj.weight"):
+            g, u = x.chunk(2, dim=0)
+            out[name] = torch.cat([rows(g), rows(u)], dim=0).contiguous()
+        elif name.endswith("self_attn.o_proj.weight") or name.endswith("mlp.down_proj.weight"):
+            out[name] = x.chunk(t, dim=1)[r].contiguous()
+        elif name in ("model.embed_tokens.weight", "lm_head.weight"):
+            part = x[start:start + vlen]
+            if name == "lm_head.weight" and vlen < vocab_local:
+                part = torch.cat([part, part.new_zeros(vocab_local - vlen, x.shape[1])])
+            out[name] = part.contiguous()
+        else:
+            out[name] = x
+    if cfg.tie_word_embeddings:  # the head is the embedding's vocabulary range
+        part = weights["model.embed_tokens.weight"][start:start + vlen]
+        if vlen < vocab_local:
+            part = torch.cat([part, part.new_zeros(vocab_local - vlen, part.shape[1])])
+        out["lm_head.weight"] = part.contiguous()
+    return out
+
+
 class LoopedDecoder:
     """A looped decoder under one looped-KV policy, weights resident in HBM (bf16)."""
 
@@ -160,66 +210,37 @@ class LoopedDecoder:
         self.hq = cfg.heads // t
         self.hkv = max(cfg.kv_heads // t, 1)
         self.inter = cfg.intermediate // t
-        d = cfg.head_dim
+        self.vocab_local = -(-cfg.vocab // t)
+        self.vocab_start = r * self.vocab_local
+        self.vocab_len = max(0, min(self.vocab_local, cfg.vocab - self.vocab_start))
+        weights = shard_weights(cfg, weights, r, t)
 
-        def bf(x: torch.Tensor) -> torch.Tensor:
+        def bf(name_or_x) -> torch.Tensor:
+            x = weights[name_or_x] if isinstance(name_or_x, str) else name_or_x
             return x.to(device=self.device, dtype=BF16).contiguous()
 
-        def rows(x: torch.Tensor) -> torch.Tensor:  # _SPLIT_DIM_0
-            return x.chunk(t, dim=0)[r]
-
-        def kv_rows(x: torch.Tensor) -> torch.Tensor:  # k/v: replicated below one head per rank
-            if cfg.kv_heads < t:
-                h = r * cfg.kv_heads // t
-                return x[h * d:(h + 1) * d]
-            return rows(x)
-
-        def qkv_shard(x: torch.Tensor) -> torch.Tensor:
-            q, k, v = x.split([cfg.heads * d, cfg.kv_heads * d, cfg.kv_heads * d], dim=0)
-            return torch.cat([rows(q), kv_rows(k), kv_rows(v)], dim=0)
-
-        def gate_up_shard(x: torch.Tensor) -> torch.Tensor:
-            g, u = x.chunk(2, dim=0)
-            return torch.cat([rows(g), rows(u)], dim=0)
-
-        def cols(x: torch.Tensor) -> torch.Tensor:  # _SPLIT_DIM_1
-            return x.chunk(t, dim=1)[r]
-
-        def opt(name: str, fn=lambda x: x) -> torch.Tensor | None:
-            return bf(fn(weights[name])) if name in weights else None
+        def opt(name: str) -> torch.Tensor | None:
+            return bf(name) if name in weights else None
 
         self.layers: dict[str, _Layer] = {}
         for p in cfg.layer_names():
-            gu = bf(gate_up_shard(weights[f"{p}.mlp.gate_up_proj.weight"]))
+            gu = bf(f"{p}.mlp.gate_up_proj.weight")
             self.layers[p] = _Layer(
-                qkv=bf(qkv_shard(weights[f"{p}.self_attn.qkv_proj.weight"])),
-                qkv_bias=opt(f"{p}.self_attn.qkv_proj.bias", qkv_shard),
-                o=bf(cols(weights[f"{p}.self_attn.o_proj.weight"])),
+                qkv=bf(f"{p}.self_attn.qkv_proj.weight"),
+                qkv_bias=opt(f"{p}.self_attn.qkv_proj.bias"),
+                o=bf(f"{p}.self_attn.o_proj.weight"),
                 gate_up=ops.swiglu_interleave(gu),
-                down=bf(cols(weights[f"{p}.mlp.down_proj.weight"])),
-                norms=[bf(weights[f"{p}.{n}.weight"]) for n in (
+                down=bf(f"{p}.mlp.down_proj.weight"),
+                norms=[bf(f"{p}.{n}.weight") for n in (
                     "input_layernorm", "input_layernorm_2", "post_attention_layernorm",
                     "post_attention_layernorm_2")],
             )
             del gu
-        # vocabulary partition (ParallelLMHead / VocabParallelEmbedding): ceil(V/t) rows per
-        # rank; the LM head is zero-padded to that size so every rank's logits gather alike
-        self.vocab_local = -(-cfg.vocab // t)
-        self.vocab_start = r * self.vocab_local
-        vlen = max(0, min(self.vocab_local, cfg.vocab - self.vocab_start))
-        self.vocab_len = vlen
-
-        def vocab_rows(x: torch.Tensor, pad: bool) -> torch.Tensor:
-            part = x[self.vocab_start:self.vocab_start + vlen]
-            if pad and vlen < self.vocab_local:
-                part = torch.cat([part, part.new_zeros(self.vocab_local - vlen, x.shape[1])])
-            return part
-
-        embed_full = weights["model.embed_tokens.weight"]
-        self.embed = bf(vocab_rows(embed_full, False)) if t > 1 else bf(embed_full)
-        head_full = embed_full if cfg.tie_word_embeddings else weights["lm_head.weight"]
-        self.lm_head_w = bf(vocab_rows(head_full, True)) if t > 1 else (
-            self.embed if cfg.tie_word_embeddings else bf(head_full))
+        self.embed = bf("model.embed_tokens.weight")
+        if cfg.tie_word_embeddings and t == 1:
+            self.lm_head_w = self.embed
+        else:
+            self.lm_head_w = bf("lm_head.weight")
         self.norm = bf(weights["model.norm.weight"])
         self.gate_w = opt("model.early_exit_gate.weight")
         self.gate_b = opt("model.early_exit_gate.bias")

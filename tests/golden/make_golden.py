@@ -16,7 +16,9 @@ What runs is the reference's own code:
 * its Triton kernels (page-table metadata, batch inputs, request-table
   assignment, last-exited reserve / alias / free / resolve) through the Triton
   interpreter (``TRITON_INTERPRET=1``), which runs programs in ascending order;
-* its ``store_cache`` CPU fallback.
+* its ``store_cache`` CPU fallback;
+* its streaming weight loader ``load_weight`` (tensor-parallel shard + merge) on a
+  small safetensors checkpoint, once per rank of two world sizes.
 
 Each fixture stores inputs and outputs; ``tests/test_oracle_golden.py`` checks
 that the oracle reproduces them (integers exactly, fp32 to 1e-5).
@@ -505,6 +507,64 @@ def store_case(out_dir):
                         k_cache=k_cache.numpy(), v_cache=v_cache.numpy())
     print("wrote store")
 
+# ---------------------------------------------------------------------------
+# Tensor-parallel weight sharding through the reference's own loader
+# ---------------------------------------------------------------------------
+
+TP_CFG = dict(hidden=32, heads=4, kv_heads=2, head_dim=8, intermediate=48, vocab=37)
+
+
+def tp_shard_case(out_dir):
+    """A tiny unmerged checkpoint (q/k/v with biases, gate/up, o/down, norms, embedding,
+    LM head; vocabulary 37 so the last rank's range is short) written as safetensors and
+    read back by ``loopsgl.models.weight.load_weight`` for every rank of worlds 2 and 4
+    (4 > kv heads, so k/v are replicated there). Stores the inputs and every rank's
+    sharded, merged tensors."""
+    import tempfile
+    from types import SimpleNamespace
+
+    import loopsgl.distributed.info as tp_info
+    from loopsgl.distributed import set_tp_info
+    from loopsgl.models.weight import load_weight
+    from safetensors.torch import save_file
+
+    c = TP_CFG
+    h, d, f, v = c["hidden"], c["head_dim"], c["intermediate"], c["vocab"]
+    g = torch.Generator().manual_seed(11)
+    p = "model.layers.0"
+    shapes = {
+        f"{p}.self_attn.q_proj.weight": (c["heads"] * d, h),
+        f"{p}.self_attn.k_proj.weight": (c["kv_heads"] * d, h),
+        f"{p}.self_attn.v_proj.weight": (c["kv_heads"] * d, h),
+        f"{p}.self_attn.q_proj.bias": (c["heads"] * d,),
+        f"{p}.self_attn.k_proj.bias": (c["kv_heads"] * d,),
+        f"{p}.self_attn.v_proj.bias": (c["kv_heads"] * d,),
+        f"{p}.self_attn.o_proj.weight": (h, c["heads"] * d),
+        f"{p}.mlp.gate_proj.weight": (f, h),
+        f"{p}.mlp.up_proj.weight": (f, h),
+        f"{p}.mlp.down_proj.weight": (h, f),
+        f"{p}.input_layernorm.weight": (h,),
+        "model.norm.weight": (h,),
+        "model.embed_tokens.weight": (v, h),
+        "lm_head.weight": (v, h),
+    }
+    tensors = {k: torch.randn(*s, generator=g) for k, s in shapes.items()}
+    rec = {f"in::{k}": t.numpy() for k, t in tensors.items()}
+    rec.update({k: np.array(val) for k, val in c.items()})
+    mc = SimpleNamespace(num_kv_heads=c["kv_heads"], is_moe=False)
+    with tempfile.TemporaryDirectory() as tmp:
+        save_file(tensors, os.path.join(tmp, "model.safetensors"))
+        for world in (2, 4):
+            for rank in range(world):
+                tp_info._TP_INFO = None
+                set_tp_info(rank, world)
+                for name, t in load_weight(tmp, torch.device("cpu"), model_config=mc):
+                    rec[f"w{world}r{rank}::{name}"] = t.numpy().copy()
+    tp_info._TP_INFO = None
+    set_tp_info(0, 1)
+    np.savez_compressed(out_dir / "tp_shard.npz", **rec)
+    print("wrote tp_shard")
+
 
 OURO_TINY = LoopedConfig(arch="ouro", hidden=128, heads=4, kv_heads=4, head_dim=32,
                          intermediate=256, vocab=512, num_core_layers=2, loop_steps=3,
@@ -529,6 +589,7 @@ def main() -> None:
     out = args.out
     metadata_case(out)
     store_case(out)
+    tp_shard_case(out)
     last_exited_case("last_exited_huginn_layout", 8, 2, 6, 3, 12, out)
     last_exited_case("last_exited_ouro_layout", 6, 0, 6, 4, 24, out)
     model_case("ouro_cb_depth_indexed", OURO_TINY, "depth_indexed", 1, PROMPTS, 3, 4, out)
