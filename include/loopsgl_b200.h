@@ -377,6 +377,61 @@ int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x, int6
                        const void* w, int64_t ldw, const void* bias, int64_t M, int64_t N,
                        int64_t K, int32_t epilogue, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Radix prefix cache (host runtime; no GPU work). A prefix tree over token ids
+ * whose nodes hold the KV token locations of those ids, matched and split at
+ * page granularity, with lock counts and oldest-first eviction of unlocked
+ * leaves: the reference's RadixPrefixCache (kvcache/radix_cache.py:102-232).
+ * Node handles are opaque int64 values that carry a generation: a handle to a
+ * node that was evicted since is refused (LSB_ERR_INVALID). One tree may be
+ * used from several threads (calls are serialised).
+ * ------------------------------------------------------------------------ */
+typedef struct lsb_radix lsb_radix;
+
+/* Length of the common prefix of two 1-D int32 (bits 32) or int64 (bits 64)
+ * arrays, the reference's fast_compare_key (kernel/csrc/src/radix.cpp:19-40). */
+int lsb_fast_compare_key(const void* a, int64_t na, const void* b, int64_t nb, int32_t bits,
+                         int64_t* out);
+
+/* A tree matching whole pages of page_size ids (RadixPrefixCache.__init__,
+ * radix_cache.py:103-112; the root is permanently locked). */
+int lsb_radix_create(int32_t page_size, lsb_radix** out);
+int lsb_radix_destroy(lsb_radix* tree);
+
+/* Longest cached page-aligned prefix of ids[n]: its end node and length
+ * (match_prefix / _tree_walk, radix_cache.py:133-135, 206-232). A node matched
+ * part-way is split at the page boundary, and the walked path is marked used. */
+int lsb_radix_match(lsb_radix* tree, const int32_t* ids, int64_t n, int64_t* node,
+                    int64_t* prefix_len);
+
+/* Insert the first floor(n / page) pages of ids with their KV locations:
+ * prefix_len = the length already cached (those locations stay the tree's; the
+ * caller frees its own copies), node/insert_len = the handle of the whole
+ * inserted prefix (insert_prefix, radix_cache.py:137-147). */
+int lsb_radix_insert(lsb_radix* tree, const int32_t* ids, const int32_t* indices, int64_t n,
+                     int64_t* node, int64_t* prefix_len, int64_t* insert_len);
+
+/* Lock (unlock = 0) or unlock a handle's path: locked nodes are never evicted
+ * (lock_handle, radix_cache.py:114-131). Unlocking an unlocked path fails and
+ * changes nothing. */
+int lsb_radix_lock(lsb_radix* tree, int64_t node, int32_t unlock);
+
+/* The KV locations of the prefix ending at `node`, root first, into out[capacity];
+ * *n = their number (RadixCacheHandle.get_matched_indices, radix_cache.py:92-99). */
+int lsb_radix_indices(lsb_radix* tree, int64_t node, int32_t* out, int64_t capacity, int64_t* n);
+
+/* Evict unlocked leaves, oldest first, until at least `size` locations are freed;
+ * writes them to out (capacity >= the evictable size), *n = how many (evict,
+ * radix_cache.py:149-176). size above the evictable size fails, changing nothing. */
+int lsb_radix_evict(lsb_radix* tree, int64_t size, int32_t* out, int64_t capacity, int64_t* n);
+
+/* Locations held by unlocked / locked nodes (size_info, radix_cache.py:181-186). */
+int lsb_radix_size_info(lsb_radix* tree, int64_t* evictable, int64_t* protected_size);
+
+/* Structural check: parent links, child keys, page-aligned runs, lock counts and
+ * the two size totals recounted (check_integrity, radix_cache.py:188-189). */
+int lsb_radix_check(lsb_radix* tree);
+
 #ifdef __cplusplus
 }
 #endif

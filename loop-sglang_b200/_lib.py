@@ -84,6 +84,16 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_allreduce": (ctypes.c_int, [P, P, I64, I64, I64, P]),
     "lsb_allgather": (ctypes.c_int, [P, P, P, I64, P]),
     "lsb_gemm_allreduce": (ctypes.c_int, [P, P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P]),
+    "lsb_fast_compare_key": (ctypes.c_int, [P, I64, P, I64, I32, P]),
+    "lsb_radix_create": (ctypes.c_int, [I32, P]),
+    "lsb_radix_destroy": (ctypes.c_int, [P]),
+    "lsb_radix_match": (ctypes.c_int, [P, P, I64, P, P]),
+    "lsb_radix_insert": (ctypes.c_int, [P, P, P, I64, P, P, P]),
+    "lsb_radix_lock": (ctypes.c_int, [P, I64, I32]),
+    "lsb_radix_indices": (ctypes.c_int, [P, I64, P, I64, P]),
+    "lsb_radix_evict": (ctypes.c_int, [P, I64, P, I64, P]),
+    "lsb_radix_size_info": (ctypes.c_int, [P, P, P]),
+    "lsb_radix_check": (ctypes.c_int, [P]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -122,7 +132,10 @@ def check(rc: int, what: str) -> None:
 
 _launches = 0
 _NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "lsb_ipc_handle",
-                 "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy"}
+                 "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy",
+                 "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
+                 "lsb_radix_insert", "lsb_radix_lock", "lsb_radix_indices", "lsb_radix_evict",
+                 "lsb_radix_size_info", "lsb_radix_check"}
 
 
 def launch_count() -> int:

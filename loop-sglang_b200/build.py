@@ -1,9 +1,10 @@
 """Build the sm_100a shared library ``libloopsgl_b200.so`` next to this file.
 
-Compiles every ``csrc/*.cu`` with nvcc for ``sm_100a`` (in parallel, skipping
-objects newer than their sources and headers) and links them with the static
-CUDA runtime. Usable as a script (``python loop-sglang_b200/build.py``) or via
-``__graft_entry__.build()``. nvcc cross-compiles, so no GPU is needed.
+Compiles every ``csrc/*.cu`` with nvcc for ``sm_100a`` and every host-only
+``csrc/*.cpp`` with the host compiler (in parallel, skipping objects newer than
+their sources and headers) and links them with the static CUDA runtime. Usable
+as a script (``python loop-sglang_b200/build.py``) or via ``__graft_entry__.build()``.
+nvcc cross-compiles, so no GPU is needed.
 """
 
 from __future__ import annotations
@@ -32,6 +33,13 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+def cxx() -> str:
+    for cand in (os.environ.get("CXX"), shutil.which("g++"), shutil.which("c++")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("no host C++ compiler found")
+
+
 def _stale(obj: Path, src: Path, deps: list[Path]) -> bool:
     if not obj.exists():
         return True
@@ -41,20 +49,24 @@ def _stale(obj: Path, src: Path, deps: list[Path]) -> bool:
 
 def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
     BUILD.mkdir(exist_ok=True)
-    sources = sorted(CSRC.glob("*.cu"))
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
     headers = sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
     cc = nvcc()
     extra = extra or []
 
     def compile_one(src: Path) -> Path:
-        obj = BUILD / (src.stem + ".o")
+        obj = BUILD / (src.name + ".o")
         if _stale(obj, src, headers):
-            cmd = [cc, *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
+            if src.suffix == ".cpp":
+                cmd = [cxx(), "-O3", "-std=c++17", "-fPIC", "-Wall", f"-I{ROOT / 'include'}",
+                       "-c", str(src), "-o", str(obj)]
+            else:
+                cmd = [cc, *ARCH, *FLAGS, *extra, "-c", str(src), "-o", str(obj)]
             if verbose:
                 print(" ".join(cmd), flush=True)
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
-                raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+                raise RuntimeError(f"compile failed on {src.name}:\n{r.stdout}\n{r.stderr}")
             if verbose and (r.stdout or r.stderr):
                 print(r.stdout + r.stderr, flush=True)
         return obj

@@ -18,7 +18,9 @@ What runs is the reference's own code:
   interpreter (``TRITON_INTERPRET=1``), which runs programs in ascending order;
 * its ``store_cache`` CPU fallback;
 * its streaming weight loader ``load_weight`` (tensor-parallel shard + merge) on a
-  small safetensors checkpoint, once per rank of two world sizes.
+  small safetensors checkpoint, once per rank of two world sizes;
+* its ``RadixPrefixCache`` on a seeded sequence of matches, inserts, locks and
+  evictions (page sizes 1 and 4).
 
 Each fixture stores inputs and outputs; ``tests/test_oracle_golden.py`` checks
 that the oracle reproduces them (integers exactly, fp32 to 1e-5).
@@ -566,6 +568,110 @@ def tp_shard_case(out_dir):
     print("wrote tp_shard")
 
 
+# ---------------------------------------------------------------------------
+# Radix prefix cache: a seeded operation sequence through the reference's tree
+# ---------------------------------------------------------------------------
+
+
+def radix_ops(page_size: int, seed: int, n_ops: int = 160) -> list[dict]:
+    """A scheduler-like sequence: requests made of one of four shared prefixes plus a
+    suffix over a small alphabet (so partial matches and splits are common) are matched,
+    locked, inserted with fresh page-aligned locations and later released; evictions
+    and unlocked probes are interleaved."""
+    rng = np.random.default_rng(seed)
+    prefixes = [rng.integers(0, 5, int(rng.integers(2, 7)) * page_size).tolist() for _ in range(4)]
+    ops: list[dict] = []
+    live: list[int] = []  # op numbers of requests whose inserted handle is locked
+    next_page = 1
+    for _ in range(n_ops):
+        r = rng.random()
+        if r < 0.5 or not live:
+            ids = list(prefixes[int(rng.integers(0, 4))])
+            ids += rng.integers(0, 3, int(rng.integers(0, 4 * page_size + 3))).tolist()
+            if rng.random() < 0.2:
+                ids = rng.integers(0, 5, int(rng.integers(1, 6 * page_size))).tolist()
+            pages = -(-len(ids) // page_size)
+            fresh = [(next_page + i // page_size) * page_size + i % page_size
+                     for i in range(pages * page_size)]
+            next_page += pages
+            ops.append({"kind": "request", "ids": ids, "fresh": fresh})
+            live.append(len(ops) - 1)
+        elif r < 0.75:
+            ops.append({"kind": "finish", "ref": live.pop(int(rng.integers(0, len(live))))})
+        elif r < 0.9:
+            ops.append({"kind": "evict", "frac": float(rng.random())})
+        else:
+            ids = list(prefixes[int(rng.integers(0, 4))])[: int(rng.integers(1, 5 * page_size))]
+            ops.append({"kind": "probe", "ids": ids})
+    return ops
+
+
+def radix_case(out_dir):
+    """Runs ``radix_ops`` through ``loopsgl.kvcache.radix_cache.RadixPrefixCache`` on the
+    CPU (its node timestamps drawn from a counter instead of the wall clock, its key
+    comparison from numpy: both order-preserving) and records every result: match and
+    insert lengths, matched indices, evicted indices in eviction order, size totals."""
+    import json
+
+    import loopsgl.core as core
+    import loopsgl.kernel as lk
+    import loopsgl.kvcache.radix_cache as rc
+
+    tick = iter(range(1, 1 << 62))
+    rc.time = type("Clock", (), {"monotonic_ns": staticmethod(lambda: next(tick))})
+
+    def compare(a, b):
+        n = min(len(a), len(b))
+        d = np.flatnonzero(a[:n].numpy() != b[:n].numpy())
+        return int(d[0]) if d.size else n
+
+    lk.fast_compare_key = compare
+
+    def indices(h):  # the reference's callers read a handle only when it holds a prefix
+        return h.get_matched_indices() if h.cached_len else torch.empty(0, dtype=torch.int32)
+
+    cases = []
+    for page_size, seed in ((1, 5), (4, 6)):
+        old = core._GLOBAL_CTX
+        core._GLOBAL_CTX = None
+        core.set_global_ctx(core.Context(page_size=page_size))
+        cache = rc.RadixPrefixCache(torch.device("cpu"))
+        ops = radix_ops(page_size, seed)
+        handles = {}
+        for i, op in enumerate(ops):
+            if op["kind"] == "request":
+                ids = torch.tensor(op["ids"], dtype=torch.int32)
+                m = cache.match_prefix(ids).cuda_handle
+                cache.lock_handle(m)
+                matched = indices(m)
+                loc = torch.cat([matched, torch.tensor(op["fresh"][m.cached_len:len(op["ids"])],
+                                                       dtype=torch.int32)])
+                ins = cache.insert_prefix(ids, loc)
+                cache.lock_handle(m, unlock=True)  # the order of CacheManager.cache_req
+                cache.lock_handle(ins.handle)
+                handles[i] = ins.handle
+                op["want"] = {"match_len": m.cached_len, "matched": matched.tolist(),
+                              "cached_len": ins.cached_len, "insert_len": ins.handle.cached_len,
+                              "inserted": indices(ins.handle).tolist()}
+            elif op["kind"] == "finish":
+                cache.lock_handle(handles.pop(op["ref"]), unlock=True)
+                op["want"] = {}
+            elif op["kind"] == "evict":
+                size = int(op["frac"] * cache.size_info.evictable_size)
+                op["size"] = size
+                op["want"] = {"evicted": cache.evict(size).tolist()}
+            else:
+                h = cache.match_prefix(torch.tensor(op["ids"], dtype=torch.int32)).cuda_handle
+                op["want"] = {"match_len": h.cached_len, "matched": indices(h).tolist()}
+            info = cache.size_info
+            op["want"]["size_info"] = [info.evictable_size, info.protected_size]
+        cases.append({"page_size": page_size, "seed": seed, "ops": ops})
+        core._GLOBAL_CTX = old
+    with open(out_dir / "radix.json", "w") as f:
+        json.dump({"cases": cases}, f, separators=(",", ":"))
+    print("wrote radix")
+
+
 OURO_TINY = LoopedConfig(arch="ouro", hidden=128, heads=4, kv_heads=4, head_dim=32,
                          intermediate=256, vocab=512, num_core_layers=2, loop_steps=3,
                          rope_theta=10000.0, max_position=256)
@@ -590,6 +696,7 @@ def main() -> None:
     metadata_case(out)
     store_case(out)
     tp_shard_case(out)
+    radix_case(out)
     last_exited_case("last_exited_huginn_layout", 8, 2, 6, 3, 12, out)
     last_exited_case("last_exited_ouro_layout", 6, 0, 6, 4, 24, out)
     model_case("ouro_cb_depth_indexed", OURO_TINY, "depth_indexed", 1, PROMPTS, 3, 4, out)
