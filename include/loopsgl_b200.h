@@ -378,6 +378,47 @@ int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x, int6
                        int64_t K, int32_t epilogue, void* stream);
 
 /* ------------------------------------------------------------------------
+ * KV snapshots for retraction: a request's KV rows copied to host memory in
+ * the reference's byte layout and restored into newly reserved locations.
+ * Host layout: [2][E][n][row_bytes] (K then V; E expanded layers in layer order,
+ * each core layer of a versioned pool once per loop depth; tokens in the order
+ * of `indices`), then, for a versioned pool, n int32 completed depths.
+ * pool is [2][lanes][pool_rows][row_bytes] on the device: a paged pool passes
+ * lanes = num_layers, pool_rows = pages * page_size and slot_map = NULL (the row
+ * of token j is indices[j]); the last-exited pool passes its slot map
+ * [fixed + steps*core groups, width], lanes = layers per slot and the core
+ * layer range [core_start, core_end) with `steps` loop depths. row_bytes must be
+ * a multiple of 16. Rows move through `staging` (device, >= 2*E*row_bytes) in
+ * chunks of tokens: one gather / scatter kernel and one strided 2-D copy per
+ * chunk; both calls return after their copies completed. A row outside the
+ * pool (or a restore into row 0, the padding row) is skipped and flagged
+ * LSB_DEVERR_SLOT. Replaces MHAKVCache.get_cpu_copy / load_cpu_copy
+ * (kvcache/mha_pool.py:68-105) and LastExitedKVCache.get_cpu_copy /
+ * load_cpu_copy (kvcache/last_exited.py:320-376).
+ * ------------------------------------------------------------------------ */
+
+/* Snapshot bytes of n tokens (cpu_copy_size, mha_pool.py:68-69 with versioned
+ * = 0; last_exited.py:317-318 with versioned = 1), or -1 for invalid shapes. */
+int64_t lsb_kv_snapshot_bytes(int64_t n, int64_t row_bytes, int32_t num_layers,
+                              int32_t core_start, int32_t core_end, int32_t steps,
+                              int32_t versioned);
+
+int lsb_kv_backup(void* host_out, const void* pool, int64_t lanes, int64_t pool_rows,
+                  int64_t row_bytes, const int32_t* indices, int64_t n, const int32_t* slot_map,
+                  int64_t width, const int32_t* completed_depth, int32_t num_layers,
+                  int32_t core_start, int32_t core_end, int32_t steps, void* staging,
+                  int64_t staging_bytes, void* stream);
+
+/* The inverse: host_in's rows into the pool at the (already reserved) rows of
+ * `indices`; a versioned snapshot's trailing depths are not read here (the
+ * caller reserves the versions with them: lsb_last_exited_reserve with
+ * restore_depths). */
+int lsb_kv_restore(void* pool, const void* host_in, int64_t lanes, int64_t pool_rows,
+                   int64_t row_bytes, const int32_t* indices, int64_t n, const int32_t* slot_map,
+                   int64_t width, int32_t num_layers, int32_t core_start, int32_t core_end,
+                   int32_t steps, void* staging, int64_t staging_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Radix prefix cache (host runtime; no GPU work). A prefix tree over token ids
  * whose nodes hold the KV token locations of those ids, matched and split at
  * page granularity, with lock counts and oldest-first eviction of unlocked

@@ -84,6 +84,11 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_allreduce": (ctypes.c_int, [P, P, I64, I64, I64, P]),
     "lsb_allgather": (ctypes.c_int, [P, P, P, I64, P]),
     "lsb_gemm_allreduce": (ctypes.c_int, [P, P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P]),
+    "lsb_kv_snapshot_bytes": (c_int64, [I64, I64, I32, I32, I32, I32, I32]),
+    "lsb_kv_backup": (ctypes.c_int, [P, P, I64, I64, I64, P, I64, P, I64, P, I32, I32, I32, I32, P,
+                                     I64, P]),
+    "lsb_kv_restore": (ctypes.c_int, [P, P, I64, I64, I64, P, I64, P, I64, I32, I32, I32, I32, P,
+                                      I64, P]),
     "lsb_fast_compare_key": (ctypes.c_int, [P, I64, P, I64, I32, P]),
     "lsb_radix_create": (ctypes.c_int, [I32, P]),
     "lsb_radix_destroy": (ctypes.c_int, [P]),

@@ -49,6 +49,36 @@ class MHAKVCache:
         kc, vc = self.slots(layer_id)
         ops.store_kv(kc, vc, out_loc, k, v)
 
+    # retraction snapshots (mha_pool.py:68-105) --------------------------------
+    @property
+    def _row_bytes(self) -> int:
+        return self._row * self._kv_buffer.element_size()
+
+    def cpu_copy_size(self, num_tokens: int) -> int:
+        return ops.kv_snapshot_bytes(num_tokens, self._row_bytes, self._num_layers)
+
+    def get_cpu_copy(self, indices: torch.Tensor) -> torch.Tensor:
+        """Every KV layer's rows of ``indices``, in token order: ``[2, L, n, Hkv, D]`` in
+        pinned host memory (one gather kernel + one strided copy per staging chunk)."""
+        idx = indices.to(device=self.device, dtype=torch.int32).contiguous()
+        out = torch.empty(2, self._num_layers, idx.numel(), self.num_kv_heads, self.head_dim,
+                          dtype=self.dtype, pin_memory=True)
+        b = self._kv_buffer
+        ops.kv_backup(out, b, self._num_layers, b.shape[2] * b.shape[3], self._row_bytes, idx,
+                      self._num_layers)
+        return out
+
+    def load_cpu_copy(self, cpu_tensors: torch.Tensor, indices: torch.Tensor) -> None:
+        """Restore exact KV values into new token locations."""
+        expected = (2, self._num_layers, indices.numel(), self.num_kv_heads, self.head_dim)
+        if (cpu_tensors.is_cuda or cpu_tensors.dtype != self.dtype
+                or tuple(cpu_tensors.shape) != expected):
+            raise ValueError("CPU KV backup does not match the destination pool and token count.")
+        idx = indices.to(device=self.device, dtype=torch.int32).contiguous()
+        b = self._kv_buffer
+        ops.kv_restore(b, cpu_tensors.contiguous(), self._num_layers, b.shape[2] * b.shape[3],
+                       self._row_bytes, idx, self._num_layers)
+
     @property
     def num_layers(self) -> int:
         return self._num_layers
@@ -161,6 +191,79 @@ class LastExitedKVCache:
                                     self._free_count, handles, self.loop_steps,
                                     self.fixed_groups, self.core_groups)
             self.available_slots += released_slots
+
+    # retraction snapshots (last_exited.py:160-178, 255-290, 313-376) ---------
+    @staticmethod
+    def memory_per_page(num_layers: int, num_core_layers: int, loop_steps: int,
+                        row_bytes: int) -> int:
+        """Storage and allocator metadata bytes per nominal one-token page."""
+        lps = gcd(num_core_layers, num_layers - num_core_layers)
+        core_groups = num_core_layers // lps
+        fixed_groups = (num_layers - num_core_layers) // lps
+        mappings = fixed_groups + loop_steps * core_groups
+        return 2 * num_layers * row_bytes + (mappings + 1 + fixed_groups + core_groups) * 4
+
+    @property
+    def _row_bytes(self) -> int:
+        return self._row * self._kv_buffer.element_size()
+
+    @property
+    def _expanded_layers(self) -> int:
+        return self._num_layers + (self.core_end - self.core_start) * (self.loop_steps - 1)
+
+    def cpu_copy_size(self, num_tokens: int) -> int:
+        return ops.kv_snapshot_bytes(num_tokens, self._row_bytes, self._num_layers,
+                                     self.core_start, self.core_end, self.loop_steps, True)
+
+    def get_cpu_copy(self, indices: torch.Tensor) -> torch.Tensor:
+        """Exact KV bytes of every layer at every loop depth of ``indices``, then one int32
+        completed depth per token, as a uint8 tensor in pinned host memory."""
+        idx = indices.to(device=self.device, dtype=torch.int32).contiguous()
+        out = torch.empty(self.cpu_copy_size(idx.numel()), dtype=torch.uint8, pin_memory=True)
+        ops.kv_backup(out, self._kv_buffer, self.layers_per_slot, self.num_kv_slots,
+                      self._row_bytes, idx, self._num_layers, slot_map=self.slot_map,
+                      completed_depth=self.completed_depth, core_start=self.core_start,
+                      core_end=self.core_end, steps=self.loop_steps)
+        return out
+
+    def restore_depths(self, backup: torch.Tensor, num_tokens: int) -> torch.Tensor:
+        if (backup.dtype != torch.uint8 or backup.is_cuda
+                or backup.numel() != self.cpu_copy_size(num_tokens)):
+            raise ValueError("Invalid last-exited CPU KV backup.")
+        depths = (backup[-num_tokens * 4:].view(torch.int32) if num_tokens
+                  else torch.empty(0, dtype=torch.int32))
+        if bool((depths < 1).any()) or bool((depths > self.loop_steps).any()):
+            raise ValueError("CPU KV backup contains invalid completed depths.")
+        return depths
+
+    def restore_slots(self, backup: torch.Tensor, num_tokens: int) -> int:
+        """Fixed-layer and recurrent slots a snapshot needs when restored."""
+        depths = self.restore_depths(backup, num_tokens)
+        return num_tokens * self.fixed_groups + int(depths.sum()) * self.core_groups
+
+    def reserve_restore_versions(self, handles: torch.Tensor, backup: torch.Tensor) -> int:
+        """Reserve exactly the versions the snapshot holds (its completed depths; deeper
+        depths alias the last computed one). Returns the versions not reserved."""
+        depths = self.restore_depths(backup, handles.numel())
+        needed = handles.numel() * self.fixed_groups + int(depths.sum()) * self.core_groups
+        if needed > self.available_slots:
+            raise RuntimeError("Recurrent KV pool lacks space for the exact CPU snapshot.")
+        if handles.numel():
+            ops.last_exited_reserve(self.slot_map, self.completed_depth, self._free_slots,
+                                    self._free_count, handles, self.loop_steps,
+                                    self.fixed_groups, self.core_groups,
+                                    restore_depths=depths.to(self.device).contiguous())
+            self.available_slots -= needed
+        return handles.numel() * self.loop_steps - int(depths.sum())
+
+    def load_cpu_copy(self, cpu_tensors: torch.Tensor, indices: torch.Tensor) -> None:
+        """Restore a snapshot after its versions have been reserved."""
+        self.restore_depths(cpu_tensors, indices.numel())
+        idx = indices.to(device=self.device, dtype=torch.int32).contiguous()
+        ops.kv_restore(self._kv_buffer, cpu_tensors.contiguous(), self.layers_per_slot,
+                       self.num_kv_slots, self._row_bytes, idx, self._num_layers,
+                       slot_map=self.slot_map, core_start=self.core_start, core_end=self.core_end,
+                       steps=self.loop_steps)
 
     @property
     def num_layers(self) -> int:

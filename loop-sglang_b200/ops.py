@@ -409,3 +409,60 @@ def set_metadata(seq_lens, extend_lens, req_to_token, req_pool_indices, max_seq_
          req_to_token.data_ptr(), req_to_token.stride(0), req_pool_indices.data_ptr(),
          seq_lens.data_ptr(), _p(extend_lens), seq_lens.numel(), max_seq_pages, page_size,
          seq_len_delta, int(is_decode), _stream())
+
+
+# ---------------------------------------------------------- KV snapshots --
+
+KV_STAGING_BYTES = 256 << 20  # device staging bound of one snapshot copy
+
+
+def kv_snapshot_bytes(n: int, row_bytes: int, num_layers: int, core_start: int = 0,
+                      core_end: int = 0, steps: int = 1, versioned: bool = False) -> int:
+    """Host bytes of an n-token KV snapshot (see ``lsb_kv_snapshot_bytes``)."""
+    b = lib().lsb_kv_snapshot_bytes(n, row_bytes, num_layers, core_start, core_end, steps,
+                                    int(versioned))
+    if b < 0:
+        raise ValueError("kv_snapshot_bytes: invalid pool shape")
+    return b
+
+
+def _staging(total: int, per_token: int, device) -> torch.Tensor:
+    size = max(per_token, min(total, KV_STAGING_BYTES // per_token * per_token))
+    return torch.empty(size, dtype=torch.uint8, device=device)
+
+
+def kv_backup(host_out: torch.Tensor, pool: torch.Tensor, lanes: int, pool_rows: int,
+              row_bytes: int, indices: torch.Tensor, num_layers: int, slot_map=None,
+              completed_depth=None, core_start: int = 0, core_end: int = 0,
+              steps: int = 1) -> None:
+    """Gather a snapshot of ``indices`` into ``host_out`` (CPU, ideally pinned); returns
+    after the copies completed. ``lsb_kv_backup``."""
+    _need(pool, pool.dtype, "pool")
+    _need(indices, torch.int32, "indices")
+    if host_out.is_cuda or not host_out.is_contiguous():
+        raise ValueError("kv_backup: host_out must be a contiguous CPU tensor")
+    n = indices.numel()
+    expanded = (num_layers + (core_end - core_start) * (steps - 1)) if slot_map is not None \
+        else num_layers
+    staging = _staging(2 * expanded * n * row_bytes, 2 * expanded * row_bytes, pool.device)
+    call("lsb_kv_backup", host_out.data_ptr(), pool.data_ptr(), lanes, pool_rows, row_bytes,
+         indices.data_ptr(), n, _p(slot_map), 0 if slot_map is None else slot_map.shape[1],
+         _p(completed_depth), num_layers, core_start, core_end, steps, staging.data_ptr(),
+         staging.numel(), _stream())
+
+
+def kv_restore(pool: torch.Tensor, host_in: torch.Tensor, lanes: int, pool_rows: int,
+               row_bytes: int, indices: torch.Tensor, num_layers: int, slot_map=None,
+               core_start: int = 0, core_end: int = 0, steps: int = 1) -> None:
+    """Scatter a snapshot back into the pool at ``indices`` (``lsb_kv_restore``)."""
+    _need(pool, pool.dtype, "pool")
+    _need(indices, torch.int32, "indices")
+    if host_in.is_cuda or not host_in.is_contiguous():
+        raise ValueError("kv_restore: host_in must be a contiguous CPU tensor")
+    n = indices.numel()
+    expanded = (num_layers + (core_end - core_start) * (steps - 1)) if slot_map is not None \
+        else num_layers
+    staging = _staging(2 * expanded * n * row_bytes, 2 * expanded * row_bytes, pool.device)
+    call("lsb_kv_restore", pool.data_ptr(), host_in.data_ptr(), lanes, pool_rows, row_bytes,
+         indices.data_ptr(), n, _p(slot_map), 0 if slot_map is None else slot_map.shape[1],
+         num_layers, core_start, core_end, steps, staging.data_ptr(), staging.numel(), _stream())

@@ -20,7 +20,8 @@ What runs is the reference's own code:
 * its streaming weight loader ``load_weight`` (tensor-parallel shard + merge) on a
   small safetensors checkpoint, once per rank of two world sizes;
 * its ``RadixPrefixCache`` on a seeded sequence of matches, inserts, locks and
-  evictions (page sizes 1 and 4).
+  evictions (page sizes 1 and 4);
+* its two KV pools' retraction snapshots (``get_cpu_copy`` / ``load_cpu_copy``).
 
 Each fixture stores inputs and outputs; ``tests/test_oracle_golden.py`` checks
 that the oracle reproduces them (integers exactly, fp32 to 1e-5).
@@ -554,7 +555,7 @@ def tp_shard_case(out_dir):
     rec = {f"in::{k}": t.numpy() for k, t in tensors.items()}
     rec.update({k: np.array(val) for k, val in c.items()})
     mc = SimpleNamespace(num_kv_heads=c["kv_heads"], is_moe=False)
-    with tempfile.TemporaryDirectory() as tmp:
+    with tempfile.TemporaryDirectory(dir=out_dir) as tmp:
         save_file(tensors, os.path.join(tmp, "model.safetensors"))
         for world in (2, 4):
             for rank in range(world):
@@ -672,6 +673,69 @@ def radix_case(out_dir):
     print("wrote radix")
 
 
+# ---------------------------------------------------------------------------
+# Retraction snapshots of both KV pools through the reference's own pools
+# ---------------------------------------------------------------------------
+
+
+def kv_snapshot_case(out_dir):
+    """``MHAKVCache`` and ``LastExitedKVCache`` (fp32, CPU) filled with seeded values:
+    the snapshot ``get_cpu_copy`` takes of some tokens, and the pool state after
+    ``load_cpu_copy`` restores it at other tokens of a fresh (zeroed) pool -- for the
+    last-exited pool after ``reserve_restore_versions`` with the snapshot's depths, and
+    with tokens that exited at different depths (aliased versions) in the snapshot."""
+    from loopsgl.kvcache.last_exited import LastExitedKVCache
+    from loopsgl.kvcache.mha_pool import MHAKVCache
+
+    g = torch.Generator().manual_seed(17)
+    rec = {}
+    # paged pool: 3 layers, 6 pages of 4, 2 heads x 8
+    mha = MHAKVCache(2, 3, 8, 6, 4, torch.float32, torch.device("cpu"))
+    mha._kv_buffer.copy_(torch.randn(mha._kv_buffer.shape, generator=g))
+    mha._kv_buffer[:, :, 0].zero_()
+    src = torch.tensor([5, 6, 7, 12, 13, 21, 4], dtype=torch.int32)
+    dst = torch.tensor([8, 9, 10, 16, 17, 18, 23], dtype=torch.int32)
+    rec["mha_pool"] = mha._kv_buffer.numpy().copy()
+    rec["mha_src"], rec["mha_dst"] = src.numpy(), dst.numpy()
+    snap = mha.get_cpu_copy(src)
+    rec["mha_snapshot"] = snap.numpy().copy()
+    fresh = MHAKVCache(2, 3, 8, 6, 4, torch.float32, torch.device("cpu"))
+    fresh._kv_buffer.zero_()
+    fresh.load_cpu_copy(snap, dst)
+    rec["mha_restored"] = fresh._kv_buffer.numpy().copy()
+
+    # last-exited pool: 6 layers, core [1, 5), 3 loop steps (2 layers per slot)
+    def pool():
+        p = LastExitedKVCache(2, 6, 8, 20, 1, torch.float32, torch.device("cpu"), 1, 5, 3)
+        p._kv_buffer.zero_()
+        return p
+
+    le = pool()
+    handles = torch.arange(1, 7, dtype=torch.int32)
+    le.reserve_versions(handles)
+    le._kv_buffer.copy_(torch.randn(le._kv_buffer.shape, generator=g))
+    le._kv_buffer[:, :, 0].zero_()
+    exits = torch.tensor([1, 3, 2, 3, 1, 2], dtype=torch.int32)
+    le.alias_versions(handles, exits, int((3 - exits).sum()))
+    rec["le_pool"] = le._kv_buffer.numpy().copy()
+    rec["le_slot_map"] = le.slot_map.numpy().copy()
+    rec["le_completed"] = le.completed_depth.numpy().copy()
+    src = torch.tensor([2, 5, 1, 6, 3], dtype=torch.int32)
+    snap = le.get_cpu_copy(src)
+    rec["le_src"], rec["le_snapshot"] = src.numpy(), snap.numpy().copy()
+    fresh = pool()
+    dst = torch.tensor([4, 9, 2, 11, 7], dtype=torch.int32)
+    rec["le_dst"] = dst.numpy()
+    rec["le_released"] = np.array(fresh.reserve_restore_versions(dst, snap))
+    fresh.load_cpu_copy(snap, dst)
+    rec["le_restored"] = fresh._kv_buffer.numpy().copy()
+    rec["le_restored_slot_map"] = fresh.slot_map.numpy().copy()
+    rec["le_restored_completed"] = fresh.completed_depth.numpy().copy()
+    rec["le_restored_free_count"] = fresh._free_count.numpy().copy()
+    np.savez_compressed(out_dir / "kv_snapshot.npz", **rec)
+    print("wrote kv_snapshot")
+
+
 OURO_TINY = LoopedConfig(arch="ouro", hidden=128, heads=4, kv_heads=4, head_dim=32,
                          intermediate=256, vocab=512, num_core_layers=2, loop_steps=3,
                          rope_theta=10000.0, max_position=256)
@@ -697,6 +761,7 @@ def main() -> None:
     store_case(out)
     tp_shard_case(out)
     radix_case(out)
+    kv_snapshot_case(out)
     last_exited_case("last_exited_huginn_layout", 8, 2, 6, 3, 12, out)
     last_exited_case("last_exited_ouro_layout", 6, 0, 6, 4, 24, out)
     model_case("ouro_cb_depth_indexed", OURO_TINY, "depth_indexed", 1, PROMPTS, 3, 4, out)
