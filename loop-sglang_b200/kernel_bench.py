@@ -10,6 +10,7 @@ CUDA events on the capturing stream after warm-up replays.
     python loop-sglang_b200/kernel_bench.py gemm --tokens 143 --shape qkv o gate_up down
     python -m torch.distributed.run --nproc-per-node 2 loop-sglang_b200/kernel_bench.py \
         gemm_ar --tokens 256     # row-parallel GEMM fused with its all-reduce, per rank
+    python loop-sglang_b200/kernel_bench.py snapshot --tokens 2048   # retraction copy
 
 It is also the small case for profiler captures of one kernel (one KV layer of a
 few GB instead of the whole pool that the decode benchmark holds).
@@ -184,6 +185,41 @@ def bench_gemm_ar(args, ops, comm, name: str) -> dict:
             "nvlink_bytes": int(link), "nvlink_GBps": round(link / us_ar / 1e3, 1)}
 
 
+def bench_snapshot(args, kvcache) -> dict:
+    """Retraction snapshot of one Ouro-1.4B request under last-exited KV (24 recurrent
+    layers, 4 loop steps, 16 KV heads x 128 bf16): ``get_cpu_copy`` of ``tokens`` handles
+    that exited at mixed depths into pinned host memory, and ``load_cpu_copy`` back into
+    freshly reserved versions of a second pool. Wall time around each call (both end
+    with a stream synchronisation), best of ``reps``."""
+    import time
+
+    dev = torch.device("cuda", 0)
+    n = args.tokens
+    pages = 4 * n + 2
+    a = kvcache.LastExitedKVCache(16, 24, 128, pages, 0, 24, 4, dev, zero=False)
+    b = kvcache.LastExitedKVCache(16, 24, 128, pages, 0, 24, 4, dev, zero=False)
+    handles = torch.arange(1, n + 1, dtype=torch.int32, device=dev)
+    a.reserve_versions(handles)
+    exits = torch.randint(1, 5, (n,), dtype=torch.int32, device=dev)
+    a.alias_versions(handles, exits, int((4 - exits).sum()))
+    snap = a.get_cpu_copy(handles)
+    b.reserve_restore_versions(handles, snap)
+    best_out = best_in = float("inf")
+    for _ in range(args.reps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        a.get_cpu_copy(handles)
+        t1 = time.perf_counter()
+        b.load_cpu_copy(snap, handles)
+        t2 = time.perf_counter()
+        best_out, best_in = min(best_out, t1 - t0), min(best_in, t2 - t1)
+    nbytes = snap.numel()
+    return {"kernel": "kv_snapshot", "tokens": n, "bytes": nbytes,
+            "backup_ms": round(best_out * 1e3, 2), "restore_ms": round(best_in * 1e3, 2),
+            "backup_GBps": round(nbytes / best_out / 1e9, 1),
+            "restore_GBps": round(nbytes / best_in / 1e9, 1)}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = ap.add_subparsers(dest="kernel", required=True)
@@ -208,6 +244,9 @@ def main(argv=None) -> None:
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
     ga.add_argument("--reps", type=int, default=60)
+    sn = sub.add_parser("snapshot")
+    sn.add_argument("--tokens", type=int, default=2048)
+    sn.add_argument("--reps", type=int, default=5)
     args = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("kernel_bench needs a CUDA device")
@@ -233,6 +272,10 @@ def main(argv=None) -> None:
         dist.destroy_process_group()
         return
     torch.cuda.set_device(0)
+    if args.kernel == "snapshot":
+        print(json.dumps(bench_snapshot(args, importlib.import_module("loop_sglang_b200.kvcache"))),
+              flush=True)
+        return
     if args.kernel == "attention":
         print(json.dumps(bench_attention(args, ops)), flush=True)
     else:
