@@ -3,7 +3,9 @@
 // layer slice and page table the caller passes in).
 //
 // Work decomposition (flash-decoding): a CTA of kWarps warps handles one query
-// row, kWarps consecutive query heads and one split of `chunk` keys. Inside a
+// row, kWarps consecutive query heads and one split of `chunk` keys (with fewer
+// heads than warps, the spare warps take interleaved sub-streams of the same
+// heads' keys and merge into the head's first warp through shared memory). Inside a
 // warp, groups of kLanes lanes each own one key at a time (kLanes = D/8 rounded
 // up to a power of two, every lane holding 8 head dims), so one warp streams
 // 32/kLanes keys per load with 16-byte non-allocating loads, kUnroll keys deep
@@ -66,8 +68,8 @@ int64_t workspace_bytes_for(int64_t rows, int32_t hq, int32_t d, int64_t splits)
   return (b + 255) & ~int64_t(255);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kWarps * 32)
+template <int D, int KSUB>
+__global__ void __launch_bounds__(kWarps * 32, 6)
     paged_attention_kernel(bf16* __restrict__ out, int64_t out_stride,
                            const bf16* __restrict__ q, int64_t q_stride,
                            const bf16* __restrict__ k_cache, const bf16* __restrict__ v_cache,
@@ -83,12 +85,18 @@ __global__ void __launch_bounds__(kWarps * 32)
   constexpr int kGroups = 32 / kLanes;        // keys per warp per load
   constexpr int kVec = D / 8;                 // active lanes per key
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int groups_per_row = (hq + kWarps - 1) / kWarps;
+  // Heads per CTA; with fewer heads than warps, the spare warps of a head take
+  // interleaved sub-streams of its keys (KSUB = kWarps / hpc streams per head, a
+  // compile-time count so the one-stream variant carries no merge state), merged below.
+  constexpr int ksub = KSUB;
+  constexpr int hpc = kWarps / KSUB;  // KSUB > 1 only when hq == hpc (one or two heads)
+  const int groups_per_row = (hq + hpc - 1) / hpc;
   const int64_t row = blockIdx.x / groups_per_row;
   const int hgroup = static_cast<int>(blockIdx.x % groups_per_row);
   const int64_t split = blockIdx.y;
-  const int h = hgroup * kWarps + warp;
-  const bool head_ok = h < hq;
+  const int kslot = warp / hpc;
+  const int h = hgroup * hpc + warp % hpc;
+  const bool head_ok = h < hq && kslot < ksub;
 
   // Request of this row: cu_seqlens_q[b] <= row < cu_seqlens_q[b + 1].
   int lo = 0, hi = num_reqs - 1;
@@ -142,7 +150,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   __syncthreads();
   const int64_t head_off = static_cast<int64_t>(kvh) * D + 8 * c;
   if (head_ok) {
-    for (int64_t base = k_begin; base < k_end; base += kGroups * kUnroll) {
+    for (int64_t base = k_begin + kslot * kGroups * kUnroll; base < k_end;
+         base += static_cast<int64_t>(ksub) * kGroups * kUnroll) {
       bf16x8 kr[kUnroll], vr[kUnroll];
       bool valid[kUnroll];
 #pragma unroll
@@ -211,8 +220,31 @@ __global__ void __launch_bounds__(kWarps * 32)
     for (int e = 0; e < 8; ++e) acc[e] = acc[e] * c1 + __shfl_xor_sync(0xffffffffu, acc[e], o) * c2;
     m = mn;
   }
+  // Merge the key sub-streams of a head (warps kslot > 0 into warp kslot = 0).
+  if constexpr (KSUB > 1) {
+    __shared__ float s_state[kWarps][10][32];
+    if (head_ok && kslot > 0) {
+      s_state[warp][0][lane] = m;
+      s_state[warp][1][lane] = l;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s_state[warp][2 + e][lane] = acc[e];
+    }
+    __syncthreads();
+    if (head_ok && kslot == 0) {
+      for (int k2 = 1; k2 < ksub; ++k2) {
+        const int w2 = k2 * hpc + warp;
+        const float m2 = s_state[w2][0][lane], l2 = s_state[w2][1][lane];
+        const float mn = fmaxf(m, m2);
+        const float c1 = exp2f(m - mn), c2 = exp2f(m2 - mn);
+        l = l * c1 + l2 * c2;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = acc[e] * c1 + s_state[w2][2 + e][lane] * c2;
+        m = mn;
+      }
+    }
+  }
 
-  const bool writer = head_ok && g == 0 && dim_ok;
+  const bool writer = head_ok && kslot == 0 && g == 0 && dim_ok;
   if (nsplit == 1) {
     if (writer) {
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -242,7 +274,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     if (is_last) *counter = 0;  // every split has arrived: reset for the next launch
   }
   __syncthreads();
-  if (!is_last || !head_ok) return;
+  if (!is_last || !head_ok || kslot != 0) return;
   __threadfence();
   // Warp h merges its head: lane j owns dims 4j .. 4j+3.
   constexpr int kQuads = D / 4;
@@ -1004,9 +1036,18 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
         static_cast<int>(num_reqs), hq, hkv, page_size, chunk, splits, max_seqlen, scale_log2,
         ws, lsb_device_error_flag());
   };
-  if (head_dim == 32) launch(paged_attention_kernel<32>);
-  else if (head_dim == 64) launch(paged_attention_kernel<64>);
-  else if (head_dim == 96) launch(paged_attention_kernel<96>);
-  else launch(paged_attention_kernel<128>);
-  return check_launch("lsb_paged_attention");
+  const int ksub = kWarps / (hq < kWarps ? hq : kWarps);  // 1, 2 (two heads) or 4 (one)
+#define LSB_CTA_DISPATCH(DIM)                                                   \
+  if (head_dim == DIM) {                                                        \
+    if (ksub == 4) launch(paged_attention_kernel<DIM, 4>);                      \
+    else if (ksub == 2) launch(paged_attention_kernel<DIM, 2>);                 \
+    else launch(paged_attention_kernel<DIM, 1>);                                \
+    return check_launch("lsb_paged_attention");                                 \
+  }
+  LSB_CTA_DISPATCH(32)
+  LSB_CTA_DISPATCH(64)
+  LSB_CTA_DISPATCH(96)
+  LSB_CTA_DISPATCH(128)
+#undef LSB_CTA_DISPATCH
+  return fail(LSB_ERR_UNSUPPORTED, "paged_attention: head_dim %d", head_dim);
 }

@@ -162,6 +162,10 @@ def test_paged_attention(d: int, page: int, mode: str) -> None:
     (20, 4, 128, 1),    # 2 heads per consumer warp, one-token pages
     (16, 16, 32, 16),   # 32 tokens per stage
     (16, 8, 128, 1),    # scattered 2 KB rows: streaming kernel, one bulk copy pair per key
+    (4, 4, 128, 1),     # scattered 1 KB rows (a TP=4 rank): per-CTA kernel, a warp per head
+    (2, 2, 128, 1),     # a TP=8 rank: per-CTA kernel, two key sub-streams per head
+    (1, 1, 64, 1),      # one head: four key sub-streams merged in shared memory
+    (3, 1, 128, 1),     # three heads: one warp idle, grouped-query KV
 ])
 @pytest.mark.parametrize("mode", ["decode", "long"])
 def test_paged_attention_heads(hq: int, hkv: int, d: int, page: int, mode: str) -> None:
