@@ -139,13 +139,21 @@ class ClockSampler:
         except Exception:
             ident = str(device.index or 0)
         self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                    "-i", ident, "-lms", "200"]
+                    "-i", ident, "-lms", "50"]
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(self.cmd, stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # the timed region starts only once samples are flowing, so it is covered by them
+        deadline = time.perf_counter() + 5.0
+        while time.perf_counter() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            if Path(self.file.name).stat().st_size > 0:
+                break
+            time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
@@ -555,10 +563,14 @@ def run_b200_cdb(args) -> None:
     steps_total = args.warmup + args.steps + 1 + (args.steps if not args.no_e2e else 0) + 1
     ctx = prompts + CDB_MID  # tokens before the one being decoded
     gen_depth = cdb_depths(CDB_NUM_REQS * CDB_MID, SEED + 1).reshape(CDB_NUM_REQS, CDB_MID)
+    # exit depths of the outputs to come (the replay depths of the run)
+    out_cap = steps_total + 8
+    future_all = cdb_depths(CDB_NUM_REQS * out_cap, SEED + 2).reshape(CDB_NUM_REQS, out_cap)
+    exits = (np.cumsum(future_all, axis=1) <= steps_total).sum(1)  # outputs finished in the run
     # version slots a request holds: prompt tokens keep every loop step (prefill runs at full
-    # depth), generated ones their exit depth; plus the token being decoded and the steps
-    # to come (at most a fresh full-depth token per step)
-    need = prompts * 4 + gen_depth.sum(1) + 4 * (steps_total + 1)
+    # depth), generated ones their exit depth; plus the token being decoded and one fresh
+    # full-depth token per output the run finishes (reserved before the exit aliases)
+    need = prompts * 4 + gen_depth.sum(1) + 4 * (exits + 2)
     max_len = int(ctx.max()) + steps_total + 2
     slot_bytes = 2 * cfg.num_core_layers * model.hkv * cfg.head_dim * 2
     free, _ = torch.cuda.mem_get_info(dev)
@@ -588,9 +600,7 @@ def run_b200_cdb(args) -> None:
                             handles[live].contiguous(), kv.loop_steps, kv.fixed_groups,
                             kv.core_groups, restore_depths=restore[live].contiguous())
     kv.available_slots -= int(restore[live].sum().item()) * kv.core_groups
-    out_cap = steps_total + 8
-    future = torch.as_tensor(cdb_depths(bs * out_cap, SEED + 2).reshape(bs, out_cap),
-                             device=dev).contiguous()
+    future = torch.as_tensor(future_all[:bs], device=dev).contiguous()
     eng = CDBDecodeEngine(model, kv, bs, max_len, out_cap, replay_depths=future)
     ids0 = torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32)
     eng.start(handles, (ctx_b + 1).to(torch.int32), ids0)
@@ -732,7 +742,9 @@ def run_b200_cdb(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 20 for cdb, 40 for cb -- a few hundred ms to "
+                         "a second and a half, covered by several clock samples)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--batch", type=int, default=0, help="override the admitted batch (debug)")
@@ -743,6 +755,10 @@ def main() -> None:
     ap.add_argument("--workload", choices=["cdb", "cb"], default="cdb",
                     help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.workload == "cdb" else 40
+    if args.steps < 1:
+        ap.error("--steps must be >= 1")
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

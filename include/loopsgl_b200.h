@@ -172,6 +172,12 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
 /* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
  * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
  * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */
+/* The launch plan lsb_gemm picks for an M x N x K product on the current device
+ * (diagnostics): out[0] tokens per tile, out[1] output tiles, out[2] split-K
+ * factor (CTAs per cluster), out[3] pipeline stages, out[4] dynamic shared
+ * memory bytes per CTA. */
+int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out);
+
 int lsb_swiglu_interleave(void* out, const void* w, int64_t inter, int64_t K, void* stream);
 
 /* ---------------------------------------------- loop-step exit kernels ---

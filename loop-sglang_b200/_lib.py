@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                                    I64, I64, I32, I32, I32, I32, I64, F, P]),
     "lsb_gemm_workspace_size": (c_int64, [I64, I64, I64]),
     "lsb_gemm": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P, I64, P]),
+    "lsb_gemm_plan": (ctypes.c_int, [I64, I64, I64, P]),
     "lsb_swiglu_interleave": (ctypes.c_int, [P, P, I64, I64, P]),
     "lsb_ouro_step_exit": (ctypes.c_int, [P, I64, P, P, P, P, P, P, P, P, P, P, I32, I32, I32, F,
                                           I64, I64, F, P]),
@@ -138,7 +139,7 @@ def check(rc: int, what: str) -> None:
 _launches = 0
 _NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "lsb_ipc_handle",
                  "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy",
-                 "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
+                 "lsb_gemm_plan", "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
                  "lsb_radix_insert", "lsb_radix_lock", "lsb_radix_indices", "lsb_radix_evict",
                  "lsb_radix_size_info", "lsb_radix_check"}
 

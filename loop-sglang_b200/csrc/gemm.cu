@@ -649,6 +649,17 @@ uint32_t make_idesc(int bn) {
 
 using namespace lsb;
 
+extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
+  LSB_REQUIRE(out && M > 0 && N > 0 && K > 0, "gemm_plan: bad arguments");
+  const Plan pl = plan_for(M, N, K);
+  out[0] = pl.bn;
+  out[1] = pl.tiles_n * pl.tiles_m;
+  out[2] = pl.splits;
+  out[3] = pl.stages;
+  out[4] = static_cast<int32_t>(pl.smem);
+  return LSB_OK;
+}
+
 extern "C" int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   (void)M;
   (void)N;

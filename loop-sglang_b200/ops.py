@@ -10,6 +10,7 @@ their counters zeroed, so one buffer serves every later call.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -20,6 +21,7 @@ from ._lib import (
     LSB_EPI_NONE,
     LSB_EPI_SWIGLU,
     call,
+    check,
     lib,
 )
 
@@ -414,6 +416,14 @@ def set_metadata(seq_lens, extend_lens, req_to_token, req_pool_indices, max_seq_
 # ---------------------------------------------------------- KV snapshots --
 
 KV_STAGING_BYTES = 256 << 20  # device staging bound of one snapshot copy
+
+
+def gemm_plan(m: int, n: int, k: int) -> dict:
+    """The tile plan ``gemm`` uses for an m x n x k product on the current device."""
+    out = (ctypes.c_int32 * 5)()
+    check(lib().lsb_gemm_plan(m, n, k, out), "gemm_plan")
+    return {"tokens_per_tile": out[0], "tiles": out[1], "splits": out[2], "stages": out[3],
+            "smem": out[4], "ctas": out[1] * out[2]}
 
 
 def kv_snapshot_bytes(n: int, row_bytes: int, num_layers: int, core_start: int = 0,
