@@ -3,7 +3,8 @@
 //
 // One CTA per row; each thread keeps up to kMaxVec 16-byte vectors (8 bf16) of
 // the row in registers between the reductions and the write, so a row is read
-// and written once. Rounding points follow the reference: the plain norm rounds
+// and written once. Weights and the residual are fetched together with the row,
+// ahead of the first reduction, so a row costs one memory round trip. Rounding points follow the reference: the plain norm rounds
 // its output; the fused add keeps the fp32 sum for the norm and stores the
 // rounded sum as the residual (layers/norm.py:16-38).
 #include "common.cuh"
@@ -44,25 +45,6 @@ __device__ __forceinline__ float sumsq(const RowRegs& r) {
   return s;
 }
 
-// r.v <- r.v * rrms * w (fp32), optionally rounded to bf16 in place.
-__device__ __forceinline__ void scale_by(RowRegs& r, const bf16* w, int64_t dim, float rrms,
-                                         bool round) {
-  const int n = nvec(dim);
-#pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    const int j = threadIdx.x + i * blockDim.x;
-    if (j < n) {
-      float wf[8];
-      unpack8(*reinterpret_cast<const bf16x8*>(w + 8 * j), wf);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float y = r.v[i][e] * rrms * wf[e];
-        r.v[i][e] = round ? round_bf16(y) : y;
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ void store_row(bf16* row, int64_t dim, const RowRegs& r) {
   const int n = nvec(dim);
 #pragma unroll
@@ -88,6 +70,39 @@ __device__ __forceinline__ void add_residual(RowRegs& r, bf16* res, int64_t dim)
   }
 }
 
+// A row's 16-byte vectors held as loaded (bf16), for operands fetched ahead of use.
+struct RowRaw {
+  bf16x8 v[kMaxVec];
+};
+
+__device__ __forceinline__ void fetch_row(const bf16* row, int64_t dim, RowRaw& o) {
+  const int n = nvec(dim);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int j = threadIdx.x + i * blockDim.x;
+    if (j < n) o.v[i] = *reinterpret_cast<const bf16x8*>(row + 8 * j);
+  }
+}
+
+// r.v <- r.v * rrms * w (w already fetched), optionally rounded to bf16.
+__device__ __forceinline__ void scale_by_raw(RowRegs& r, const RowRaw& w, int64_t dim, float rrms,
+                                             bool round) {
+  const int n = nvec(dim);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int j = threadIdx.x + i * blockDim.x;
+    if (j < n) {
+      float wf[8];
+      unpack8(w.v[i], wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float y = r.v[i][e] * rrms * wf[e];
+        r.v[i][e] = round ? round_bf16(y) : y;
+      }
+    }
+  }
+}
+
 __global__ void rmsnorm_kernel(bf16* __restrict__ out, int64_t out_stride,
                                const bf16* __restrict__ x, int64_t x_stride,
                                const bf16* __restrict__ w, int64_t dim, float eps) {
@@ -95,9 +110,11 @@ __global__ void rmsnorm_kernel(bf16* __restrict__ out, int64_t out_stride,
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
+  RowRaw rw;
   load_row(x + row * x_stride, dim, r);
+  fetch_row(w, dim, rw);  // with x: one memory round trip before the reduction
   const float rrms = rsqrtf(block_sum(sumsq(r), red) / static_cast<float>(dim) + eps);
-  scale_by(r, w, dim, rrms, false);
+  scale_by_raw(r, rw, dim, rrms, false);
   store_row(out + row * out_stride, dim, r);
 }
 
@@ -107,23 +124,42 @@ __global__ void add_rmsnorm_kernel(bf16* __restrict__ x, bf16* __restrict__ res,
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   RowRegs r;
+  RowRaw rw;
   load_row(x + row * dim, dim, r);
+  fetch_row(w, dim, rw);  // fetched with x and the residual, ahead of the reduction
   add_residual(r, res + row * dim, dim);
   const float rrms = rsqrtf(block_sum(sumsq(r), red) / static_cast<float>(dim) + eps);
-  scale_by(r, w, dim, rrms, false);
+  scale_by_raw(r, rw, dim, rrms, false);
   store_row(x + row * dim, dim, r);
 }
 
 // y = round(rms(x) * wa); s = y + res; res = round(s); out = rms(s) * wb.
+// Both weights and the residual are fetched with x, before the first reduction, so the
+// row costs one memory round trip instead of three.
 __device__ __forceinline__ void sandwich_row(RowRegs& r, const bf16* x, bf16* res,
                                              const bf16* wa, const bf16* wb, int64_t dim,
                                              float eps, float* red) {
+  RowRaw ra, rb, rr;
   load_row(x, dim, r);
+  fetch_row(wa, dim, ra);
+  fetch_row(res, dim, rr);
+  fetch_row(wb, dim, rb);
   const float rrms1 = rsqrtf(block_sum(sumsq(r), red) / static_cast<float>(dim) + eps);
-  scale_by(r, wa, dim, rrms1, true);
-  add_residual(r, res, dim);
+  scale_by_raw(r, ra, dim, rrms1, true);
+  const int n = nvec(dim);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {  // r.v <- r.v + residual (fp32); residual <- bf16(sum)
+    const int j = threadIdx.x + i * blockDim.x;
+    if (j < n) {
+      float rf[8];
+      unpack8(rr.v[i], rf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r.v[i][e] += rf[e];
+      *reinterpret_cast<bf16x8*>(res + 8 * j) = pack8(r.v[i]);
+    }
+  }
   const float rrms2 = rsqrtf(block_sum(sumsq(r), red) / static_cast<float>(dim) + eps);
-  scale_by(r, wb, dim, rrms2, false);
+  scale_by_raw(r, rb, dim, rrms2, false);
 }
 
 __global__ void sandwich_kernel(bf16* __restrict__ out, const bf16* x, bf16* __restrict__ res,

@@ -11,6 +11,7 @@ CUDA events on the capturing stream after warm-up replays.
     python -m torch.distributed.run --nproc-per-node 2 loop-sglang_b200/kernel_bench.py \
         gemm_ar --tokens 256     # row-parallel GEMM fused with its all-reduce, per rank
     python loop-sglang_b200/kernel_bench.py snapshot --tokens 2048   # retraction copy
+    python loop-sglang_b200/kernel_bench.py norm --rows 263          # Ouro sandwich norm
 
 It is also the small case for profiler captures of one kernel (one KV layer of a
 few GB instead of the whole pool that the decode benchmark holds).
@@ -185,6 +186,20 @@ def bench_gemm_ar(args, ops, comm, name: str) -> dict:
             "nvlink_bytes": int(link), "nvlink_GBps": round(link / us_ar / 1e3, 1)}
 
 
+def bench_norm(args, ops) -> dict:
+    """The Ouro sandwich norm (rmsnorm, residual add, rmsnorm) on ``rows`` x 2048, its
+    inputs resident in L2 as they are in the decode step (it reads the GEMM output just
+    written); device time per launch inside a CUDA graph."""
+    dev = torch.device("cuda", 0)
+    x = torch.randn(args.rows, 2048, device=dev).to(torch.bfloat16)
+    res = torch.randn(args.rows, 2048, device=dev).to(torch.bfloat16)
+    wa = torch.rand(2048, device=dev).to(torch.bfloat16)
+    wb = torch.rand(2048, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    us = _time_graph(lambda i: ops.sandwich_norm(x, res, wa, wb, 1e-6, out=out), args.reps)
+    return {"kernel": "sandwich_norm", "rows": args.rows, "us": round(us, 2)}
+
+
 def bench_snapshot(args, kvcache) -> dict:
     """Retraction snapshot of one Ouro-1.4B request under last-exited KV (24 recurrent
     layers, 4 loop steps, 16 KV heads x 128 bf16): ``get_cpu_copy`` of ``tokens`` handles
@@ -244,6 +259,9 @@ def main(argv=None) -> None:
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
     ga.add_argument("--reps", type=int, default=60)
+    nm = sub.add_parser("norm")
+    nm.add_argument("--rows", type=int, default=263)
+    nm.add_argument("--reps", type=int, default=100)
     sn = sub.add_parser("snapshot")
     sn.add_argument("--tokens", type=int, default=2048)
     sn.add_argument("--reps", type=int, default=5)
@@ -272,6 +290,9 @@ def main(argv=None) -> None:
         dist.destroy_process_group()
         return
     torch.cuda.set_device(0)
+    if args.kernel == "norm":
+        print(json.dumps(bench_norm(args, ops)), flush=True)
+        return
     if args.kernel == "snapshot":
         print(json.dumps(bench_snapshot(args, importlib.import_module("loop_sglang_b200.kvcache"))),
               flush=True)
