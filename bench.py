@@ -1,7 +1,7 @@
 """Decode throughput of the looped-decoder hot path on B200 (one JSON line on stdout).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload cdb|cb]
+                    [--workload cdb|cb|radix]
 
 Default workload (the metric's): Ouro-1.4B architecture (24 shared
 layers x 4 loop steps, hidden 2048, 16 MHA heads x 128, SwiGLU 5632, vocab 49152),
@@ -18,6 +18,11 @@ repository's kernels, replayed as one CUDA graph; ``value`` = output tokens / ti
 ``--workload cb``: full-depth CB decode with depth-indexed KV and
 16-token pages, 256 requests with prompts U[512, 2048] + 256 outputs; a step is one
 decode step of the running batch (4 x 24 layers, LM head, sampling).
+
+``--workload radix``: Ouro-2.6B (48 layers) full-depth decode, 256
+requests in 4 groups of 64 sharing a 2048-token prefix + 2048 unique tokens, 512 outputs;
+the page tables come from the radix prefix cache, so a group's rows read one copy of the
+prefix pages (the roofline counts those bytes once per group).
 
 KV contents and token ids are synthetic (seeded random), as are the weights. ``value``
 times K device-resident steps; ``e2e`` times K steps through the host (H2D of the
@@ -50,6 +55,7 @@ sys.path.insert(0, str(ROOT))
 OURO_14B = dict(arch="ouro", hidden=2048, heads=16, kv_heads=16, head_dim=128,
                 intermediate=5632, vocab=49152, num_core_layers=24, loop_steps=4,
                 rope_theta=1e6, rms_eps=1e-6, max_position=4096)
+OURO_26B = {**OURO_14B, "num_core_layers": 48, "max_position": 8192}
 PAGE = 16
 NUM_REQS = 256
 PROMPT_RANGE = (512, 2048)
@@ -180,18 +186,19 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU side --
 
-def cpu_decode_sample(steps: int, batch: int, threads: int) -> dict:
+def cpu_decode_sample(steps: int, batch: int, threads: int, model_cfg: dict | None = None,
+                      contexts: np.ndarray | None = None, name: str = "Ouro-1.4B") -> dict:
     """The oracle (CPU restatement of the reference decode step) on a bounded sample:
-    ``batch`` requests of the workload at mean context, ``steps`` decode steps."""
+    ``batch`` requests of the workload (configs[1] contexts unless given), ``steps``
+    full-depth decode steps."""
     from oracle import model as om
 
     torch.set_num_threads(threads)
-    cfg = om.LoopedConfig(**OURO_14B)
+    cfg = om.LoopedConfig(**(model_cfg or OURO_14B))
     t0 = time.perf_counter()
     w = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
     mdl = om.LoopedModel(cfg, w, "depth_indexed")
-    prompts = request_lengths()[:batch]
-    ctx = prompts + MID
+    ctx = (request_lengths()[:batch] + MID) if contexts is None else np.asarray(contexts)[:batch]
     pages_per = [(int(c) + steps + PAGE) // PAGE for c in ctx]
     num_pages = sum(pages_per) + 1
     pool = om.PagedKVPool(mdl.num_kv_layers, num_pages, PAGE, cfg.kv_heads, cfg.head_dim,
@@ -218,7 +225,7 @@ def cpu_decode_sample(steps: int, batch: int, threads: int) -> dict:
     total = sum(times)
     return {"value": batch * steps / total, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": (f"{batch} requests at context {int(ctx.mean())} (mean), {steps} decode "
-                       f"steps of Ouro-1.4B through the CPU oracle in torch bf16/fp32, "
+                       f"steps of {name} through the CPU oracle in torch bf16/fp32, "
                        f"{threads} threads; setup {setup:.0f}s untimed"),
             "p50_step_s": statistics.median(times)}
 
@@ -231,6 +238,10 @@ def run_reference(args) -> None:
     if args.workload == "cdb":
         base = cpu_cdb_sample(max(1, args.steps), args.cpu_batch, threads)
         metric, workload = CDB_METRIC, CDB_WORKLOAD
+    elif args.workload == "radix":
+        base = cpu_decode_sample(max(1, min(args.steps, 2)), 1, threads, OURO_26B,
+                                 np.array([RADIX_PREFIX + RADIX_SUFFIX + RADIX_MID]), "Ouro-2.6B")
+        metric, workload = RADIX_METRIC, RADIX_WORKLOAD
     else:
         base = cpu_decode_sample(max(1, args.steps), args.cpu_batch, threads)
         metric, workload = METRIC, WORKLOAD
@@ -248,6 +259,24 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# Ouro-2.6B, depth-indexed KV, radix prefix cache: 256 requests in 4
+# groups of 64 sharing a 2048-token random prefix, each with a 2048-token unique suffix,
+# 512 outputs. Requests are interleaved over the groups so every group is present in a
+# capacity-limited batch; page tables come from this repository's radix prefix cache.
+RADIX_GROUPS = 4
+RADIX_REQS = 256
+RADIX_PREFIX = 2048
+RADIX_SUFFIX = 2048
+RADIX_OUT = 512
+RADIX_MID = 256
+RADIX_METRIC = ("decode output tok/s, Ouro-2.6B CB full depth with a shared-prefix radix "
+                "cache (configs[3]), TP over the job's GPUs")
+RADIX_WORKLOAD = ("configs[3]: Ouro-2.6B random-init bf16 (48 layers x 4 loop steps), full-depth "
+                  "decode, depth-indexed KV with 16-token pages, 256 requests in 4 groups of 64 "
+                  "sharing a 2048-token random prefix + 2048 unique tokens, 512 outputs; page "
+                  "tables built through the radix prefix cache (shared prefix pages); "
+                  "capacity-limited running batch decoding at prompt+256")
+
 METRIC = "decode output tok/s, Ouro-1.4B CB full depth (configs[1]), TP over the job's GPUs"
 WORKLOAD = ("configs[1]: Ouro-1.4B random-init bf16, full-depth CB decode, depth-indexed KV, "
             "16-token pages, 256 requests prompt U[512,2048] + 256 outputs, capacity-limited "
@@ -255,6 +284,39 @@ WORKLOAD = ("configs[1]: Ouro-1.4B random-init bf16, full-depth CB decode, depth
 
 
 # ---------------------------------------------------------------- GPU side --
+
+def radix_page_tables(eng, free_pages: np.ndarray, bs: int, vocab: int, dev) -> int:
+    """Page tables of the radix workload built as the reference's cache manager builds them
+    (match the request's ids, lock, allocate pages for the rest, insert the prompt):
+    through this repository's radix prefix cache. Returns the prompt tokens served from
+    the cache (the shared prefixes)."""
+    from loop_sglang_b200.prefix_cache import RadixPrefixCache
+
+    rng = np.random.default_rng(SEED + 3)
+    prefixes = rng.integers(0, vocab, (RADIX_GROUPS, RADIX_PREFIX)).astype(np.int32)
+    cache = RadixPrefixCache("cpu", page_size=PAGE)
+    total = RADIX_PREFIX + RADIX_SUFFIX + RADIX_OUT
+    nxt, hits = 0, 0
+    for r in range(bs):
+        ids = np.concatenate([prefixes[r % RADIX_GROUPS],
+                              rng.integers(0, vocab, RADIX_SUFFIX).astype(np.int32)])
+        handle = cache.match_prefix(torch.from_numpy(ids)).cuda_handle
+        cache.lock_handle(handle)
+        cached = handle.cached_len
+        hits += cached
+        matched = handle.get_matched_indices().numpy()[::PAGE] // PAGE if cached else \
+            np.zeros(0, np.int64)
+        n_new = (total - cached) // PAGE
+        pages = np.concatenate([matched, free_pages[nxt:nxt + n_new]]).astype(np.int64)
+        nxt += n_new
+        locs = (pages[:, None] * PAGE + np.arange(PAGE)).reshape(-1).astype(np.int32)
+        ins = cache.insert_prefix(torch.from_numpy(ids), torch.from_numpy(locs[:ids.size]))
+        cache.lock_handle(handle, unlock=True)
+        cache.lock_handle(ins.handle)
+        eng.assign_pages(r + 1, torch.from_numpy(pages).to(dev))
+    cache.check_integrity()
+    return hits
+
 
 def run_b200(args) -> None:
     from __graft_entry__ import load_package
@@ -275,7 +337,9 @@ def run_b200(args) -> None:
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
-    cfg = LoopedConfig(**OURO_14B)
+    radix = args.workload == "radix"
+    cfg = LoopedConfig(**(OURO_26B if radix else OURO_14B))
+    out_tokens, mid = (RADIX_OUT, RADIX_MID) if radix else (OUT_TOKENS, MID)
     t0 = time.perf_counter()
     comm = None
     if world > 1:  # symmetric buffer: the largest all-reduce / LM-head gather of a step
@@ -285,33 +349,44 @@ def run_b200(args) -> None:
     model = LoopedDecoder(cfg, weights, "depth_indexed", dev, comm=comm)
     del weights
     torch.cuda.empty_cache()
-    prompts = request_lengths()
     page_bytes = 2 * model.num_kv_layers * PAGE * model.hkv * cfg.head_dim * 2
     free, _ = torch.cuda.mem_get_info(dev)
     pool_pages = int((free - 8 * 2**30) // page_bytes)
-    if args.batch:
-        bs = args.batch
+    if radix:
+        prompts = np.full(RADIX_REQS, RADIX_PREFIX + RADIX_SUFFIX)
+        shared_pages = RADIX_GROUPS * RADIX_PREFIX // PAGE
+        own_pages = (RADIX_SUFFIX + RADIX_OUT) // PAGE
+        fit = (pool_pages - 1 - shared_pages) // own_pages
+        bs = args.batch or int(max(0, min(RADIX_REQS, fit)))
     else:
-        bs = min(admit(prompts, pool_pages - 1), NUM_REQS)
+        prompts = request_lengths()
+        bs = args.batch or min(admit(prompts, pool_pages - 1), NUM_REQS)
     bs = agree_min(bs, world, dev)  # tensor parallel: every rank runs the same batch
     prompts = prompts[:bs]
-    full = prompts + OUT_TOKENS
+    full = prompts + out_tokens
     pages_per = (full + PAGE - 1) // PAGE
-    num_pages = min(pool_pages, int(pages_per.sum()) + 1)
+    if radix:
+        num_pages = min(pool_pages, shared_pages + bs * own_pages + 1)
+    else:
+        num_pages = min(pool_pages, int(pages_per.sum()) + 1)
     kv = model.make_kv_cache(num_pages, PAGE, zero=False)
     kv._kv_buffer.normal_(generator=torch.Generator(device=dev).manual_seed(SEED + 1))
     kv._kv_buffer[:, :, 0].zero_()
     max_len = int(full.max())
     eng = DecodeEngine(model, kv, bs, max_len, PAGE, max_reqs=bs)
     perm = torch.randperm(num_pages - 1, generator=torch.Generator().manual_seed(SEED + 2)) + 1
-    off = 0
-    for r in range(bs):
-        n = int(pages_per[r])
-        eng.assign_pages(r + 1, perm[off:off + n].to(dev))
-        off += n
+    shared_hits = 0
+    if radix:
+        shared_hits = radix_page_tables(eng, perm.numpy(), bs, cfg.vocab, dev)
+    else:
+        off = 0
+        for r in range(bs):
+            n = int(pages_per[r])
+            eng.assign_pages(r + 1, perm[off:off + n].to(dev))
+            off += n
     rows = torch.arange(1, bs + 1, dtype=torch.int32, device=dev)
     steps_total = args.warmup + args.steps
-    base_seq = torch.as_tensor(prompts + MID, dtype=torch.int32, device=dev)
+    base_seq = torch.as_tensor(prompts + mid, dtype=torch.int32, device=dev)
     sched = torch.stack([base_seq + 1 + s for s in range(steps_total + 1)])  # incl. new token
     eng.ids.copy_(torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32))
     eng.set_batch(rows, sched[0])
@@ -359,7 +434,11 @@ def run_b200(args) -> None:
 
     # roofline of the dominant kernel: layer-0 attention of the same batch, timed alone
     ctx = (sched[args.warmup + args.steps - 1]).to(torch.int64)
-    attn_bytes = int(ctx.sum().item()) * model.hkv * cfg.head_dim * 2 * 2 \
+    # context tokens whose K/V must come from HBM: with the radix workload a group's shared
+    # prefix pages are one copy read by all of its rows, so they count once per group
+    groups_present = min(bs, RADIX_GROUPS) if radix else 0
+    kv_tokens = int(ctx.sum().item()) - (bs - groups_present) * RADIX_PREFIX * int(radix)
+    attn_bytes = kv_tokens * model.hkv * cfg.head_dim * 2 * 2 \
         + 2 * bs * model.hq * cfg.head_dim * 2
     q = torch.randn(bs, model.hq, cfg.head_dim, device=dev).to(torch.bfloat16)
     kc, vc = kv.slots(0)
@@ -390,7 +469,7 @@ def run_b200(args) -> None:
     weight_bytes = sum(t.numel() * 2 for lw in model.layers.values()
                        for t in (lw.qkv, lw.o, lw.gate_up, lw.down)) * cfg.loop_steps \
         + model.lm_head_w.numel() * 2 + bs * cfg.hidden * 2
-    kv_bytes = int(ctx.sum().item()) * model.num_kv_layers * model.hkv * cfg.head_dim * 4
+    kv_bytes = kv_tokens * model.num_kv_layers * model.hkv * cfg.head_dim * 4
     step_bytes = weight_bytes + kv_bytes
     peak, peak_kind = peaks()
     # NVLink bytes each rank sends per step: 2 fused all-reduces per layer and loop step
@@ -408,26 +487,34 @@ def run_b200(args) -> None:
     # launch of the same kernel on a one-layer case (profiles/paged_attention_*.md),
     # per context token, scaled by this batch's context tokens (traffic grows with them).
     traffic = ATTN_DRAM_BYTES_PER_CTX_TOKEN * model.hkv / cfg.kv_heads * int(ctx.sum().item())
+    if radix:
+        traffic = None  # shared prefix pages are L2 hits for most rows: no per-token constant
+    metric, workload = (RADIX_METRIC, RADIX_WORKLOAD) if radix else (METRIC, WORKLOAD)
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_max / args.steps,
         "p50_tpot_ms": statistics.median(step_ms), "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: seeded random-init weights, random KV contents and token ids",
-        "config": {"workload": WORKLOAD, "model": "Ouro-1.4B architecture (random init)",
+        "config": {"workload": workload,
+                   "model": ("Ouro-2.6B" if radix else "Ouro-1.4B") + " architecture (random init)",
                    "global_batch": bs, "running_batch_per_gpu": bs,
                    "mean_context": round(mean_ctx, 1), "kv_pool_pages": num_pages,
                    "page_size": PAGE, "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2 (each step streams the KV pool, ~%d GB)"
                          % (step_bytes // 10**9)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": round(traffic),
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None if traffic is None else round(traffic),
                      "kernel": "paged_attention (layer-0 decode, whole running batch)",
                      "peak_kind": peak_kind,
                      "step_frac": round(step_bytes / step_s / 1e9 / peak, 4),
                      "step_bytes": step_bytes, "nvlink_bytes_per_step": nvlink_bytes,
                      "combined_step_frac": round(ideal_s / step_s, 4)},
+        **({"radix": {"shared_prefix_tokens_matched": shared_hits,
+                      "kv_tokens_unique": kv_tokens,
+                      "kv_tokens_per_row_sum": int(ctx.sum().item())}} if radix else {}),
         "e2e": {"value": tokens / (e2e_max / 1000.0), "unit": "tok/s",
                 "h2d_bytes_per_step": 2 * bs * 4, "d2h_bytes_per_step": bs * 4},
         "gpu_launches": eng.launches_per_step * args.steps,
@@ -438,8 +525,13 @@ def run_b200(args) -> None:
         line["device_error_word"] = err  # a bounded in-kernel wait gave up or an index was bad
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
-            line["cpu_baseline"] = cpu_decode_sample(args.cpu_steps, args.cpu_batch,
-                                                     os.cpu_count() or 1)
+            if radix:
+                line["cpu_baseline"] = cpu_decode_sample(
+                    1, 1, os.cpu_count() or 1, OURO_26B,
+                    np.array([RADIX_PREFIX + RADIX_SUFFIX + RADIX_MID]), "Ouro-2.6B")
+            else:
+                line["cpu_baseline"] = cpu_decode_sample(args.cpu_steps, args.cpu_batch,
+                                                         os.cpu_count() or 1)
             line["cpu_baseline"].pop("p50_step_s", None)
         except Exception as exc:  # reported, never silently dropped
             line["cpu_baseline"] = {"value": None, "error": repr(exc)}
@@ -752,11 +844,12 @@ def main() -> None:
     ap.add_argument("--cpu-batch", type=int, default=2)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
-    ap.add_argument("--workload", choices=["cdb", "cb"], default="cdb",
-                    help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB")
+    ap.add_argument("--workload", choices=["cdb", "cb", "radix"], default="cdb",
+                    help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB; "
+                         "radix: configs[3] (Ouro-2.6B, shared prefixes)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.workload == "cdb" else 40
+        args.steps = {"cdb": 20, "cb": 40, "radix": 10}[args.workload]
     if args.steps < 1:
         ap.error("--steps must be >= 1")
     if args.warmup < 3:
@@ -766,7 +859,7 @@ def main() -> None:
     elif args.workload == "cdb":
         run_b200_cdb(args)
     else:
-        run_b200(args)
+        run_b200(args)  # cb and radix
 
 
 if __name__ == "__main__":
