@@ -91,13 +91,20 @@ def bench_attention(args, ops) -> dict:
     else:
         ctx = torch.full((rows,), args.ctx)
     pages_per = (ctx + page - 1) // page
-    num_pages = int(pages_per.sum()) + 1
+    # with --shared-prefix P, row r's first P tokens are group (r % groups)'s shared pages
+    sp = args.shared_prefix // page if args.shared_prefix else 0
+    groups = args.groups if sp else 0
+    own = pages_per - sp
+    num_pages = int(own.sum()) + groups * sp + 1
     perm = torch.randperm(num_pages - 1, generator=gen) + 1
     table = torch.zeros(rows, int(pages_per.max()), dtype=torch.int32)
-    off = 0
+    off = groups * sp
     for r in range(rows):
-        n = int(pages_per[r])
-        table[r, :n] = perm[off:off + n].to(torch.int32)
+        if sp:
+            g = r % groups
+            table[r, :sp] = perm[g * sp:(g + 1) * sp].to(torch.int32)
+        n = int(own[r])
+        table[r, sp:sp + n] = perm[off:off + n].to(torch.int32)
         off += n
     slots = num_pages * page
     kv = torch.empty(2, slots, hkv, d, dtype=torch.bfloat16, device=dev).normal_()
@@ -114,12 +121,15 @@ def bench_attention(args, ops) -> dict:
                             hkv, out=out)
 
     us = _time_graph(launch, args.reps)
-    kv_bytes = int(ctx.sum()) * hkv * d * 2 * 2
+    kv_tokens = int(ctx.sum()) - (rows - min(rows, groups)) * sp * page  # shared pages once
+    kv_bytes = kv_tokens * hkv * d * 2 * 2
     nbytes = kv_bytes + rows * hq * d * 2 * 2
     return {"kernel": "paged_attention", "rows": rows, "mean_ctx": float(ctx.float().mean()),
             "heads": hq, "kv_heads": hkv, "head_dim": d, "page_size": page,
             "kv_layer_bytes": slots * hkv * d * 2 * 2, "algorithmic_bytes": nbytes,
-            "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1)}
+            "shared_prefix": sp * page, "groups": groups,
+            "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
+            "per_row_GBps": round((int(ctx.sum()) * hkv * d * 4 + rows * hq * d * 4) / us / 1e3, 1)}
 
 
 def tp_shape(name: str, tp: int) -> tuple[int, int, bool]:
@@ -249,6 +259,9 @@ def main(argv=None) -> None:
     at.add_argument("--page", type=int, default=16)
     at.add_argument("--reps", type=int, default=20)
     at.add_argument("--seed", type=int, default=0)
+    at.add_argument("--shared-prefix", type=int, default=0,
+                    help="tokens of each row's context shared with its group (page multiple)")
+    at.add_argument("--groups", type=int, default=4, help="prefix groups (rows interleaved)")
     gm = sub.add_parser("gemm")
     gm.add_argument("--tokens", type=int, default=143)
     gm.add_argument("--shape", nargs="+", default=["qkv", "o", "gate_up", "down"],
