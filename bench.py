@@ -169,8 +169,13 @@ class ClockSampler:
 
     def summary(self) -> dict:
         self.file.flush()
+        return self.parse(Path(self.file.name).read_text())
+
+    @staticmethod
+    def parse(text: str) -> dict:
+        """Median SM clock, max clock and the throttle reasons seen in nvidia-smi CSV rows."""
         rows = []
-        for line in Path(self.file.name).read_text().splitlines():
+        for line in text.splitlines():
             parts = [p.strip() for p in line.split(",")]
             if len(parts) == 7:
                 rows.append(parts)

@@ -87,25 +87,14 @@ def test_radix_page_tables_share_each_groups_prefix() -> None:
     assert all(not (a & b) for i, a in enumerate(prefixes) for b in prefixes[i + 1:])
 
 
-def test_clock_summary_reads_samples(tmp_path) -> None:
-    s = B.ClockSampler.__new__(B.ClockSampler)
-
-    class _F:
-        name = str(tmp_path / "clocks.csv")
-
-        def flush(self) -> None:
-            pass
-
-    s.file = _F()
-    Path(s.file.name).write_text(
+def test_clock_summary_reads_samples() -> None:
+    got = B.ClockSampler.parse(
         "1965, 1965, 700.1, Not Active, Not Active, Not Active, Not Active\n"
         "1900, 1965, 990.0, Not Active, Not Active, Not Active, Active\n"
         "1965, 1965, 800.0, Not Active, Not Active, Not Active, Not Active\n")
-    got = s.summary()
     assert got == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
                    "samples": 3}
-    Path(s.file.name).write_text("")
-    assert s.summary()["reasons"] == ["unsampled"]
+    assert B.ClockSampler.parse("")["reasons"] == ["unsampled"]
 
 
 def test_admission_counts_whole_pages() -> None:
