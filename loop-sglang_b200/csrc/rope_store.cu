@@ -2,13 +2,16 @@
 // the scatter of the rotated k and the v rows into their paged KV slots.
 //
 // One warp per (token, head) of the q heads and the k heads; the warp of k head
-// j also copies v head j. Lane l rotates the pairs (i, i + D/2) for
-// i = 2l, 2l+1 (+64 per pass) in fp32 and rounds once, as the FlashInfer kernel
-// the reference calls does (pos_enc.cuh vec_apply_llama_rope_cos_sin).
+// j also stores k head j and copies v head j into the slot. Lane l rotates the
+// pairs (i, i + D/2) for i = 2l, 2l+1 (+64 per pass) in fp32 and rounds once, as
+// the FlashInfer kernel the reference calls does (pos_enc.cuh
+// vec_apply_llama_rope_cos_sin).
 #include "common.cuh"
 
 namespace lsb {
 namespace {
+
+constexpr int kMaxPairs = 4;  // bf16 pairs per lane of a row: head_dim <= 256
 
 __global__ void rope_store_kernel(bf16* __restrict__ qkv, int64_t qkv_stride,
                                   const int32_t* __restrict__ positions,
@@ -25,13 +28,36 @@ __global__ void rope_store_kernel(bf16* __restrict__ qkv, int64_t qkv_stride,
   const int64_t t = item / heads;
   const int h = static_cast<int>(item % heads);
   const int half = head_dim >> 1;
+  // Everything that does not depend on the position is fetched with it: the slot of a k
+  // head and its v row, so a k head costs one memory round trip before its stores.
+  const bool kv_head = h >= hq && k_cache != nullptr;
   int pos = positions[t];
+  int64_t loc = kv_head ? static_cast<int64_t>(out_loc[t]) : 0;
+  bf16* row = qkv + t * qkv_stride + static_cast<int64_t>(h) * head_dim;
+  bf162 vv[kMaxPairs];
+  if (kv_head) {
+    const bf16* vrow = qkv + t * qkv_stride + static_cast<int64_t>(hq + hkv + (h - hq)) * head_dim;
+#pragma unroll
+    for (int k = 0; k < kMaxPairs; ++k) {
+      const int i = 2 * lane + 64 * k;
+      if (i < head_dim) vv[k] = *reinterpret_cast<const bf162*>(vrow + i);
+    }
+  }
   if (pos < 0 || pos >= max_pos) {
     if (lane == 0 && error_flag) atomicOr(error_flag, LSB_DEVERR_POSITION);
     pos = 0;
   }
+  bool store = false;
+  if (kv_head && loc != 0) {  // slot 0 is the padding slot and is never written
+    if (loc < 0 || loc >= num_slots) {
+      if (lane == 0 && error_flag) atomicOr(error_flag, LSB_DEVERR_SLOT);
+    } else {
+      store = true;
+    }
+  }
+  const int kh = h - hq;
+  bf16* kdst = store ? k_cache + loc * slot_stride + static_cast<int64_t>(kh) * head_dim : nullptr;
   const float* cs = cos_sin + static_cast<int64_t>(pos) * head_dim;
-  bf16* row = qkv + t * qkv_stride + static_cast<int64_t>(h) * head_dim;
   for (int i = 2 * lane; i < half; i += 64) {
     const float2 c = *reinterpret_cast<const float2*>(cs + i);
     const float2 s = *reinterpret_cast<const float2*>(cs + half + i);
@@ -39,25 +65,21 @@ __global__ void rope_store_kernel(bf16* __restrict__ qkv, int64_t qkv_stride,
     const float2 x2 = __bfloat1622float2(*reinterpret_cast<const bf162*>(row + half + i));
     const float2 y1 = make_float2(x1.x * c.x - x2.x * s.x, x1.y * c.y - x2.y * s.y);
     const float2 y2 = make_float2(x2.x * c.x + x1.x * s.x, x2.y * c.y + x1.y * s.y);
-    *reinterpret_cast<bf162*>(row + i) = __floats2bfloat162_rn(y1.x, y1.y);
-    *reinterpret_cast<bf162*>(row + half + i) = __floats2bfloat162_rn(y2.x, y2.y);
+    const bf162 r1 = __floats2bfloat162_rn(y1.x, y1.y);
+    const bf162 r2 = __floats2bfloat162_rn(y2.x, y2.y);
+    *reinterpret_cast<bf162*>(row + i) = r1;
+    *reinterpret_cast<bf162*>(row + half + i) = r2;
+    if (store) {  // the rotated k goes to its slot straight from registers
+      *reinterpret_cast<bf162*>(kdst + i) = r1;
+      *reinterpret_cast<bf162*>(kdst + half + i) = r2;
+    }
   }
-  if (h < hq || k_cache == nullptr) return;
-  // k head (h - hq): store the rotated k row and the matching v row.
-  const int kh = h - hq;
-  const int64_t loc = out_loc[t];
-  if (loc == 0) return;  // padding slot, never written
-  if (loc < 0 || loc >= num_slots) {
-    if (lane == 0 && error_flag) atomicOr(error_flag, LSB_DEVERR_SLOT);
-    return;
-  }
-  __syncwarp();
-  const bf16* vrow = qkv + t * qkv_stride + static_cast<int64_t>(hq + hkv + kh) * head_dim;
-  bf16* kdst = k_cache + loc * slot_stride + static_cast<int64_t>(kh) * head_dim;
+  if (!store) return;
   bf16* vdst = v_cache + loc * slot_stride + static_cast<int64_t>(kh) * head_dim;
-  for (int i = 2 * lane; i < head_dim; i += 64) {
-    *reinterpret_cast<bf162*>(kdst + i) = *reinterpret_cast<const bf162*>(row + i);
-    *reinterpret_cast<bf162*>(vdst + i) = *reinterpret_cast<const bf162*>(vrow + i);
+#pragma unroll
+  for (int k = 0; k < kMaxPairs; ++k) {
+    const int i = 2 * lane + 64 * k;
+    if (i < head_dim) *reinterpret_cast<bf162*>(vdst + i) = vv[k];
   }
 }
 
@@ -101,7 +123,7 @@ extern "C" int lsb_rope_store_kv(void* qkv, int64_t qkv_stride, const int32_t* p
                                  const int32_t* out_loc, int64_t tokens, int32_t hq,
                                  int32_t hkv, int32_t head_dim, void* stream) {
   LSB_REQUIRE(qkv && positions && cos_sin, "null pointer");
-  LSB_REQUIRE(head_dim % 4 == 0 && head_dim > 0 && hq > 0 && hkv >= 0 &&
+  LSB_REQUIRE(head_dim % 4 == 0 && head_dim > 0 && head_dim <= 256 && hq > 0 && hkv >= 0 &&
                   (hkv == 0 || hq % hkv == 0),
               "rope_store_kv: bad head shape hq=%d hkv=%d head_dim=%d", hq, hkv, head_dim);
   LSB_REQUIRE(hkv > 0 || !k_cache, "rope_store_kv: a KV store needs k/v heads");

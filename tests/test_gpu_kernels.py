@@ -94,7 +94,18 @@ def test_rope_store(hq: int, hkv: int, d: int) -> None:
     assert torch.equal(vc_d.cpu(), ev), "v rows are copied bit-exactly, slot 0 untouched"
     close(kc_d, ek, rtol=1e-2, atol=1e-2)
     assert torch.equal(kc_d[0].cpu(), kc[0])
+    # the stored k is the rotated k left in the QKV output, bit for bit
+    live = (loc != 0).nonzero().flatten()
+    assert torch.equal(kc_d[loc[live].long()].cpu(), qkv_d[live, hq * d:(hq + hkv) * d].cpu())
     no_device_errors()
+    # a slot outside the pool is skipped and flagged; the other rows are stored as before
+    bad = loc.clone()
+    bad[2] = slots + 3
+    kc2, vc2 = kc.to(DEV), vc.to(DEV)
+    ops.rope_store_kv(qkv.to(DEV), pos.to(DEV), cs.to(DEV), hq, hkv, d, kc2, vc2, bad.to(DEV))
+    assert ops.device_error_word(reset=True) & 2
+    keep = [r for r in range(t) if r != 2 and int(loc[r]) != 0]
+    assert torch.equal(vc2[loc[keep].long()].cpu(), ev[loc[keep].long()])
 
 
 def test_store_kv_exact_and_bounds() -> None:
