@@ -257,6 +257,8 @@ def test_paged_attention_full_size_property() -> None:
 
 GEMM_SHAPES = [(1, 128, 64), (3, 256, 128), (16, 384, 512), (144, 6144, 2048), (300, 256, 256),
                (8, 2048, 5632), (256, 1024, 2048), (40, 11264, 2048),
+               # more than 256 tokens: two or more token tiles (CDB batch; a TP=2 rank's rows)
+               (263, 6144, 2048), (512, 3072, 2048), (263, 2048, 5632),
                # ragged N and K (Huginn: H = 5280, QKV N = 15840; tiny shapes below 64 / 128)
                (7, 288, 96), (33, 15840, 5280), (5, 100, 40), (130, 5280, 10560)]
 
@@ -274,7 +276,7 @@ def test_gemm(m: int, n: int, k: int) -> None:
 
 
 @pytest.mark.parametrize("epi", ["bias", "bias_after_round", "swiglu"])
-@pytest.mark.parametrize("m", [5, 144])
+@pytest.mark.parametrize("m", [5, 144, 263])
 def test_gemm_epilogues(epi: str, m: int) -> None:
     g = gen(m)
     k, n = 512, 1024
