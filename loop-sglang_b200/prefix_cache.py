@@ -83,8 +83,11 @@ class RadixPrefixCache:
     def __del__(self) -> None:
         tree = getattr(self, "_tree", None)
         if tree is not None and tree.value:
-            _lib.lib().lsb_radix_destroy(tree)
             self._tree = None
+            try:
+                _lib.lib().lsb_radix_destroy(tree)
+            except Exception:  # interpreter shutdown: the library may already be unloaded
+                pass
 
     # -- the BasePrefixCache interface (kvcache/base.py:86-154) --
 
