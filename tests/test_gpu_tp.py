@@ -77,7 +77,10 @@ def _worker(rank: int, world: int, port: int, errq) -> None:
             assert torch.equal(got.cpu(), torch.cat(parts)), f"all_gather call {it}"
 
         # fused row-parallel GEMM + all-reduce (o_proj / down_proj shards, ragged shapes, bias)
-        shapes = [(143, 2048, 2048), (143, 2048, 5632), (1, 2048, 2048), (33, 200, 192), (256, 2048, 512)]
+        # (1100, 2048, 2048): more rows than the communicator's buffer takes at once (512 x
+        # 2048), so the call runs as several complete launches of resident tiles
+        shapes = [(143, 2048, 2048), (143, 2048, 5632), (1, 2048, 2048), (33, 200, 192),
+                  (256, 2048, 512), (1100, 2048, 2048)]
         for it in range(2):
             for (m, n, k_full) in shapes:
                 k = k_full // world
