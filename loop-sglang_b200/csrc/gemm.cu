@@ -594,14 +594,16 @@ size_t smem_for(int stages, int stage_bytes) {
 // cluster left for a second wave would double the kernel's time.
 Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   Plan pl;
-  // tokens per tile: up to 256 tokens one tile; beyond that, balanced tiles of at most 96
-  // (263 tokens -> 3 x 96, 512 -> 6 x 96). Past one tile every weight tile is read again per
-  // token tile anyway (from L2), and narrow tiles let two or three CTAs share an SM, which
-  // evens out the waves: the Ouro layer's four GEMMs took 64.4 us at 263 tokens as 2 x 144
-  // and 57.4 us as 3 x 96; 63.5 -> 57.7 us at 512 tokens of a TP=2 rank. A single-wave plan
-  // (the fused all-reduce, whose CTAs must all be resident) keeps tiles of up to 256 tokens:
-  // its caller sizes each launch's rows for 256-token tiles on one CTA per SM.
-  const int64_t m_tiles = (M > 256 && !single_wave) ? (M + 95) / 96 : (M + 255) / 256;
+  // tokens per tile: up to 256 tokens one tile; for decode batches of 257-512 tokens,
+  // balanced tiles of at most 96 (263 -> 3 x 96, 512 -> 6 x 96): past one tile every weight
+  // tile is read again per token tile anyway (from L2), and narrow tiles let two or three
+  // CTAs share an SM, which evens out the waves (the Ouro layer's four GEMMs: 64.4 us at 263
+  // tokens as 2 x 144, 57.4 us as 3 x 96; 63.5 -> 57.7 us at 512 tokens of a TP=2 rank).
+  // Larger token counts (prefill, tensor-bound) keep 256-token tiles, which read each weight
+  // tile fewest times. A single-wave plan (the fused all-reduce, whose CTAs must all be
+  // resident) keeps 256-token tiles too: its caller sizes each launch's rows for them.
+  const bool narrow = M > 256 && M <= 512 && !single_wave;
+  const int64_t m_tiles = narrow ? (M + 95) / 96 : (M + 255) / 256;
   int64_t bn = (((M + m_tiles - 1) / m_tiles + 15) / 16) * 16;
   if (bn > 256) bn = 256;
   if (bn < 16) bn = 16;
