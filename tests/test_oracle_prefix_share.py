@@ -5,7 +5,6 @@ backend through the golden fixtures)."""
 
 from __future__ import annotations
 
-import numpy as np
 import torch
 
 from oracle import ops as O
