@@ -21,7 +21,8 @@ What runs is the reference's own code:
   small safetensors checkpoint, once per rank of two world sizes;
 * its ``RadixPrefixCache`` on a seeded sequence of matches, inserts, locks and
   evictions (page sizes 1 and 4);
-* its two KV pools' retraction snapshots (``get_cpu_copy`` / ``load_cpu_copy``).
+* its two KV pools' retraction snapshots (``get_cpu_copy`` / ``load_cpu_copy``);
+* BASELINE configs[0] (the tiny Ouro model, 4 x 128-token prompts, 32 greedy tokens).
 
 Each fixture stores inputs and outputs; ``tests/test_oracle_golden.py`` checks
 that the oracle reproduces them (integers exactly, fp32 to 1e-5).
@@ -736,6 +737,57 @@ def kv_snapshot_case(out_dir):
     print("wrote kv_snapshot")
 
 
+# ---------------------------------------------------------------------------
+# the tiny Ouro model the reference runs on the CPU
+# ---------------------------------------------------------------------------
+
+C1 = LoopedConfig(arch="ouro", hidden=512, heads=8, kv_heads=8, head_dim=64, intermediate=1408,
+                  vocab=32000, num_core_layers=4, loop_steps=4, rope_theta=10000.0,
+                  max_position=512)
+
+
+def c1_case(out_dir, decode_steps=32, seed=7):
+    """configs[0] through the reference model on the CPU in fp32: 4 requests with prompts
+    of 128 uniform-random ids, one prefill, then 32 greedy decode steps at full depth over
+    depth-indexed KV in 16-token pages. Records every step's batch metadata and input ids,
+    the greedy tokens with their top-2 logit margins, and the full logits of the prefill
+    and of the last step (the other steps' logits are not kept: 0.5 MB each)."""
+    weights = make_weights(C1, seed, dtype=torch.float32, gate_bias=0.0)
+    run = RefRun(C1, weights, "depth_indexed", 16, num_pages=64, max_reqs=8, max_len=192)
+    prompts = np.random.default_rng(seed).integers(0, C1.vocab, (4, 128)).astype(np.int32)
+    rows = [1, 2, 3, 4]
+    for r in rows:
+        run.allocate(r, prompts.shape[1])
+    ids = torch.from_numpy(prompts.reshape(-1).copy())
+    fb, logits = run.run(run.batch(rows, [prompts.shape[1]] * 4, "prefill"), ids)
+    rec: dict[str, np.ndarray] = {"seed": np.array(seed), "page_size": np.array(16),
+                                  "prefill_ids": ids.numpy(), "prefill_logits": logits.numpy()}
+    for k, v in snapshot_meta(fb).items():
+        rec[f"prefill_{k}"] = v
+
+    def top2(lg):
+        v = torch.topk(lg, 2, dim=-1).values
+        return torch.argmax(lg, dim=-1).to(torch.int32), (v[:, 0] - v[:, 1]).numpy()
+
+    tokens, margin = top2(logits)
+    all_tokens, margins = [tokens.numpy()], [margin]
+    for step in range(decode_steps):
+        for r in rows:
+            run.allocate(r, run.seq_lens[r] + 1)
+        fb, logits = run.run(run.batch(rows, [1] * 4, "decode"), tokens)
+        rec[f"step{step}_ids"] = tokens.numpy()
+        for k, v in snapshot_meta(fb).items():
+            rec[f"step{step}_{k}"] = v
+        tokens, margin = top2(logits)
+        all_tokens.append(tokens.numpy())
+        margins.append(margin)
+    rec["last_logits"] = logits.numpy()
+    rec["tokens"] = np.stack(all_tokens)
+    rec["margins"] = np.stack(margins).astype(np.float32)
+    np.savez_compressed(out_dir / "c1_ouro_tiny.npz", **rec)
+    print(f"wrote c1_ouro_tiny: {decode_steps} decode steps")
+
+
 OURO_TINY = LoopedConfig(arch="ouro", hidden=128, heads=4, kv_heads=4, head_dim=32,
                          intermediate=256, vocab=512, num_core_layers=2, loop_steps=3,
                          rope_theta=10000.0, max_position=256)
@@ -762,6 +814,7 @@ def main() -> None:
     tp_shard_case(out)
     radix_case(out)
     kv_snapshot_case(out)
+    c1_case(out)
     last_exited_case("last_exited_huginn_layout", 8, 2, 6, 3, 12, out)
     last_exited_case("last_exited_ouro_layout", 6, 0, 6, 4, 24, out)
     model_case("ouro_cb_depth_indexed", OURO_TINY, "depth_indexed", 1, PROMPTS, 3, 4, out)
