@@ -20,6 +20,7 @@ Modules:
   model   -- Ouro / Huginn looped decoders built from ``ops`` over a paged KV pool.
   cdb     -- continuous-depth-batching exit routing.
   kvsnap  -- retraction snapshots of both KV pools (the reference's byte layout).
+  radix   -- the radix prefix tree (match, split, insert, lock, evict).
   prefix_share -- attention over shared prefix pages split into per-group prefix and
              per-row suffix parts (the specification of a prefix-sharing pass).
 """
