@@ -66,7 +66,7 @@ NVLINK_GBS = 770.0  # measured peer-copy bandwidth per direction on this pool's 
 
 
 # Measured DRAM traffic of the decode attention kernel per context token (K+V of 16
-# heads x 128 = 8192 algorithmic bytes), from the ncu capture in profiles/.
+# heads x 128 = 8192 algorithmic bytes), from an ncu capture of a one-layer case.
 ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8362.3
 
 
@@ -189,6 +189,119 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# ------------------------------------------------------------- parity --
+
+PARITY_PROMPTS = (48, 80, 112, 160)
+PARITY_DECODE = 3
+
+
+def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict | None:
+    """Greedy tokens of the benchmarked model object (same weights, same kernels, same
+    tensor-parallel split) against the CPU oracle on the same inputs.
+
+    4 requests with prompts of 48-160 random ids are prefilled at full depth into a fresh
+    small KV pool of the model's own policy, then decoded for 3 steps, each step fed the
+    CUDA path's own greedy tokens; the oracle (bf16 rounding points) runs the same
+    prefill and steps on rank 0. A token agrees when the argmaxes match; it is a near tie
+    when they differ but the oracle's logit of the CUDA path's token is within 2e-2 x
+    max |logit| of its maximum (bf16 reduction order may take either); anything else is
+    a mismatch. Collective over the ranks: every rank runs the CUDA part.
+    """
+    from oracle import model as om
+
+    from loop_sglang_b200.model import DeviceBatch
+
+    dev = model.device
+    cfg = model.cfg
+    policy = model.policy
+    page = 1 if policy == "last_exited" else PAGE
+    g = torch.Generator().manual_seed(SEED + 11)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g, dtype=torch.int32)
+               for n in PARITY_PROMPTS]
+    b = len(prompts)
+    span = max(PARITY_PROMPTS) + PARITY_DECODE + 1
+    pages_per = (span + page - 1) // page
+    table = (1 + torch.arange(b).view(-1, 1) * pages_per + torch.arange(pages_per)).to(torch.int32)
+    num_pages = b * pages_per + 1
+    lens = torch.tensor(PARITY_PROMPTS, dtype=torch.int32)
+
+    def batch(step: int, ids: torch.Tensor):
+        if step < 0:
+            pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in PARITY_PROMPTS])
+            rows = torch.cat([torch.full((n,), r) for r, n in enumerate(PARITY_PROMPTS)])
+            seq, cu = lens.clone(), torch.zeros(b + 1, dtype=torch.int32)
+            cu[1:] = torch.cumsum(lens, 0)
+        else:
+            pos, rows = lens + step, torch.arange(b)
+            seq, cu = lens + step + 1, torch.arange(b + 1, dtype=torch.int32)
+        loc = (table[rows, (pos // page).long()] * page + pos % page).to(torch.int32)
+        return om.Batch(ids.to(torch.int32), pos.to(torch.int32), loc, table.clone(),
+                        seq.to(torch.int32), cu, step < 0)
+
+    kv = model.make_kv_cache(num_pages, page)
+    ids = torch.cat(prompts)
+    got, fed = [], []
+    for step in range(-1, PARITY_DECODE):
+        ob = batch(step, ids)
+        db = DeviceBatch(ob.input_ids.to(dev), ob.positions.to(dev), ob.out_loc.to(dev),
+                         ob.page_table.to(dev), ob.cache_seqlens.to(dev),
+                         ob.cu_seqlens_q.to(dev), ob.is_prefill, max_seqlen=pages_per * page)
+        if policy == "last_exited":
+            kv.reserve_versions(db.out_loc)
+        logits = model.forward(db, kv).float().cpu()
+        got.append(logits)
+        fed.append(ids)
+        ids = logits.argmax(-1).to(torch.int32)
+    del kv
+    if rank != 0 or cpu_weights is None:
+        return None
+    ocfg = om.LoopedConfig(**cfg.__dict__)
+    oracle = om.LoopedModel(ocfg, om.with_fp32_matrices(cpu_weights), policy)
+    if policy == "last_exited":
+        pool = om.SlotKVPool(oracle.slot_layout(), num_pages, cfg.kv_heads, cfg.head_dim,
+                             torch.bfloat16)
+    else:
+        pool = om.PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads,
+                              cfg.head_dim, torch.bfloat16)
+    counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
+    worst = 0.0
+    for i, step in enumerate(range(-1, PARITY_DECODE)):
+        ob = batch(step, fed[i])
+        if policy == "last_exited":
+            pool.versions.reserve(ob.out_loc.numpy())
+        ref = oracle.forward(ob, pool).float()
+        scale = ref.abs().max(-1).values
+        worst = max(worst, float((got[i] - ref).abs().max() / scale.max()))
+        gi, ri = got[i].argmax(-1), ref.argmax(-1)
+        for r in range(b):
+            if int(gi[r]) == int(ri[r]):
+                counts["agree"] += 1
+            elif ref[r, gi[r]] >= ref[r, ri[r]] - 2e-2 * scale[r]:
+                counts["near_tie"] += 1
+            else:
+                counts["mismatch"] += 1
+    n = sum(counts.values())
+    return {"agree": round(counts["agree"] / n, 4), "tokens": n, "rows": b,
+            "near_ties": counts["near_tie"], "mismatches": counts["mismatch"],
+            "max_logit_rel_err": round(worst, 5), "tp": world, "policy": policy,
+            "vs": "CPU oracle, bf16 rounding points, same weights and inputs",
+            "sample": (f"{b} requests, prompts {list(PARITY_PROMPTS)} random ids, full-depth "
+                       f"prefill + {PARITY_DECODE} greedy decode steps through the benchmarked "
+                       "model object")}
+
+
+def rank_info(world: int, rank: int, local: int, dev) -> list | None:
+    """(rank, local rank, device name, PCI bus id) of every rank that took part."""
+    p = torch.cuda.get_device_properties(dev)
+    me = [rank, local, p.name, f"{getattr(p, 'pci_domain_id', 0):04x}:"
+          f"{getattr(p, 'pci_bus_id', 0):02x}:{getattr(p, 'pci_device_id', 0):02x}"]
+    if world == 1:
+        return [me]
+    out: list = [None] * world
+    torch.distributed.all_gather_object(out, me)
+    return out
+
+
 # ---------------------------------------------------------------- CPU side --
 
 def cpu_decode_sample(steps: int, batch: int, threads: int, model_cfg: dict | None = None,
@@ -201,7 +314,7 @@ def cpu_decode_sample(steps: int, batch: int, threads: int, model_cfg: dict | No
     torch.set_num_threads(threads)
     cfg = om.LoopedConfig(**(model_cfg or OURO_14B))
     t0 = time.perf_counter()
-    w = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
+    w = om.with_fp32_matrices(om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16))
     mdl = om.LoopedModel(cfg, w, "depth_indexed")
     ctx = (request_lengths()[:batch] + MID) if contexts is None else np.asarray(contexts)[:batch]
     pages_per = [(int(c) + steps + PAGE) // PAGE for c in ctx]
@@ -240,15 +353,17 @@ def run_reference(args) -> None:
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    # a bounded sample: at most --cpu-steps decode steps (output tokens) of the batch
+    steps = max(1, min(args.steps, args.cpu_steps))
     if args.workload == "cdb":
-        base = cpu_cdb_sample(max(1, args.steps), args.cpu_batch, threads)
+        base = cpu_cdb_sample(steps, args.cpu_batch, threads)
         metric, workload = CDB_METRIC, CDB_WORKLOAD
     elif args.workload == "radix":
-        base = cpu_decode_sample(max(1, min(args.steps, 2)), 1, threads, OURO_26B,
+        base = cpu_decode_sample(min(steps, 2), 1, threads, OURO_26B,
                                  np.array([RADIX_PREFIX + RADIX_SUFFIX + RADIX_MID]), "Ouro-2.6B")
         metric, workload = RADIX_METRIC, RADIX_WORKLOAD
     else:
-        base = cpu_decode_sample(max(1, args.steps), args.cpu_batch, threads)
+        base = cpu_decode_sample(steps, args.cpu_batch, threads)
         metric, workload = METRIC, WORKLOAD
     line = {
         "impl": "reference", "metric": metric, "value": base["value"], "unit": "tok/s",
@@ -351,6 +466,8 @@ def run_b200(args) -> None:
         vocab_local = -(-cfg.vocab // world)
         comm = B200Communicator(rank, world, NUM_REQS * max(cfg.hidden, vocab_local))
     weights = gpu_weights(cfg, dev, SEED)  # same seed on every rank: the same full model
+    cpu_weights = ({k: v.cpu() for k, v in weights.items()}
+                   if rank == 0 and not args.no_parity else None)
     model = LoopedDecoder(cfg, weights, "depth_indexed", dev, comm=comm)
     del weights
     torch.cuda.empty_cache()
@@ -489,8 +606,8 @@ def run_b200(args) -> None:
     ideal_s = max(step_bytes / (peak * 1e9), nvlink_bytes / (NVLINK_GBS * 1e9))
     achieved = attn_bytes / attn_s / 1e9
     # DRAM bytes per launch: ncu's dram__bytes_read.sum + dram__bytes_write.sum of one
-    # launch of the same kernel on a one-layer case (profiles/paged_attention_*.md),
-    # per context token, scaled by this batch's context tokens (traffic grows with them).
+    # launch of the same kernel on a one-layer case, per context token, scaled by this
+    # batch's context tokens (traffic grows with them).
     traffic = ATTN_DRAM_BYTES_PER_CTX_TOKEN * model.hkv / cfg.kv_heads * int(ctx.sum().item())
     if radix:
         traffic = None  # shared prefix pages are L2 hits for most rows: no per-token constant
@@ -528,6 +645,9 @@ def run_b200(args) -> None:
     err = ops.device_error_word(reset=False)
     if err:
         line["device_error_word"] = err  # a bounded in-kernel wait gave up or an index was bad
+    line["ranks"] = rank_info(world, rank, local, dev)
+    if not args.no_parity:
+        line["parity"] = parity_stamp(model, cpu_weights, rank, world)
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
             if radix:
@@ -561,7 +681,7 @@ CDB_OUT_TOKENS = 512
 CDB_MID = 256
 CDB_EXIT_P = (0.15, 0.25, 0.30, 0.30)
 # DRAM bytes per context key of the attention kernel over last-exited versions (scattered
-# 4 KB K and V rows), from the ncu capture in profiles/cdb_step_launches_*.md
+# 4 KB K and V rows), from an ncu capture of that kernel on the CDB step's layout
 CDB_ATTN_DRAM_BYTES_PER_CTX_TOKEN = 8216.1
 CDB_METRIC = ("decode output tok/s, Ouro-1.4B CDB (configs[2]), last-exited KV, TP over the "
               "job's GPUs")
@@ -578,15 +698,17 @@ def cdb_depths(n: int, seed: int) -> np.ndarray:
 
 
 def cpu_cdb_sample(tokens: int, batch: int, threads: int) -> dict:
-    """The oracle on a bounded CDB sample: ``batch`` requests at mean context, each output
-    token = prelude, its prescribed number of loop steps, LM head (shared-KV addressing;
+    """The oracle on a bounded CDB sample: ``batch`` requests at the workload's contexts
+    decode ``tokens`` output tokens each, batched: every token is the prelude of all rows,
+    then loop step s for the rows whose prescribed exit depth exceeds s (the batch shrinks
+    as rows exit), then the LM head and greedy sampling of all rows (shared-KV addressing;
     the per-token arithmetic is the last-exited policy's)."""
     from oracle import model as om
 
     torch.set_num_threads(threads)
     cfg = om.LoopedConfig(**{**OURO_14B, "exit_threshold": 0.2})
     t0 = time.perf_counter()
-    w = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
+    w = om.with_fp32_matrices(om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16))
     mdl = om.LoopedModel(cfg, w, "shared")
     rng = np.random.default_rng(SEED)
     ctx = rng.integers(CDB_PROMPT_RANGE[0], CDB_PROMPT_RANGE[1] + 1, batch) + CDB_MID
@@ -604,26 +726,31 @@ def cpu_cdb_sample(tokens: int, batch: int, threads: int) -> dict:
     depths = cdb_depths(batch * tokens, SEED + 7).reshape(batch, tokens)
     ids = torch.randint(0, cfg.vocab, (batch,), generator=torch.Generator().manual_seed(2),
                         dtype=torch.int32)
+    rows = torch.arange(batch)
     t = time.perf_counter()
-    steps = 0
+    passes = 0
     for k in range(tokens):
-        for b in range(batch):
-            pos = torch.tensor([int(ctx[b]) + k], dtype=torch.int32)
-            loc = table[b, pos.long() // PAGE] * PAGE + pos % PAGE
-            bt = om.Batch(ids[b:b + 1], pos, loc.to(torch.int32), table[b:b + 1], pos + 1,
-                          torch.arange(2, dtype=torch.int32), False)
-            h, _ = mdl.forward_prelude(bt, pool)
-            for step in range(int(depths[b, k])):
-                h = mdl.core_step(h, step, None, bt, pool)
-                steps += 1
-            ids[b] = mdl.lm_head(h, None).float().argmax(-1).to(torch.int32)[0]
+        pos = torch.as_tensor(ctx + k, dtype=torch.int32)
+        loc = (table[rows, pos.long() // PAGE] * PAGE + pos % PAGE).to(torch.int32)
+        full = om.Batch(ids, pos, loc, table, pos + 1, torch.arange(batch + 1, dtype=torch.int32),
+                        False)
+        h, _ = mdl.forward_prelude(full, pool)
+        for step in range(cfg.loop_steps):
+            act = torch.from_numpy(np.nonzero(depths[:, k] > step)[0])
+            if act.numel() == 0:
+                break
+            bt = om.Batch(ids[act], pos[act], loc[act], table[act], pos[act] + 1,
+                          torch.arange(act.numel() + 1, dtype=torch.int32), False)
+            h[act] = mdl.core_step(h[act], step, None, bt, pool)
+            passes += act.numel()
+        ids = mdl.lm_head(h, None).float().argmax(-1).to(torch.int32)
     total = time.perf_counter() - t
     return {"value": batch * tokens / total, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": (f"{batch} requests at context {int(ctx.mean())} (mean), {tokens} output "
-                       f"tokens each ({steps} loop steps at the prescribed exit depths) of "
-                       f"Ouro-1.4B through the CPU oracle in torch bf16/fp32, {threads} "
-                       f"threads; setup {setup:.0f}s untimed"),
-            "p50_step_s": total / max(1, steps)}
+                       f"tokens each, batched ({passes} row loop steps at the prescribed exit "
+                       f"depths) of Ouro-1.4B through the CPU oracle in torch bf16/fp32, "
+                       f"{threads} threads; setup {setup:.0f}s untimed"),
+            "p50_step_s": total / max(1, tokens)}
 
 
 def run_b200_cdb(args) -> None:
@@ -652,6 +779,8 @@ def run_b200_cdb(args) -> None:
         vocab_local = -(-cfg.vocab // world)
         comm = B200Communicator(rank, world, CDB_NUM_REQS * max(cfg.hidden, vocab_local))
     weights = gpu_weights(cfg, dev, SEED)
+    cpu_weights = ({k: v.cpu() for k, v in weights.items()}
+                   if rank == 0 and not args.no_parity else None)
     model = LoopedDecoder(cfg, weights, "last_exited", dev, comm=comm)
     del weights
     torch.cuda.empty_cache()
@@ -820,6 +949,9 @@ def run_b200_cdb(args) -> None:
     err = ops.device_error_word(reset=False)
     if err:
         line["device_error_word"] = err  # a bounded in-kernel wait gave up or an index was bad
+    line["ranks"] = rank_info(world, rank, local, dev)
+    if not args.no_parity:
+        line["parity"] = parity_stamp(model, cpu_weights, rank, world)
     if rank == 0 and world == 1 and not args.no_cpu:
         try:
             line["cpu_baseline"] = cpu_cdb_sample(args.cpu_steps, args.cpu_batch,
@@ -840,21 +972,24 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None,
-                    help="timed steps (default: 20 for cdb, 40 for cb -- a few hundred ms to "
-                         "a second and a half, covered by several clock samples)")
+                    help="timed steps (default: 120 for cdb, 40 for cb, 20 for radix -- each "
+                         "about a second or more, covered by many clock samples)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--batch", type=int, default=0, help="override the admitted batch (debug)")
-    ap.add_argument("--cpu-steps", type=int, default=2)
-    ap.add_argument("--cpu-batch", type=int, default=2)
+    ap.add_argument("--cpu-steps", type=int, default=3,
+                    help="decode steps (CDB: output tokens per request) of the CPU sample")
+    ap.add_argument("--cpu-batch", type=int, default=16, help="requests in the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the parity stamp (greedy tokens vs the CPU oracle)")
     ap.add_argument("--workload", choices=["cdb", "cb", "radix"], default="cdb",
                     help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB; "
                          "radix: configs[3] (Ouro-2.6B, shared prefixes)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"cdb": 20, "cb": 40, "radix": 10}[args.workload]
+        args.steps = {"cdb": 120, "cb": 40, "radix": 20}[args.workload]
     if args.steps < 1:
         ap.error("--steps must be >= 1")
     if args.warmup < 3:

@@ -130,9 +130,11 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
  * static device array of LSB_NOALLOC_ATTENTION_SCRATCH_BYTES per GPU, held
  * until the process exits; calls needing more (see
  * lsb_paged_attention_workspace_size) fail with LSB_ERR_INVALID. All calls on a
- * device share the array: calls that overlap on the GPU race. The first call on
- * a device looks up the array and clears its counters (an async memset on
- * `stream`); make it before any stream capture. Allocates nothing. */
+ * device share the array: calls that overlap on the GPU race. Every call looks
+ * up the array's device address and clears its arrival counters (an async
+ * memset on `stream`) before the kernel, so a call whose bounded wait gave up
+ * leaves nothing stale for the next; the first call on a device may load the
+ * module, so make it before any stream capture. Allocates nothing. */
 #define LSB_NOALLOC_ATTENTION_SCRATCH_BYTES (16 * 1024 * 1024)
 int lsb_paged_attention_noalloc(void* out, int64_t out_stride, const void* q, int64_t q_stride,
                                 const void* k_cache, const void* v_cache, int64_t slot_stride,

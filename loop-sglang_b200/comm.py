@@ -1,114 +1,34 @@
-"""Tensor-parallel communicator plugin stack (python/loopsgl/distributed/{impl,info}.py).
+"""NVLink communicator of a tensor-parallel node, and its plugin for the reference's
+communicator stack (python/loopsgl/distributed/impl.py:16-70).
 
-``DistributedCommunicator`` keeps the reference's contract: a class-level plugin
-list whose last entry serves ``all_reduce(x) -> x`` (in place, returns the same
-tensor) and ``all_gather(x) -> new`` along dim 0 (distributed/impl.py:63-70).
-``TorchDistributedImpl`` is the reference's torch.distributed fallback
-(impl.py:25-41); it is what the multi-process CPU tests (gloo) exercise.
+``B200Communicator`` is the NVLink path (the PyNCCL plugin's place, impl.py:44-60):
+one symmetric device buffer per rank, mapped into every peer with CUDA IPC (handles
+exchanged over the host process group, as the reference exchanges its NCCL unique
+id, kernel/pynccl.py:59-92), and the library's all-reduce, all-gather and fused
+row-parallel GEMM + all-reduce on top.
 
-``B200Communicator`` is the NVLink path (the PyNCCL plugin's place,
-impl.py:44-60): one symmetric device buffer per rank, mapped into every peer
-with CUDA IPC (handles exchanged over the host process group, as the reference
-exchanges its NCCL unique id, kernel/pynccl.py:59-92), and the library's
-all-reduce, all-gather and fused row-parallel GEMM + all-reduce on top.
-``B200CommImpl`` installs it as a ``DistributedImpl`` plugin.
+``B200CommImpl`` is the plugin. When ``loopsgl`` is importable it subclasses the
+reference's own ``DistributedImpl``, and ``install`` appends it to the reference's
+``DistributedCommunicator.plugins`` (the last plugin wins, impl.py:63-70), so the
+reference's row-parallel linears, vocab-parallel embedding and LM head all-reduce and
+all-gather through it unchanged. ``install`` also makes it this package's active
+communicator (``active``), which the drop-in linears of ``plugins`` use for the fused
+GEMM + all-reduce.
 """
 
 from __future__ import annotations
-
-from dataclasses import dataclass
-from typing import List
 
 import ctypes
 
 import torch
 import torch.distributed as dist
 
-
-@dataclass(frozen=True)
-class DistributedInfo:
-    """distributed/info.py:7-18."""
-
-    rank: int
-    size: int
-
-    def is_primary(self) -> bool:
-        return self.rank == 0
-
-
-_TP_INFO: DistributedInfo | None = None
-
-
-def set_tp_info(rank: int, size: int) -> None:
-    """info.py:21-25 (raises if already set)."""
-    global _TP_INFO
-    if _TP_INFO is not None:
-        raise RuntimeError("TP info has been set")
-    _TP_INFO = DistributedInfo(rank, size)
-
-
-def reset_tp_info() -> None:
-    global _TP_INFO
-    _TP_INFO = None
-
-
-def tp_info() -> DistributedInfo:
-    """``get_tp_info`` with a TP=1 default when nothing was set."""
-    return _TP_INFO if _TP_INFO is not None else DistributedInfo(0, 1)
-
-
-class DistributedImpl:
-    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
-        raise NotImplementedError
-
-    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
-        raise NotImplementedError
-
-
-class TorchDistributedImpl(DistributedImpl):
-    """impl.py:25-41."""
-
-    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
-        if dist.get_world_size() == 1:
-            return x
-        dist.all_reduce(x, op=dist.ReduceOp.SUM)
-        return x
-
-    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
-        world = dist.get_world_size()
-        if world == 1:
-            return x
-        shape = list(x.shape)
-        shape[0] *= world
-        out = torch.empty(shape, dtype=x.dtype, device=x.device)
-        dist.all_gather_into_tensor(out, x)
-        return out
-
-
-class DistributedCommunicator:
-    """impl.py:63-70: the last plugin wins."""
-
-    plugins: List[DistributedImpl] = [TorchDistributedImpl()]
-
-    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
-        return self.plugins[-1].all_reduce(x)
-
-    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
-        return self.plugins[-1].all_gather(x)
-
-
-def lm_head_gather(logits_local: torch.Tensor, vocab: int) -> torch.Tensor:
-    """The LM-head all-gather + permute of layers/embedding.py:99-111."""
-    comm = DistributedCommunicator()
-    size = tp_info().size
-    if size == 1:
-        return logits_local
-    bs, local = logits_local.shape
-    out = comm.all_gather(logits_local)
-    if bs == 1:
-        return out.view(1, -1)[:, :vocab]
-    out = out.view(size, bs, local).permute(1, 0, 2).contiguous().view(bs, size * local)
-    return out[:, :vocab]
+try:  # the reference's plugin base class and communicator stack, when installed
+    from loopsgl.distributed.impl import DistributedCommunicator as RefCommunicator
+    from loopsgl.distributed.impl import DistributedImpl as _PluginBase
+except ImportError:
+    RefCommunicator = None
+    _PluginBase = object
 
 
 class B200Communicator:
@@ -213,8 +133,10 @@ class B200Communicator:
         self._call("lsb_comm_free", self._local)
 
 
-class B200CommImpl(DistributedImpl):
-    """The reference's plugin seam (impl.py:63-64) served by ``B200Communicator``."""
+class B200CommImpl(_PluginBase):
+    """The reference's plugin seam (``DistributedImpl``, impl.py:16-22) served by
+    ``B200Communicator``: ``all_reduce(x) -> x`` in place, ``all_gather(x) -> new``
+    along dim 0."""
 
     def __init__(self, comm: B200Communicator) -> None:
         self.comm = comm
@@ -224,3 +146,62 @@ class B200CommImpl(DistributedImpl):
 
     def all_gather(self, x: torch.Tensor) -> torch.Tensor:
         return self.comm.all_gather(x)
+
+    def __repr__(self) -> str:
+        return f"B200CommImpl(rank={self.comm.rank}, world={self.comm.world})"
+
+    # identity, not the field-wise equality of the reference's dataclass base: two
+    # plugins over different communicators are different plugins
+    __eq__ = object.__eq__
+    __hash__ = object.__hash__
+
+
+_ACTIVE: B200CommImpl | None = None
+
+
+def install(comm: B200Communicator) -> B200CommImpl:
+    """Make ``comm`` the communicator of this process: appended to the reference's
+    ``DistributedCommunicator.plugins`` when ``loopsgl`` is importable, and the one the
+    drop-in linears of ``plugins`` use."""
+    global _ACTIVE
+    impl = B200CommImpl(comm)
+    if RefCommunicator is not None:
+        RefCommunicator.plugins.append(impl)
+    _ACTIVE = impl
+    return impl
+
+
+def uninstall(impl: B200CommImpl) -> None:
+    """Undo ``install`` (before the communicator is closed)."""
+    global _ACTIVE
+    if RefCommunicator is not None and impl in RefCommunicator.plugins:
+        RefCommunicator.plugins.remove(impl)
+    if _ACTIVE is impl:
+        _ACTIVE = None
+
+
+def active() -> B200Communicator | None:
+    """The installed communicator, or None."""
+    return None if _ACTIVE is None else _ACTIVE.comm
+
+
+def tp_size() -> int:
+    """Tensor-parallel size: the reference's ``get_tp_info`` when it is set
+    (distributed/info.py:21-37), else the installed communicator's world, else 1."""
+    try:
+        from loopsgl.distributed import try_get_tp_info
+
+        info = try_get_tp_info()
+        if info is not None:
+            return info.size
+    except ImportError:
+        pass
+    comm = active()
+    return comm.world if comm is not None else 1
+
+
+def reference_all_reduce(x: torch.Tensor) -> torch.Tensor:
+    """All-reduce through the reference's communicator stack (its last plugin)."""
+    if RefCommunicator is None:
+        raise RuntimeError("tensor parallelism without an installed communicator")
+    return RefCommunicator().all_reduce(x)

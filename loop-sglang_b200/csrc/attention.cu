@@ -49,8 +49,8 @@ struct Workspace {
 
 // Layout: a fixed region of per-(row, head group) arrival counters at the head
 // (so calls of any shape find them zeroed), then the fp32 partials.
-constexpr int64_t kCounterCap = 65536;
-constexpr int64_t kCounterBytes = kCounterCap * sizeof(int);
+constexpr int64_t kCounterCap = kAttnCounterCap;
+constexpr int64_t kCounterBytes = kAttnCounterBytes;
 
 Workspace carve(void* base, int64_t rows, int32_t hq, int32_t d, int64_t splits) {
   Workspace w;

@@ -15,44 +15,35 @@
 //    contents: calls that overlap on the GPU (different streams, or different
 //    host threads without ordering) race on it and must be serialised by the
 //    caller;
-//  * the first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress and clears its arrival-counter region with an
-//    asynchronous memset on the caller's stream; make that first call before
-//    any stream capture. Later calls issue only the attention kernel, which
-//    leaves the counters zeroed again.
-#include <mutex>
-
+//  * every call looks up the array's device address on the current device with
+//    cudaGetSymbolAddress (host code cannot use the array's name as a device
+//    address) and clears the arrival-counter region with an asynchronous memset
+//    on the caller's stream before the kernel, so a call whose bounded wait gave
+//    up (LSB_DEVERR_TIMEOUT) cannot leave stale counters for the next one. The
+//    first call on a device may load the module: make it before any stream
+//    capture.
 #include "common.cuh"
 
 namespace {
 
 constexpr int64_t kScratchBytes = LSB_NOALLOC_ATTENTION_SCRATCH_BYTES;
-// Arrival counters at the head of the attention workspace (see attention.cu).
-constexpr int64_t kCounterRegionBytes = 65536 * 4;
+static_assert(kScratchBytes > lsb::kAttnCounterBytes,
+              "the static scratch must hold the attention counter region");
 
 __device__ __align__(256) unsigned char g_attention_scratch[kScratchBytes];
 
-std::mutex g_setup_mutex;
-void* g_scratch_ptr[64] = {nullptr};
-
-// Device address of the array on the current device, set up once per device.
+// Device address of the array on the current device, with its counters cleared on
+// `stream`. Allocates nothing.
 int scratch_for_current_device(void** out, cudaStream_t stream) {
-  int dev = 0;
-  LSB_CUDA(cudaGetDevice(&dev));
-  LSB_REQUIRE(dev >= 0 && dev < 64, "paged_attention_noalloc: device %d out of range", dev);
-  std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_ptr[dev]) {
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      cudaGetLastError();
-      return lsb::fail(LSB_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress failed: %s",
-                       cudaGetErrorString(e));
-    }
-    LSB_CUDA(cudaMemsetAsync(ptr, 0, kCounterRegionBytes, stream));
-    g_scratch_ptr[dev] = ptr;
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+  if (e != cudaSuccess || ptr == nullptr) {
+    cudaGetLastError();
+    return lsb::fail(LSB_ERR_CUDA, "paged_attention_noalloc: cudaGetSymbolAddress failed: %s",
+                     cudaGetErrorString(e));
   }
-  *out = g_scratch_ptr[dev];
+  LSB_CUDA(cudaMemsetAsync(ptr, 0, lsb::kAttnCounterBytes, stream));
+  *out = ptr;
   return LSB_OK;
 }
 

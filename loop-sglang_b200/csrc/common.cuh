@@ -57,6 +57,12 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// The paged-attention workspace starts with a fixed region of arrival counters (one
+// int per (row, head group) or per (row, consumer warp)), then the fp32 split
+// partials. Both attention entry points size and clear the region from these.
+constexpr int64_t kAttnCounterCap = 65536;
+constexpr int64_t kAttnCounterBytes = kAttnCounterCap * sizeof(int);
+
 // ---------------------------------------------------------------------------
 // Device helpers
 // ---------------------------------------------------------------------------

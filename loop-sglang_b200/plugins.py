@@ -2,15 +2,19 @@
 
 Each class keeps the name, method signatures, argument meaning and error behaviour
 of the Loop-SGLang interface it replaces, so the reference can register it where
-it registers its own (see INTEGRATION.md for the three-line bindings):
+it registers its own:
 
-* ``B200AttnBackend`` -- ``BaseAttnBackend`` (python/loopsgl/attention/base.py:19-38),
-  registered in ``SUPPORTED_ATTENTION_BACKENDS`` (attention/__init__.py:19-40). It
-  serves all three looped-KV policies, including last-exited on SM100 (the
-  reference's selector rejects that combination, attention/selector.py:99-106).
+* ``B200AttnBackend`` -- a ``BaseAttnBackend`` (python/loopsgl/attention/base.py:19-38).
+  When ``loopsgl`` is importable it subclasses the reference's own abstract class and
+  ``register()`` adds it to ``SUPPORTED_ATTENTION_BACKENDS`` as ``"b200"``
+  (attention/__init__.py:19-40). It serves all three looped-KV policies, including
+  last-exited on SM100 (the reference's selector rejects that combination,
+  attention/selector.py:99-106), over this package's pools or the reference's own.
 * ``LinearReplicated`` / ``LinearColParallelMerged`` / ``LinearQKVMerged`` /
   ``LinearOProj`` / ``LinearRowParallel`` -- the TP linear layers
-  (layers/linear.py:14-128), ``forward(x) -> y`` on the tcgen05 GEMM.
+  (layers/linear.py:14-128), ``forward(x) -> y`` on the tcgen05 GEMM; the row-parallel
+  ones run the GEMM and the NVLink all-reduce as one kernel when the B200 communicator
+  is installed (``comm.install``).
 * ``RMSNorm`` / ``RMSNormFused`` -- layers/norm.py:8-38.
 * ``RotaryEmbedding`` -- layers/rotary.py:12-55 (neox, fp32 cos/sin table).
 * ``silu_and_mul`` -- layers/activation.py:9-12.
@@ -24,20 +28,54 @@ The batch object passed to the backend is the reference's ``ForwardBatch``
 
 from __future__ import annotations
 
+from abc import ABC, abstractmethod
 from dataclasses import dataclass
 from typing import List
 
 import torch
 
 from . import ops
-from .kvcache import LastExitedKVCache
 from .model import rope_cos_sin_cache
+
+try:  # the reference's own abstract interface, when it is installed
+    from loopsgl.attention.base import BaseAttnBackend, BaseAttnMetadata
+
+    HAVE_LOOPSGL = True
+except ImportError:
+    HAVE_LOOPSGL = False
+
+    class BaseAttnMetadata(ABC):  # type: ignore[no-redef]
+        """The abstract metadata of attention/base.py:13-16."""
+
+        @abstractmethod
+        def get_last_indices(self, bs: int) -> torch.Tensor: ...
+
+    class BaseAttnBackend(ABC):  # type: ignore[no-redef]
+        """The abstract backend of attention/base.py:19-38."""
+
+        @abstractmethod
+        def forward(self, q, k, v, layer_id: int, batch) -> torch.Tensor: ...
+
+        @abstractmethod
+        def prepare_metadata(self, batch) -> None: ...
+
+        def prepare_core_metadata(self, batch, depths) -> None:
+            raise ValueError("This attention backend does not support last-exited KV")
+
+        @abstractmethod
+        def init_capture_graph(self, max_seq_len: int, bs_list: List[int]) -> None: ...
+
+        @abstractmethod
+        def prepare_for_capture(self, batch) -> None: ...
+
+        @abstractmethod
+        def prepare_for_replay(self, batch) -> None: ...
 
 
 # ----------------------------------------------------------------- attention --
 
 @dataclass
-class B200Metadata:
+class B200Metadata(BaseAttnMetadata):
     """Attention metadata (the fields of ``FAMetadata``, attention/fa.py:26-41)."""
 
     cu_seqlens_k: torch.Tensor
@@ -66,20 +104,43 @@ class _Buffers:
         self.page_table = torch.zeros(max_bs, max_pages, **i32)
 
 
-class B200AttnBackend:
-    """``BaseAttnBackend`` on the sm_100a paged-attention kernel."""
+def _slot_views(kvcache, layer_id: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """One KV layer as ``[slots, Hkv*D]`` matrices: this package's pools expose them
+    directly, the reference's as ``k_cache``/``v_cache`` views (mha_pool.py:48-52,
+    last_exited.py:292-296) of contiguous ``[..., Hkv, D]`` rows."""
+    if hasattr(kvcache, "slots"):
+        return kvcache.slots(layer_id)
+    kc, vc = kvcache.k_cache(layer_id), kvcache.v_cache(layer_id)
+    return (kc.reshape(-1, kc.shape[-2] * kc.shape[-1]),
+            vc.reshape(-1, vc.shape[-2] * vc.shape[-1]))
 
-    def __init__(self, config, ctx) -> None:
+
+class B200AttnBackend(BaseAttnBackend):
+    """``BaseAttnBackend`` on the sm_100a paged-attention kernel.
+
+    ``B200AttnBackend(config)`` takes the pool and page size from the reference's global
+    ``Context`` (as its FlashAttention backend does, attention/fa.py:47-52); ``ctx``
+    supplies them directly."""
+
+    def __init__(self, config, ctx=None) -> None:
+        if ctx is None:
+            from loopsgl.core import get_global_ctx
+
+            ctx = get_global_ctx()
         self.config = config
         self.ctx = ctx
         self.kvcache = ctx.kv_cache
         self.page_size = ctx.page_size
         self.scale = config.head_dim ** -0.5
-        self.num_kv_heads = getattr(self.kvcache, "num_kv_heads", config.num_kv_heads)
+        self.num_kv_heads = getattr(self.kvcache, "num_kv_heads", None) or \
+            getattr(config, "num_kv_heads")
+        # last-exited pools carry a slot map (the reference's test, attention/fa.py:74)
+        self.last_exited = hasattr(self.kvcache, "slot_map")
+        self.core_start = getattr(self.kvcache, "core_start", 0)
+        self.core_end = getattr(self.kvcache, "core_end", 0)
         self.eager: _Buffers | None = None
         self.capture: _Buffers | None = None
         self.capture_bs: List[int] = []
-        self.last_exited = isinstance(self.kvcache, LastExitedKVCache)
         self._group_tables: dict[tuple[str, bool], tuple[torch.Tensor, torch.Tensor]] = {}
 
     # -- BaseAttnBackend.forward (attention/fa.py:68-93) ---------------------------
@@ -88,16 +149,15 @@ class B200AttnBackend:
         md = batch.attn_metadata
         out_loc, table = batch.out_loc, md.page_table
         if self.last_exited:
-            kv = self.kvcache
-            group = kv.layer_groups[layer_id]
-            core = kv.is_core_layer(layer_id)
+            group = self.kvcache.layer_groups[layer_id]
+            core = self.core_start <= layer_id < self.core_end
             locs = md.core_out_loc if core else md.fixed_out_loc
             tables = md.core_page_table if core else md.fixed_page_table
             if locs is None or tables is None:
                 raise ValueError("Last-exited KV needs prepare_core_metadata before attention")
             out_loc, table = locs[group], tables[group]
         self.kvcache.store_kv(k, v, out_loc, layer_id)
-        kc, vc = self.kvcache.slots(layer_id)
+        kc, vc = _slot_views(self.kvcache, layer_id)
         q3 = q.view(q.shape[0], -1, self.config.head_dim) if q.dim() == 2 else q
         return ops.paged_attention(q3, kc, vc, table, md.cache_seqlens, md.cu_seqlens_q,
                                    self.page_size, table.shape[1] * self.page_size, self.scale,
@@ -121,6 +181,7 @@ class B200AttnBackend:
         if not self.last_exited:
             return
         kv = self.kvcache
+        dev = md.page_table.device
         for kind, groups in (("core", kv.core_groups), ("fixed", kv.fixed_groups)):
             if not groups:
                 continue
@@ -130,8 +191,8 @@ class B200AttnBackend:
             have = self._group_tables.get(key)
             if have is None or have[0].shape[1] < shape[1] or have[0].shape[2] < shape[2] \
                     or have[1].shape[1] < n:
-                have = (torch.zeros(shape, dtype=torch.int32, device=kv.device),
-                        torch.zeros(groups, max(n, 1), dtype=torch.int32, device=kv.device))
+                have = (torch.zeros(shape, dtype=torch.int32, device=dev),
+                        torch.zeros(groups, max(n, 1), dtype=torch.int32, device=dev))
                 self._group_tables[key] = have
             table, out = have[0][:, : shape[1], : shape[2]], have[1][:, :n]
             setattr(md, f"{kind}_page_table", table)
@@ -166,7 +227,8 @@ class B200AttnBackend:
     def init_capture_graph(self, max_seq_len: int, bs_list: List[int]) -> None:
         assert self.capture is None, "Capture already initialized."
         max_pages = (max_seq_len + self.page_size - 1) // self.page_size
-        self.capture = _Buffers(max(bs_list), max_pages, self.kvcache.device)
+        dev = self.ctx.page_table.device
+        self.capture = _Buffers(max(bs_list), max_pages, dev)
         self.capture_bs = sorted(bs_list)
 
     def prepare_for_capture(self, batch) -> None:
@@ -187,6 +249,24 @@ class B200AttnBackend:
         self._attach(batch, md, capture=True)
 
 
+def create_b200_backend(config) -> B200AttnBackend:
+    """The ``BackendCreator`` of attention/__init__.py:15-16."""
+    return B200AttnBackend(config)
+
+
+def register(name: str = "b200") -> bool:
+    """Add the backend to the reference's ``SUPPORTED_ATTENTION_BACKENDS``
+    (attention/__init__.py:19-40) under ``name``. False when ``loopsgl`` is absent;
+    registering twice is a no-op."""
+    if not HAVE_LOOPSGL:
+        return False
+    from loopsgl.attention import SUPPORTED_ATTENTION_BACKENDS
+
+    if name not in SUPPORTED_ATTENTION_BACKENDS.supported_names():
+        SUPPORTED_ATTENTION_BACKENDS.register(name)(create_b200_backend)
+    return True
+
+
 # ------------------------------------------------------------------- linears --
 
 class _LinearTPImpl:
@@ -205,10 +285,10 @@ class _LinearTPImpl:
         return y.view(*shape[:-1], y.shape[-1])
 
 
-def _tp():
-    from .comm import tp_info
+def _tp_size() -> int:
+    from .comm import tp_size
 
-    return tp_info()
+    return tp_size()
 
 
 class LinearReplicated(_LinearTPImpl):
@@ -218,7 +298,7 @@ class LinearReplicated(_LinearTPImpl):
 
 class LinearColParallelMerged(_LinearTPImpl):
     def __init__(self, input_size: int, output_sizes: List[int], has_bias: bool) -> None:
-        size = _tp().size
+        size = _tp_size()
         if any(s % size for s in output_sizes):
             raise ValueError(f"output sizes {output_sizes} do not divide by TP {size}")
         super().__init__(input_size, sum(output_sizes), input_size,
@@ -228,7 +308,7 @@ class LinearColParallelMerged(_LinearTPImpl):
 class LinearQKVMerged(_LinearTPImpl):
     def __init__(self, hidden_size: int, head_dim: int, num_qo_heads: int, num_kv_heads: int,
                  has_bias: bool) -> None:
-        size = _tp().size
+        size = _tp_size()
         if num_qo_heads % size:
             raise ValueError(f"{num_qo_heads} heads do not divide by TP {size}")
         local_kv = num_kv_heads // size if num_kv_heads % size == 0 else num_kv_heads
@@ -237,21 +317,29 @@ class LinearQKVMerged(_LinearTPImpl):
 
 
 class _RowParallel(_LinearTPImpl):
-    def __init__(self, input_size: int, output_size: int, has_bias: bool) -> None:
-        from .comm import DistributedCommunicator
+    """Row-parallel: this rank's input columns, the sum over the ranks. With the B200
+    communicator installed the GEMM and the all-reduce are one kernel
+    (``lsb_gemm_allreduce``); otherwise the local GEMM is all-reduced through the
+    reference's communicator stack, as layers/linear.py:103-107 does."""
 
-        size = _tp().size
+    def __init__(self, input_size: int, output_size: int, has_bias: bool) -> None:
+        size = _tp_size()
         if input_size % size:
             raise ValueError(f"input size {input_size} does not divide by TP {size}")
-        self._comm = DistributedCommunicator()
         self._tp_size = size
         super().__init__(input_size, output_size, input_size // size, output_size, has_bias)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        y = super().forward(x)
-        if self._tp_size > 1:
-            y = self._comm.all_reduce(y)
-        return y
+        from .comm import active, reference_all_reduce
+
+        if self._tp_size == 1:
+            return super().forward(x)
+        comm = active()
+        if comm is None:
+            return reference_all_reduce(super().forward(x))
+        shape = x.shape
+        y = comm.gemm_allreduce(x.reshape(-1, shape[-1]), self.weight, self.bias)
+        return y.view(*shape[:-1], y.shape[-1])
 
 
 class LinearOProj(_RowParallel):

@@ -122,6 +122,21 @@ def make_weights(
     return w
 
 
+LINEAR_SUFFIXES = ("qkv_proj.weight", "o_proj.weight", "gate_up_proj.weight",
+                   "down_proj.weight", "adapter.weight", "lm_head.weight")
+
+
+def with_fp32_matrices(weights: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    """The same weights with every ``ops.linear`` matrix held in fp32.
+
+    bf16 values are exact in fp32 and ``ops.linear`` computes in fp32 and rounds to the
+    activation's dtype, so results are bit-identical; only the per-call conversion of the
+    matrix is saved (full-size models: several GB per step). Embedding and norm weights
+    keep their dtype (they set the dtype of the rows they produce).
+    """
+    return {k: (v.float() if k.endswith(LINEAR_SUFFIXES) else v) for k, v in weights.items()}
+
+
 @dataclass
 class Batch:
     """The fields of ``ForwardBatch`` + attention metadata the hot path consumes

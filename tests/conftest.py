@@ -18,6 +18,20 @@ for p in (str(ROOT), str(ROOT / "tests")):
         sys.path.insert(0, p)
 
 
+def reference_python() -> str | None:
+    """The ``python/`` directory of a Loop-SGLang checkout, for the CPU tests that drive
+    this package through the reference's own plugin seams: ``$LOOPSGL_REFERENCE_PYTHON``,
+    else a checkout named ``reference`` beside this repository. None when neither has
+    ``loopsgl`` (those tests then skip; the GPU tests never need it)."""
+    import os
+
+    for cand in (os.environ.get("LOOPSGL_REFERENCE_PYTHON"),
+                 str(ROOT.parent / "reference" / "python")):
+        if cand and (Path(cand) / "loopsgl" / "__init__.py").exists():
+            return cand
+    return None
+
+
 def pytest_configure(config: pytest.Config) -> None:
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 

@@ -52,13 +52,16 @@ def _noalloc(q, kc, vc, table, seq, cu, hq, hkv, d, page, max_seq) -> torch.Tens
     return out
 
 
-@pytest.mark.parametrize("q_lens,kv_lens", [
-    ([1, 1, 1], [40, 300, 2000]),   # decode rows, several splits
-    ([1, 2], [3000, 4100]),         # long rows: many splits merged through the scratch
-    ([5, 1, 12], [5, 40, 30]),      # prefill rows with a cached prefix
+@pytest.mark.parametrize("q_lens,kv_lens,shape", [
+    ([1, 1, 1], [40, 300, 2000], {}),   # decode rows, several splits (streaming kernel)
+    ([1, 2], [3000, 4100], {}),         # long rows: many splits merged through the scratch
+    ([5, 1, 12], [5, 40, 30], {}),      # prefill rows with a cached prefix
+    # one-token pages with 2 KV heads of 128 (under 2 KB of K per key): the per-CTA
+    # kernel, whose split partials and (row, head group) counters also use the scratch
+    ([1, 1, 3], [700, 2900, 1500], {"hq": 8, "hkv": 2, "page": 1}),
 ])
-def test_noalloc_matches_workspace_entry_point(q_lens, kv_lens) -> None:
-    args = _case(7, q_lens, kv_lens)
+def test_noalloc_matches_workspace_entry_point(q_lens, kv_lens, shape) -> None:
+    args = _case(7, q_lens, kv_lens, **shape)
     q, kc, vc, table, seq, cu, hq, hkv, d, page, max_seq = args
     ref = ops.paged_attention(q, kc, vc, table, seq, cu, page, max_seq, d ** -0.5, hkv)
     for _ in range(2):  # two calls in a row: the shared scratch must come back clean
