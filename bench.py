@@ -116,6 +116,8 @@ def gpu_weights(cfg, device, seed: int) -> dict[str, torch.Tensor]:
     mat("model.embed_tokens.weight", cfg.vocab, h)
     for p in cfg.layer_names():
         mat(f"{p}.self_attn.qkv_proj.weight", cfg.qkv_out, h)
+        if cfg.attention_bias:
+            mat(f"{p}.self_attn.qkv_proj.bias", cfg.qkv_out)
         mat(f"{p}.self_attn.o_proj.weight", h, cfg.heads * cfg.head_dim)
         mat(f"{p}.mlp.gate_up_proj.weight", 2 * i, h)
         mat(f"{p}.mlp.down_proj.weight", h, i)
@@ -123,8 +125,13 @@ def gpu_weights(cfg, device, seed: int) -> dict[str, torch.Tensor]:
                   "post_attention_layernorm_2"):
             norm(f"{p}.{n}.weight", h)
     norm("model.norm.weight", h)
-    mat("model.early_exit_gate.weight", 1, h)
-    w["model.early_exit_gate.bias"] = torch.zeros(1, dtype=torch.bfloat16, device=device)
+    if cfg.arch == "ouro":
+        mat("model.early_exit_gate.weight", 1, h)
+        w["model.early_exit_gate.bias"] = torch.zeros(1, dtype=torch.bfloat16, device=device)
+    else:
+        mat("model.adapter.weight", h, 2 * h)
+        if cfg.adapter_bias:
+            mat("model.adapter.bias", h)
     mat("lm_head.weight", cfg.vocab, h)
     return w
 
@@ -195,7 +202,8 @@ PARITY_PROMPTS = (48, 80, 112, 160)
 PARITY_DECODE = 3
 
 
-def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict | None:
+def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int,
+                 prompts: tuple[int, ...] = PARITY_PROMPTS) -> dict | None:
     """Greedy tokens of the benchmarked model object (same weights, same kernels, same
     tensor-parallel split) against the CPU oracle on the same inputs.
 
@@ -205,7 +213,11 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict
     prefill and steps on rank 0. A token agrees when the argmaxes match; it is a near tie
     when they differ but the oracle's logit of the CUDA path's token is within 2e-2 x
     max |logit| of its maximum (bf16 reduction order may take either); anything else is
-    a mismatch. Collective over the ranks: every rank runs the CUDA part.
+    a mismatch. ``agree_decided`` leaves the near ties out. The oracle also runs in fp32
+    arithmetic on the same weights: after 96 layer passes of a random-init model two bf16
+    computations that differ only in summation order drift apart by about as much as
+    either drifts from fp32, so ``vs_fp32`` puts the logit error in that context.
+    Collective over the ranks: every rank runs the CUDA part.
     """
     from oracle import model as om
 
@@ -216,19 +228,23 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict
     policy = model.policy
     page = 1 if policy == "last_exited" else PAGE
     g = torch.Generator().manual_seed(SEED + 11)
+    prompt_lens = tuple(prompts)
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g, dtype=torch.int32)
-               for n in PARITY_PROMPTS]
+               for n in prompt_lens]
     b = len(prompts)
-    span = max(PARITY_PROMPTS) + PARITY_DECODE + 1
+    span = max(prompt_lens) + PARITY_DECODE + 1
     pages_per = (span + page - 1) // page
     table = (1 + torch.arange(b).view(-1, 1) * pages_per + torch.arange(pages_per)).to(torch.int32)
     num_pages = b * pages_per + 1
-    lens = torch.tensor(PARITY_PROMPTS, dtype=torch.int32)
+    if policy == "last_exited":  # version slots: one per loop step of every token
+        tokens = sum(prompt_lens) + b * (PARITY_DECODE + 1)
+        num_pages = max(num_pages, cfg.loop_steps * tokens + 1)
+    lens = torch.tensor(prompt_lens, dtype=torch.int32)
 
     def batch(step: int, ids: torch.Tensor):
         if step < 0:
-            pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in PARITY_PROMPTS])
-            rows = torch.cat([torch.full((n,), r) for r, n in enumerate(PARITY_PROMPTS)])
+            pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in prompt_lens])
+            rows = torch.cat([torch.full((n,), r) for r, n in enumerate(prompt_lens)])
             seq, cu = lens.clone(), torch.zeros(b + 1, dtype=torch.int32)
             cu[1:] = torch.cumsum(lens, 0)
         else:
@@ -256,23 +272,40 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict
     if rank != 0 or cpu_weights is None:
         return None
     ocfg = om.LoopedConfig(**cfg.__dict__)
-    oracle = om.LoopedModel(ocfg, om.with_fp32_matrices(cpu_weights), policy)
-    if policy == "last_exited":
-        pool = om.SlotKVPool(oracle.slot_layout(), num_pages, cfg.kv_heads, cfg.head_dim,
-                             torch.bfloat16)
-    else:
-        pool = om.PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads,
-                              cfg.head_dim, torch.bfloat16)
-    counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
-    worst = 0.0
-    for i, step in enumerate(range(-1, PARITY_DECODE)):
-        ob = batch(step, fed[i])
+
+    def oracle_logits(dtype: torch.dtype) -> list[torch.Tensor]:
+        w = (om.with_fp32_matrices(cpu_weights) if dtype == torch.bfloat16
+             else {k: v.float() for k, v in cpu_weights.items()})
+        oracle = om.LoopedModel(ocfg, w, policy)
         if policy == "last_exited":
-            pool.versions.reserve(ob.out_loc.numpy())
-        ref = oracle.forward(ob, pool).float()
+            pool = om.SlotKVPool(oracle.slot_layout(), num_pages, cfg.kv_heads, cfg.head_dim,
+                                 dtype)
+        else:
+            pool = om.PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads,
+                                  cfg.head_dim, dtype)
+        out = []
+        for i, step in enumerate(range(-1, PARITY_DECODE)):
+            ob = batch(step, fed[i])
+            if policy == "last_exited":
+                pool.versions.reserve(ob.out_loc.numpy())
+            out.append(oracle.forward(ob, pool).float())
+        return out
+
+    def rel(a: torch.Tensor, ref: torch.Tensor) -> float:
+        return float((a - ref).abs().max() / ref.abs().max())
+
+    refs, exact = oracle_logits(torch.bfloat16), oracle_logits(torch.float32)
+    counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
+    worst = worst_exact = floor = 0.0
+    agree_exact = oracle_exact = 0
+    for i, ref in enumerate(refs):
         scale = ref.abs().max(-1).values
-        worst = max(worst, float((got[i] - ref).abs().max() / scale.max()))
+        worst = max(worst, rel(got[i], ref))
+        worst_exact = max(worst_exact, rel(got[i], exact[i]))
+        floor = max(floor, rel(ref, exact[i]))
         gi, ri = got[i].argmax(-1), ref.argmax(-1)
+        agree_exact += int((gi == exact[i].argmax(-1)).sum())
+        oracle_exact += int((ri == exact[i].argmax(-1)).sum())
         for r in range(b):
             if int(gi[r]) == int(ri[r]):
                 counts["agree"] += 1
@@ -281,11 +314,20 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int) -> dict
             else:
                 counts["mismatch"] += 1
     n = sum(counts.values())
-    return {"agree": round(counts["agree"] / n, 4), "tokens": n, "rows": b,
-            "near_ties": counts["near_tie"], "mismatches": counts["mismatch"],
-            "max_logit_rel_err": round(worst, 5), "tp": world, "policy": policy,
-            "vs": "CPU oracle, bf16 rounding points, same weights and inputs",
-            "sample": (f"{b} requests, prompts {list(PARITY_PROMPTS)} random ids, full-depth "
+    decided = counts["agree"] + counts["mismatch"]
+    return {"agree": round(counts["agree"] / n, 4),
+            "agree_decided": round(counts["agree"] / max(1, decided), 4),
+            "tokens": n, "rows": b, "near_ties": counts["near_tie"],
+            "mismatches": counts["mismatch"], "max_logit_rel_err": round(worst, 5),
+            "vs_fp32": {"agree": round(agree_exact / n, 4),
+                        "bf16_oracle_agree": round(oracle_exact / n, 4),
+                        "max_logit_rel_err": round(worst_exact, 5),
+                        "bf16_oracle_rel_err": round(floor, 5)},
+            "tp": world, "policy": policy,
+            "vs": ("CPU oracle with the reference's bf16 rounding points, same weights and "
+                   "inputs (vs_fp32: the oracle in fp32 arithmetic on the same weights, and "
+                   "how far the bf16 oracle itself lands from it)"),
+            "sample": (f"{b} requests, prompts {list(prompt_lens)} random ids, full-depth "
                        f"prefill + {PARITY_DECODE} greedy decode steps through the benchmarked "
                        "model object")}
 
@@ -305,17 +347,20 @@ def rank_info(world: int, rank: int, local: int, dev) -> list | None:
 # ---------------------------------------------------------------- CPU side --
 
 def cpu_decode_sample(steps: int, batch: int, threads: int, model_cfg: dict | None = None,
-                      contexts: np.ndarray | None = None, name: str = "Ouro-1.4B") -> dict:
+                      contexts: np.ndarray | None = None, name: str = "Ouro-1.4B",
+                      policy: str = "depth_indexed", weights: dict | None = None) -> dict:
     """The oracle (CPU restatement of the reference decode step) on a bounded sample:
     ``batch`` requests of the workload (configs[1] contexts unless given), ``steps``
-    full-depth decode steps."""
+    full-depth decode steps (``weights``: bf16 weights to reuse instead of generating)."""
     from oracle import model as om
 
     torch.set_num_threads(threads)
     cfg = om.LoopedConfig(**(model_cfg or OURO_14B))
     t0 = time.perf_counter()
-    w = om.with_fp32_matrices(om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16))
-    mdl = om.LoopedModel(cfg, w, "depth_indexed")
+    if weights is None:
+        weights = om.make_weights(cfg, seed=SEED, dtype=torch.bfloat16)
+    w = om.with_fp32_matrices(weights)
+    mdl = om.LoopedModel(cfg, w, policy)
     ctx = (request_lengths()[:batch] + MID) if contexts is None else np.asarray(contexts)[:batch]
     pages_per = [(int(c) + steps + PAGE) // PAGE for c in ctx]
     num_pages = sum(pages_per) + 1
@@ -362,6 +407,12 @@ def run_reference(args) -> None:
         base = cpu_decode_sample(min(steps, 2), 1, threads, OURO_26B,
                                  np.array([RADIX_PREFIX + RADIX_SUFFIX + RADIX_MID]), "Ouro-2.6B")
         metric, workload = RADIX_METRIC, RADIX_WORKLOAD
+    elif args.workload == "huginn":
+        rng = np.random.default_rng(SEED)
+        ctx = rng.integers(HUGINN_PROMPT_RANGE[0], HUGINN_PROMPT_RANGE[1] + 1, 8) + HUGINN_MID
+        base = cpu_decode_sample(min(steps, 2), min(args.cpu_batch, 8), threads, HUGINN, ctx,
+                                 "Huginn-0125", policy="shared")
+        metric, workload = HUGINN_METRIC, HUGINN_WORKLOAD
     else:
         base = cpu_decode_sample(steps, args.cpu_batch, threads)
         metric, workload = METRIC, WORKLOAD
@@ -968,6 +1019,204 @@ def run_b200_cdb(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+# ---------------------------------------------------------- Huginn replicas --
+# Huginn-0125 architecture (hidden 5280, 55 heads x 96, prelude 2 +
+# core 4 x 32 recurrences + coda 2, SwiGLU 17920, vocab 65536, RoPE 5e4), random-init bf16,
+# fully shared looped KV, TP=1 x one data-parallel replica per GPU (55 heads do not shard):
+# 64 requests per replica with prompts U[512, 1024] and 256 outputs. The embedding scale is
+# sqrt(hidden) and q/k/v carry a bias, as in Huginn-0125's published configuration; the
+# recurrent state starts at zero (state_init "zero", the deterministic choice).
+HUGINN = dict(arch="huginn", hidden=5280, heads=55, kv_heads=55, head_dim=96, intermediate=17920,
+              vocab=65536, num_prelude_layers=2, num_core_layers=4, num_coda_layers=2,
+              loop_steps=32, rope_theta=50000.0, rms_eps=1e-6, max_position=2048,
+              embed_scale=5280 ** 0.5, attention_bias=True, adapter_bias=False)
+HUGINN_REQS = 64
+HUGINN_PROMPT_RANGE = (512, 1024)
+HUGINN_OUT = 256
+HUGINN_MID = 128
+HUGINN_METRIC = ("decode output tok/s, Huginn-0125 architecture, shared looped KV, one "
+                 "TP=1 replica per GPU (configs[4]), summed over the job's GPUs")
+HUGINN_WORKLOAD = ("configs[4]: Huginn-0125 architecture random-init bf16 (prelude 2 + core 4 "
+                   "x 32 recurrences + coda 2, hidden 5280, 55 heads x 96), fully shared looped "
+                   "KV in 16-token pages, 64 requests per replica with prompt U[512,1024] + 256 "
+                   "outputs decoding at prompt+128, one independent replica per GPU")
+
+
+def run_b200_huginn(args) -> None:
+    """Data-parallel replicas: every rank decodes its own 64 requests through its own
+    TP=1 model; the ranks share nothing but the barrier and the max over their times."""
+    from __graft_entry__ import load_package
+
+    load_package()
+    from loop_sglang_b200 import ops
+    from loop_sglang_b200.engine import DecodeEngine
+    from loop_sglang_b200.model import LoopedConfig, LoopedDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                             device_id=dev)
+    cfg = LoopedConfig(**HUGINN)
+    t0 = time.perf_counter()
+    weights = gpu_weights(cfg, dev, SEED)
+    cpu_weights = ({k: v.cpu() for k, v in weights.items()}
+                   if rank == 0 and not args.no_parity else None)
+    model = LoopedDecoder(cfg, weights, "shared", dev)
+    del weights
+    torch.cuda.empty_cache()
+    rng = np.random.default_rng(SEED + 100 * rank)  # each replica serves its own requests
+    bs = args.batch or HUGINN_REQS
+    prompts = rng.integers(HUGINN_PROMPT_RANGE[0], HUGINN_PROMPT_RANGE[1] + 1, bs)
+    full = prompts + HUGINN_OUT
+    pages_per = (full + PAGE - 1) // PAGE
+    num_pages = int(pages_per.sum()) + 1
+    kv = model.make_kv_cache(num_pages, PAGE, zero=False)
+    kv._kv_buffer.normal_(generator=torch.Generator(device=dev).manual_seed(SEED + 1))
+    kv._kv_buffer[:, :, 0].zero_()
+    max_len = int(full.max())
+    eng = DecodeEngine(model, kv, bs, max_len, PAGE, max_reqs=bs)
+    perm = torch.randperm(num_pages - 1, generator=torch.Generator().manual_seed(SEED + 2)) + 1
+    off = 0
+    for r in range(bs):
+        n = int(pages_per[r])
+        eng.assign_pages(r + 1, perm[off:off + n].to(dev))
+        off += n
+    rows = torch.arange(1, bs + 1, dtype=torch.int32, device=dev)
+    steps_total = args.warmup + args.steps
+    base_seq = torch.as_tensor(prompts + HUGINN_MID, dtype=torch.int32, device=dev)
+    sched = torch.stack([base_seq + 1 + s for s in range(steps_total + 1)])
+    eng.ids.copy_(torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32))
+    eng.set_batch(rows, sched[0])
+    eng.capture()
+    log(f"[bench] rank {rank}: Huginn replica batch {bs}, {num_pages} pages, setup "
+        f"{time.perf_counter() - t0:.1f}s, {eng.launches_per_step} kernels/step")
+    s = eng.stream
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(s):
+        for k in range(args.warmup):
+            eng.seq_lens.copy_(sched[k], non_blocking=True)
+            eng.replay()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(dev) as clocks, torch.cuda.stream(s):
+        ev[0].record(s)
+        for k in range(args.steps):
+            eng.seq_lens.copy_(sched[args.warmup + k], non_blocking=True)
+            eng.replay()
+            ev[k + 1].record(s)
+        s.synchronize()
+    barrier()
+    step_ms = [ev[k].elapsed_time(ev[k + 1]) for k in range(args.steps)]
+    total_ms = ev[0].elapsed_time(ev[-1])
+    clk = clocks.summary()
+    host_rows = torch.arange(1, bs + 1, dtype=torch.int32).pin_memory()
+    host_sched = sched.cpu().pin_memory()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for k in range(args.steps):
+        eng.decode_step_host(host_rows, host_sched[k])
+    e1.record(s)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # roofline of the dominant kernel: one layer's attention over the batch, timed alone
+    ctx = sched[args.warmup + args.steps - 1].to(torch.int64)
+    kv_row = model.hkv * cfg.head_dim * 2 * 2
+    attn_bytes = int(ctx.sum().item()) * kv_row + 2 * bs * model.hq * cfg.head_dim * 2
+    q = torch.randn(bs, model.hq, cfg.head_dim, device=dev).to(torch.bfloat16)
+    kc, vc = kv.slots(0)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    with torch.cuda.stream(s):
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+        a0.record(s)
+        for _ in range(reps):
+            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
+                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+        a1.record(s)
+        s.synchronize()
+    attn_s = a0.elapsed_time(a1) / 1000.0 / reps
+
+    t_max, e2e_max, tokens = total_ms, e2e_ms, bs * args.steps
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms, float(tokens)], device=dev)
+        tt = t.clone()
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.SUM)
+        t_max, e2e_max, tokens = float(t[0]), float(t[1]), int(tt[2])
+    # algorithmic bytes of one replica's step: every layer pass reads its weights and the
+    # KV of its (shared) layer for every row; the adapter once per recurrence; LM head
+    passes = cfg.num_prelude_layers + cfg.loop_steps * cfg.num_core_layers + cfg.num_coda_layers
+    layer_w = sum(t.numel() * 2 for t in (model.layers["model.layers.0"].qkv,
+                                          model.layers["model.layers.0"].o,
+                                          model.layers["model.layers.0"].gate_up,
+                                          model.layers["model.layers.0"].down))
+    step_bytes = (passes * layer_w + cfg.loop_steps * model.adapter.numel() * 2
+                  + model.lm_head_w.numel() * 2 + passes * int(ctx.sum().item()) * kv_row)
+    peak, peak_kind = peaks()
+    step_s = t_max / 1000.0 / args.steps
+    achieved = attn_bytes / attn_s / 1e9
+    line = {
+        "metric": HUGINN_METRIC, "value": tokens / (t_max / 1000.0), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_max / args.steps, "p50_tpot_ms": statistics.median(step_ms),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded random-init weights, random KV contents and token ids",
+        "config": {"workload": HUGINN_WORKLOAD, "model": "Huginn-0125 architecture (random init)",
+                   "global_batch": bs * world, "running_batch_per_gpu": bs,
+                   "mean_context": round(float(ctx.float().mean()), 1), "kv_pool_pages": num_pages,
+                   "page_size": PAGE, "parallelism": f"dp{world} (replicas, TP=1 each)",
+                   "l2": "inputs larger than L2 (each step streams ~%d GB)" % (step_bytes // 10**9)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "kernel": "paged_attention (one shared KV layer, whole replica batch)",
+                     "peak_kind": peak_kind,
+                     "step_frac": round(step_bytes / step_s / 1e9 / peak, 4),
+                     "step_bytes": step_bytes},
+        "e2e": {"value": tokens / (e2e_max / 1000.0), "unit": "tok/s",
+                "h2d_bytes_per_step": 2 * bs * 4, "d2h_bytes_per_step": bs * 4},
+        "gpu_launches": eng.launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    err = ops.device_error_word(reset=False)
+    if err:
+        line["device_error_word"] = err
+    line["ranks"] = rank_info(world, rank, local, dev)
+    if not args.no_parity:
+        line["parity"] = parity_stamp(model, cpu_weights, rank, world, prompts=HUGINN_PARITY)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_decode_sample(
+                min(args.cpu_steps, 2), min(args.cpu_batch, 8), os.cpu_count() or 1, HUGINN,
+                (prompts + HUGINN_MID)[:8], "Huginn-0125", policy="shared", weights=cpu_weights)
+            line["cpu_baseline"].pop("p50_step_s", None)
+        except Exception as exc:  # reported, never silently dropped
+            line["cpu_baseline"] = {"value": None, "error": repr(exc)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    eng.graph = None
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+HUGINN_PARITY = (8, 12, 16, 20)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -984,12 +1233,13 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the parity stamp (greedy tokens vs the CPU oracle)")
-    ap.add_argument("--workload", choices=["cdb", "cb", "radix"], default="cdb",
+    ap.add_argument("--workload", choices=["cdb", "cb", "radix", "huginn"], default="cdb",
                     help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB; "
-                         "radix: configs[3] (Ouro-2.6B, shared prefixes)")
+                         "radix: configs[3] (Ouro-2.6B, shared prefixes); huginn: configs[4] "
+                         "(one Huginn replica per GPU)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"cdb": 120, "cb": 40, "radix": 20}[args.workload]
+        args.steps = {"cdb": 120, "cb": 40, "radix": 20, "huginn": 25}[args.workload]
     if args.steps < 1:
         ap.error("--steps must be >= 1")
     if args.warmup < 3:
@@ -998,6 +1248,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "cdb":
         run_b200_cdb(args)
+    elif args.workload == "huginn":
+        run_b200_huginn(args)
     else:
         run_b200(args)  # cb and radix
 

@@ -171,6 +171,16 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
              const void* bias, int64_t M, int64_t N, int64_t K, int32_t epilogue,
              void* workspace, int64_t workspace_bytes, void* stream);
 
+/* y[M, N] = [x1 | x2] . w^T (+ bias) with w [N, K1 + K2]: the product over the
+ * concatenation of two activation tensors along K without materialising it (the
+ * K loop reads x1 and w's first K1 columns, then x2 and the last K2). Replaces
+ * Huginn's adapter, models/looped/huginn.py:162-167 (F.linear over
+ * torch.cat([hidden, injection], -1)). K1 a multiple of 8; epilogue LSB_EPI_NONE,
+ * LSB_EPI_BIAS or LSB_EPI_BIAS_AFTER_ROUND. */
+int lsb_gemm_concat(void* y, int64_t ldy, const void* x1, int64_t ldx1, const void* x2,
+                    int64_t ldx2, const void* w, int64_t ldw, const void* bias, int64_t M,
+                    int64_t N, int64_t K1, int64_t K2, int32_t epilogue, void* stream);
+
 /* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
  * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
  * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */

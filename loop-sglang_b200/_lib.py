@@ -55,6 +55,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_gemm_workspace_size": (c_int64, [I64, I64, I64]),
     "lsb_gemm": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P, I64, P]),
     "lsb_gemm_plan": (ctypes.c_int, [I64, I64, I64, P]),
+    "lsb_gemm_concat": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, P, I64, I64, I64, I64,
+                                       I32, P]),
     "lsb_swiglu_interleave": (ctypes.c_int, [P, P, I64, I64, P]),
     "lsb_ouro_step_exit": (ctypes.c_int, [P, I64, P, P, P, P, P, P, P, P, P, P, I32, I32, I32, F,
                                           I64, I64, F, P]),

@@ -51,6 +51,9 @@ struct GemmParams {
   int64_t ldy;
   const bf16* bias;
   int M, N, K;
+  // K blocks taken from the first (tmap_w, tmap_x) pair; the rest come from the second
+  // pair (a product over the concatenation [x | x2] of two activation tensors along K)
+  int kb1;
   int bn, stages, splits, epilogue;
   uint32_t idesc;
   int* error_flag;
@@ -162,7 +165,9 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 template <int EPI, bool CLUSTER, bool AR>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
-                        const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_w2,
+                        const __grid_constant__ CUtensorMap tmap_x2, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -203,6 +208,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)));
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)));
+    if (p.kb1 < kblocks) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w2)));
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x2)));
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -221,23 +230,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Weights do not depend on the previous kernel: fetch the first stages of the
       // weight stream, then wait for the producer of x, then fetch x.
       const int pre = nk < stages ? nk : stages;
-      auto kx_of = [&](int i) { return (kb_begin + (i + rot) % nk) * kBK; };
+      // K block of pipeline step i, and the tensor-map pair and K offset it reads
+      auto kb_of = [&](int i) { return kb_begin + (i + rot) % nk; };
+      auto load_w = [&](uint8_t* dst, uint64_t* bar, int kb) {
+        if (kb < p.kb1) tma_load_2d(dst, &tmap_w, bar, kb * kBK, n0);
+        else tma_load_2d(dst, &tmap_w2, bar, (kb - p.kb1) * kBK, n0);
+      };
+      auto load_x = [&](uint8_t* dst, uint64_t* bar, int kb) {
+        if (kb < p.kb1) tma_load_2d(dst, &tmap_x, bar, kb * kBK, m0);
+        else tma_load_2d(dst, &tmap_x2, bar, (kb - p.kb1) * kBK, m0);
+      };
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
-        tma_load_2d(smem + i * stage_bytes, &tmap_w, &full[i], kx_of(i), n0);
+        load_w(smem + i * stage_bytes, &full[i], kb_of(i));
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(smem + i * stage_bytes + kABytes, &tmap_x, &full[i], kx_of(i), m0);
+      for (int i = 0; i < pre; ++i) load_x(smem + i * stage_bytes + kABytes, &full[i], kb_of(i));
       for (int i = pre; i < nk; ++i) {
         const int s = i % stages;
         const uint32_t round = static_cast<uint32_t>(i / stages);
         if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, p.error_flag)) break;
         uint8_t* a_tile = smem + s * stage_bytes;
         mbar_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
-        const int kx = kx_of(i);
-        tma_load_2d(a_tile, &tmap_w, &full[s], kx, n0);
-        tma_load_2d(a_tile + kABytes, &tmap_x, &full[s], kx, m0);
+        const int kb = kb_of(i);
+        load_w(a_tile, &full[s], kb);
+        load_x(a_tile + kABytes, &full[s], kb);
       }
     }
   } else if (warp == 1) {
@@ -493,7 +510,8 @@ int num_sms() {
   return sms;
 }
 
-using Kernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
+using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                        const CUtensorMap, GemmParams);
 
 Kernel kernel_for(bool cluster, int epilogue, bool ar = false) {
   static const Kernel kernels[2][4] = {
@@ -674,17 +692,38 @@ extern "C" int64_t lsb_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return 0;  // split-K partials are reduced in distributed shared memory
 }
 
+// A second K segment: y = [x | x2] . [w | w2]^T, where x2 [M, K2] (row stride ldx2) and
+// w2 = w + K (the weight's columns K..K+K2, same row stride).
+struct Segment2 {
+  const void* x2;
+  int64_t ldx2;
+  int64_t K2;
+};
+
 static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
                      int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
-                     int32_t epilogue, const lsb_comm* comm, void* stream) {
+                     int32_t epilogue, const lsb_comm* comm, void* stream,
+                     const Segment2* seg2 = nullptr) {
   LSB_REQUIRE(y && x && w, "gemm: null pointer");
   LSB_REQUIRE(N > 0 && K > 0, "gemm: empty N or K (N=%lld K=%lld)", (long long)N, (long long)K);
+  const int64_t K2 = seg2 ? seg2->K2 : 0;
+  if (seg2) {
+    LSB_REQUIRE(seg2->x2 && K2 > 0 && seg2->ldx2 % 8 == 0 && seg2->ldx2 >= K2 &&
+                    aligned(seg2->x2, 16),
+                "gemm_concat: x2 must be 16-byte aligned with a row stride >= K2, a multiple "
+                "of 8");
+    LSB_REQUIRE(K % 8 == 0 && ldw >= K + K2,
+                "gemm_concat: K1 must be a multiple of 8 (w's second block starts 16-byte "
+                "aligned) and ldw >= K1 + K2");
+    LSB_REQUIRE(comm == nullptr, "gemm_concat: no fused all-reduce");
+  }
   LSB_REQUIRE(epilogue != LSB_EPI_SWIGLU || N % kBM == 0,
               "gemm: the SwiGLU epilogue needs N %% 128 == 0 (N=%lld)", (long long)N);
   LSB_REQUIRE(N < (int64_t(1) << 31) && K < (int64_t(1) << 31) && M < (int64_t(1) << 31),
               "gemm: dimension too large");
   LSB_REQUIRE(ldx % 8 == 0 && ldw % 8 == 0 && ldx >= K && ldw >= K,
               "gemm: ldx/ldw must be multiples of 8 (16-byte TMA strides) and >= K");
+  LSB_REQUIRE(K + K2 < (int64_t(1) << 31), "gemm: dimension too large");
   LSB_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 2),
               "gemm: x and w must be 16-byte aligned");
   LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue <= LSB_EPI_SWIGLU, "gemm: bad epilogue");
@@ -695,17 +734,27 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   if (M <= 0) return LSB_OK;
   // The all-reduce variant waits on the same CTA of every rank: its whole grid must be
   // resident at once, so it keeps one CTA per SM and at most one wave.
-  Plan pl = plan_for(M, N, K, comm != nullptr);
-  CUtensorMap tw, tx;
+  const int64_t kb1 = (K + kBK - 1) / kBK;
+  const int64_t kb2 = (K2 + kBK - 1) / kBK;
+  Plan pl = plan_for(M, N, (kb1 + kb2) * kBK, comm != nullptr);
+  CUtensorMap tw, tx, tw2, tx2;
   if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
   if (int rc = make_tmap(&tx, x, M, K, ldx, pl.bn)) return rc;
+  if (seg2) {  // each segment's last K block is zero-filled past its own width
+    if (int rc = make_tmap(&tw2, static_cast<const bf16*>(w) + K, N, K2, ldw, kBM)) return rc;
+    if (int rc = make_tmap(&tx2, seg2->x2, M, K2, seg2->ldx2, pl.bn)) return rc;
+  } else {
+    tw2 = tw;
+    tx2 = tx;
+  }
   GemmParams p;
   p.y = static_cast<bf16*>(y);
   p.ldy = ldy;
   p.bias = static_cast<const bf16*>(bias);
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
-  p.K = static_cast<int>(K);
+  p.K = static_cast<int>((kb1 + kb2) * kBK);  // sets the K-block count of the whole loop
+  p.kb1 = static_cast<int>(kb1);
   p.bn = pl.bn;
   p.stages = pl.stages;
   p.splits = pl.splits;
@@ -742,7 +791,7 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   }
   cfg.attrs = attrs;
   cfg.numAttrs = nattr;
-  LSB_CUDA(cudaLaunchKernelEx(&cfg, kernel, tw, tx, p));
+  LSB_CUDA(cudaLaunchKernelEx(&cfg, kernel, tw, tx, tw2, tx2, p));
   return check_launch("lsb_gemm");
 }
 
@@ -753,6 +802,14 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   (void)workspace;
   (void)workspace_bytes;
   return gemm_impl(y, ldy, x, ldx, w, ldw, bias, M, N, K, epilogue, nullptr, stream);
+}
+
+extern "C" int lsb_gemm_concat(void* y, int64_t ldy, const void* x1, int64_t ldx1,
+                               const void* x2, int64_t ldx2, const void* w, int64_t ldw,
+                               const void* bias, int64_t M, int64_t N, int64_t K1, int64_t K2,
+                               int32_t epilogue, void* stream) {
+  const Segment2 seg{x2, ldx2, K2};
+  return gemm_impl(y, ldy, x1, ldx1, w, ldw, bias, M, N, K1, epilogue, nullptr, stream, &seg);
 }
 
 extern "C" int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x,

@@ -159,13 +159,30 @@ def bench_gemm(args, ops, name: str) -> dict:
     us = _time_graph(launch, args.reps)
     nbytes = w_bytes + m * k * 2 + m * cols * 2
     flops = 2.0 * m * n * k
-    return {"kernel": "gemm", "shape": name, "tp": args.tp, "tokens": m, "N": n, "K": k,
-            "swiglu": swiglu,
-            "weight_copies": copies, "algorithmic_bytes": nbytes, "us": round(us, 2),
-            "GBps": round(nbytes / us / 1e3, 1), "TFLOPs": round(flops / us / 1e6, 1)}
+    out = {"kernel": "gemm", "shape": name, "tp": args.tp, "tokens": m, "N": n, "K": k,
+           "swiglu": swiglu,
+           "weight_copies": copies, "algorithmic_bytes": nbytes, "us": round(us, 2),
+           "GBps": round(nbytes / us / 1e3, 1), "TFLOPs": round(flops / us / 1e6, 1)}
+    if args.cublas:
+        # the reference's GPU path for the same product: F.linear (cuBLAS bf16), and for
+        # gate_up its separate SiLU*mul (models/utils.py:45-50); same rotating weights
+        import torch.nn.functional as F
+
+        yc = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        us_c = _time_graph(lambda i: torch.matmul(x, ws[i % copies].t(), out=yc), args.reps)
+        out["us_cublas"] = round(us_c, 2)
+        if swiglu:
+            half = n // 2
+
+            def ref_swiglu(i):
+                torch.matmul(x, ws[i % copies].t(), out=yc)
+                torch.mul(F.silu(yc[:, :half]), yc[:, half:], out=y)
+
+            out["us_cublas_plus_silu_mul"] = round(_time_graph(ref_swiglu, args.reps), 2)
+    return out
 
 
-def bench_gemm_ar(args, ops, comm, name: str) -> dict:
+def bench_gemm_ar(args, ops, comm, name: str, nccl=None) -> dict:
     """One row-parallel shard GEMM fused with its NVLink all-reduce (every rank runs it),
     next to the same local GEMM alone; the max over ranks of the per-launch time."""
     import torch.distributed as dist
@@ -185,15 +202,40 @@ def bench_gemm_ar(args, ops, comm, name: str) -> dict:
     us_local = _time_graph(lambda i: ops.gemm(x, ws[i % copies], out=y), args.reps)
     dist.barrier()
     us_allreduce = _time_graph(lambda i: comm.all_reduce(y), args.reps)
-    t = torch.tensor([us_ar, us_local, us_allreduce], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us_nccl = us_cublas = 0.0
+    if nccl is not None:
+        # the reference's path: F.linear (cuBLAS) then an NCCL all-reduce of the result
+        dist.barrier()
+        yc = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+
+        def ref_path(i):
+            torch.matmul(x, ws[i % copies].t(), out=yc)
+            dist.all_reduce(yc, group=nccl)
+
+        us_nccl = _time_graph(ref_path, args.reps)
+        dist.barrier()
+        us_cublas = _time_graph(lambda i: torch.matmul(x, ws[i % copies].t(), out=yc), args.reps)
+    t = torch.tensor([us_ar, us_local, us_allreduce, us_nccl, us_cublas], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl) if nccl is not None else \
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
     us_ar, us_local, us_allreduce = float(t[0]), float(t[1]), float(t[2])
     link = 2 * (tp - 1) / tp * m * n * 2  # bytes each rank sends: partials + sums
-    return {"kernel": "gemm_allreduce", "shape": name, "tp": tp, "tokens": m, "N": n, "K": k,
-            "us": round(us_ar, 2), "us_local_gemm": round(us_local, 2),
-            "us_allreduce_alone": round(us_allreduce, 2),
-            "weight_GBps": round(w_bytes / us_ar / 1e3, 1),
-            "nvlink_bytes": int(link), "nvlink_GBps": round(link / us_ar / 1e3, 1)}
+    out = {"kernel": "gemm_allreduce", "shape": name, "tp": tp, "tokens": m, "N": n, "K": k,
+           "us": round(us_ar, 2), "us_local_gemm": round(us_local, 2),
+           "us_allreduce_alone": round(us_allreduce, 2),
+           "weight_GBps": round(w_bytes / us_ar / 1e3, 1),
+           "nvlink_bytes": int(link), "nvlink_GBps": round(link / us_ar / 1e3, 1)}
+    if nccl is not None:
+        out["us_cublas_plus_nccl"] = round(float(t[3]), 2)
+        out["us_cublas"] = round(float(t[4]), 2)
+    # roofline of the fused kernel: the slower of the weight stream from HBM and the bytes
+    # that must cross NVLink (one all-reduce's worth, (t-1)/t of the output each way)
+    peaks = pathlib.Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    hbm = json.loads(peaks.read_text())["hbm_gbs"] if peaks.exists() else 6650.0
+    bound_us = max(w_bytes / hbm / 1e3, (tp - 1) / tp * m * n * 2 / 770.0 / 1e3)
+    out["roofline_us"] = round(bound_us, 3)
+    out["roofline_frac"] = round(bound_us / us_ar, 4)
+    return out
 
 
 def bench_norm(args, ops) -> dict:
@@ -268,10 +310,14 @@ def main(argv=None) -> None:
                     choices=sorted(OURO_GEMMS))
     gm.add_argument("--reps", type=int, default=60)
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
+    gm.add_argument("--cublas", action="store_true",
+                    help="also time torch.matmul (cuBLAS) on the same shapes and weights")
     ga = sub.add_parser("gemm_ar")
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
     ga.add_argument("--reps", type=int, default=60)
+    ga.add_argument("--vs-nccl", action="store_true",
+                    help="also time F.linear (cuBLAS) + an NCCL all-reduce on the same shapes")
     nm = sub.add_parser("norm")
     nm.add_argument("--rows", type=int, default=263)
     nm.add_argument("--reps", type=int, default=100)
@@ -295,8 +341,9 @@ def main(argv=None) -> None:
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
         comm = C.B200Communicator(rank, world, args.tokens * 8192)
+        nccl = dist.new_group(backend="nccl") if args.vs_nccl else None
         for name in args.shape:
-            line = bench_gemm_ar(args, ops, comm, name)
+            line = bench_gemm_ar(args, ops, comm, name, nccl)
             if rank == 0:
                 print(json.dumps(line), flush=True)
         comm.close()

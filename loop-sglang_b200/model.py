@@ -401,7 +401,8 @@ class LoopedDecoder:
             ops.ouro_step_exit(d, residual, last.norms[3], self.norm, c.rms_eps, hidden_out=out)
             return out
         step = loop_step if isinstance(loop_step, int) else None
-        x = ops.linear(torch.cat([hidden, injection], dim=-1), self.adapter, self.adapter_b)
+        # adapter(cat[h, injection]) (huginn.py:162-167): the GEMM's K loop reads both halves
+        x = ops.gemm_concat(hidden, injection, self.adapter, self.adapter_b)
         for i, name in enumerate(self.core_names):
             layer = core_cache_layer_index(self.policy, c, i, step if step is not None else 0)
             x = self._huginn_layer(self.layers[name], x, layer, batch, kv)

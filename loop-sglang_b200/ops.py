@@ -28,7 +28,7 @@ from ._lib import (
 __all__ = [
     "rmsnorm", "fused_add_rmsnorm", "sandwich_norm", "rope_store_kv", "rope_only", "store_kv",
     "paged_attention",
-    "gemm", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
+    "gemm", "gemm_concat", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
     "gather_rows", "argmax", "argmax_sharded", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
     "last_exited_release", "cdb_route", "cdb_admit", "device_error_word", "Workspace", "prepare_batch_inputs",
     "set_metadata",
@@ -220,6 +220,27 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     call("lsb_gemm", out.data_ptr(), _row_stride(out, "out"), x.data_ptr(),
          _row_stride(x, "x"), w.data_ptr(), _row_stride(w, "w"), _p(bias), m, n, k, epilogue,
          _p(ws), 0 if ws is None else ws.numel(), _stream())
+    return out
+
+
+def gemm_concat(x1: torch.Tensor, x2: torch.Tensor, w: torch.Tensor,
+                bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``F.linear(torch.cat([x1, x2], -1), w, bias)`` without the concatenation
+    (models/looped/huginn.py:162-167, Huginn's adapter)."""
+    for t, n in ((x1, "x1"), (x2, "x2"), (w, "w")):
+        _need(t, BF16, n, contiguous=False)
+    m, k1 = x1.shape
+    k2 = x2.shape[1]
+    n = w.shape[0]
+    if x2.shape[0] != m or w.shape[1] != k1 + k2:
+        raise ValueError(f"gemm_concat: x1 [{m}, {k1}], x2 {list(x2.shape)}, w {list(w.shape)}")
+    if bias is not None:
+        _need(bias, BF16, "bias")
+    out = torch.empty(m, n, dtype=BF16, device=x1.device) if out is None else out
+    call("lsb_gemm_concat", out.data_ptr(), _row_stride(out, "out"), x1.data_ptr(),
+         _row_stride(x1, "x1"), x2.data_ptr(), _row_stride(x2, "x2"), w.data_ptr(),
+         _row_stride(w, "w"), _p(bias), m, n, k1, k2,
+         LSB_EPI_BIAS if bias is not None else LSB_EPI_NONE, _stream())
     return out
 
 

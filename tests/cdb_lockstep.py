@@ -80,20 +80,21 @@ def prefill_batch(sc: Scenario):
     return ids, pos, loc, seq, cu
 
 
-def oracle_run(cfg, weights, sc: Scenario, use_replay: bool = True, steps: int | None = None):
-    """Lock-step restatement of ``CDBDecodeEngine`` on the oracle (bf16).
+def oracle_run(cfg, weights, sc: Scenario, use_replay: bool = True, steps: int | None = None,
+               dtype: torch.dtype = torch.bfloat16):
+    """Lock-step restatement of ``CDBDecodeEngine`` on the oracle (bf16 rounding points; fp32
+    arithmetic throughout with ``dtype=torch.float32``, on the same bf16-valued weights).
 
     Returns a dict: ``preds`` [B][K] tokens, ``topk`` [B][K] (values, ids, max |logit|)
     of the logits at each output, ``hidden`` [B][K] the exiting rows' hidden, ``depths``
     [B][K], ``pool`` (the oracle pool), ``gates`` per step (signals, exit state, depth).
     """
-    w = {k: v.to(torch.bfloat16) for k, v in weights.items()}
+    w = {k: v.to(torch.bfloat16).to(dtype) for k, v in weights.items()}
     model = LoopedModel(cfg, with_fp32_matrices(w), "last_exited")
     b = len(sc.prompts)
     steps = sc.steps if steps is None else steps
     assert model.slot_layout().slots_per_token == sc.slots_per_token
-    pool = SlotKVPool(model.slot_layout(), sc.num_pages, cfg.kv_heads, cfg.head_dim,
-                      torch.bfloat16)
+    pool = SlotKVPool(model.slot_layout(), sc.num_pages, cfg.kv_heads, cfg.head_dim, dtype)
     ids, pos, loc, seq, cu = prefill_batch(sc)
     pool.versions.reserve(loc.numpy())
     model.forward(Batch(ids, pos, loc, sc.handles.clone(), seq, cu, True), pool)
@@ -101,7 +102,7 @@ def oracle_run(cfg, weights, sc: Scenario, use_replay: bool = True, steps: int |
     cur_ids = sc.first.clone()
     depth = torch.zeros(b, dtype=torch.int32)
     slots = torch.arange(1, b + 1)
-    state = {"hidden": torch.zeros(b + 1, cfg.hidden, dtype=torch.bfloat16),
+    state = {"hidden": torch.zeros(b + 1, cfg.hidden, dtype=dtype),
              "exit": torch.zeros(b + 1, dtype=torch.float32)}
     cur = sc.handles[torch.arange(b), seq.long() - 1]
     pool.versions.reserve(cur.numpy())

@@ -10,11 +10,13 @@ including the reference's fp32 run of BASELINE configs[0]) on the scenarios of
 
 * CB: for the prefill and 4 greedy decode steps, the oracle in bf16 (the reference's
   rounding points) -- logits on every 24th vocabulary column, the top 8 logits and
-  the LM-head input rows -- and the oracle in fp32 on the same (bf16-valued) weights
-  and inputs (its top 8 logits: greedy agreement of bf16 against fp32 arithmetic).
+  the LM-head input rows -- and the same for the oracle in fp32 on the same
+  (bf16-valued) weights and inputs: how far bf16 arithmetic itself lands from exact
+  arithmetic after 96 layer passes, the floor any bf16 implementation is held to.
 * CDB: the lock-step restatement of the device-routed engine (``tests/cdb_lockstep.py``)
   in bf16: every output's token, top 8 logits and hidden row, its exit depth, and the
-  final version map, completed depths and free-slot stack of the last-exited pool.
+  final version map, completed depths and free-slot stack of the last-exited pool; and
+  the hidden rows of the same run in fp32.
 
 The GPU test rebuilds the same weights and inputs from the seeds, so only outputs
 are stored.
@@ -97,7 +99,9 @@ def run_cb_part(out: dict, t0: float) -> None:
     out["cb_bf16_scale"] = torch.stack([x.abs().max(-1).values for x in lg]).numpy()
     print(f"cb bf16 {time.time() - t0:.0f}s", flush=True)
 
-    _, lg32, _ = run_cb(torch.float32, fed)
+    hid32, lg32, _ = run_cb(torch.float32, fed)
+    out["cb_fp32_hidden"] = torch.stack(hid32).numpy()
+    out["cb_fp32_probe"] = torch.stack([x[:, cols] for x in lg32]).numpy()
     top = [x.topk(S.TOPK, dim=-1) for x in lg32]
     out["cb_fp32_top_v"] = torch.stack([t.values for t in top]).numpy()
     out["cb_fp32_top_i"] = torch.stack([t.indices for t in top]).to(torch.int32).numpy()
@@ -119,6 +123,8 @@ def run_cdb_part(out: dict, t0: float) -> None:
     out["cdb_scale"] = np.array([[ref["topk"][r][j][2] for j in range(k)] for r in range(b)],
                                 dtype=np.float32)
     out["cdb_hidden"] = np.stack([S.bf16_bits(torch.stack(ref["hidden"][r])) for r in range(b)])
+    ref32 = oracle_run(S.OURO_14B_GATED, S.weights(), sc, dtype=torch.float32)
+    out["cdb_fp32_hidden"] = np.stack([torch.stack(ref32["hidden"][r]).numpy() for r in range(b)])
     v = ref["pool"].versions
     out["cdb_slot_map"] = np.asarray(v.slot_map, dtype=np.int32)
     out["cdb_completed_depth"] = np.asarray(v.completed_depth, dtype=np.int32)

@@ -295,6 +295,25 @@ def test_gemm_epilogues(epi: str, m: int) -> None:
     no_device_errors()
 
 
+@pytest.mark.parametrize("m,n,k1,k2", [
+    (5, 5280, 5280, 5280),    # Huginn adapter: [h | injection] . W^T, K blocks of 64 straddle
+    (130, 5280, 5280, 5280),  # each segment's end (5280 = 82.5 blocks)
+    (17, 256, 40, 72),        # short, unaligned segments
+])
+def test_gemm_concat_matches_linear_of_cat(m: int, n: int, k1: int, k2: int) -> None:
+    g = gen(m + k1)
+    x1 = bf(torch.randn(m, k1, generator=g))
+    x2 = bf(torch.randn(m, k2, generator=g))
+    w = bf(torch.randn(n, k1 + k2, generator=g) * 0.02)
+    b = bf(torch.randn(n, generator=g))
+    ref = O.linear(torch.cat([x1, x2], dim=-1), w, b)
+    for _ in range(2):
+        close(ops.gemm_concat(x1.to(DEV), x2.to(DEV), w.to(DEV), b.to(DEV)), ref)
+    close(ops.gemm_concat(x1.to(DEV), x2.to(DEV), w.to(DEV)),
+          O.linear(torch.cat([x1, x2], dim=-1), w))
+    no_device_errors()
+
+
 def test_gemm_rejects_bad_shapes() -> None:
     x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)  # row stride 200 B: not TMA-able
     w = torch.zeros(128, 100, dtype=torch.bfloat16, device=DEV)

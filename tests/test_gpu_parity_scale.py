@@ -9,13 +9,20 @@ size, through the CUDA path.
   apart); greedy agreement with the reference's fp32 run at least that of the bf16
   oracle itself (the part bf16 arithmetic alone costs) less two tokens.
 * Ouro-1.4B CB (configs[1] shapes): a real prefill of 4 requests with prompts of
-  256-1024 tokens, then 4 greedy decode steps; LM-head rows and logits within 2e-2 of the
-  bf16 oracle (``tests/golden/ouro14b_fullsize.npz``, made by
-  ``tests/golden/make_fullsize.py``), tokens equal up to near ties.
+  256-1024 tokens, then 4 greedy decode steps, against the oracle
+  (``tests/golden/ouro14b_fullsize.npz``, made by ``tests/golden/make_fullsize.py``):
+  tokens equal to the bf16 oracle's up to near ties. After 96 layer passes of a
+  random-init model, summation order alone moves bf16 results by several percent: the
+  bf16 oracle's own logits and LM-head rows sit 7-8% (max |diff| / max |value|) from the
+  same computation in fp32 arithmetic. So the CUDA path's logits and rows must be within
+  max(2e-2, 1.5 x that floor) of the fp32 result (as exact as the reference's bf16
+  arithmetic), and within max(2e-2, 2 x the floor) of the bf16 oracle (two bf16
+  computations, each that far from exact).
 * Ouro-1.4B CDB (configs[2] shapes, last-exited KV): the device-routed engine after a
   real prefill, exit depths prescribed from the 15/25/30/30% mix: tokens (near-tie
-  aware) and the hidden row of every output against the lock-step oracle; exit depths,
-  version maps, completed depths and the free-slot stack bit-exact.
+  aware) against the lock-step oracle, the hidden row of every output held to the same
+  floor-relative bounds; exit depths, version maps, completed depths and the free-slot
+  stack bit-exact.
 """
 
 from __future__ import annotations
@@ -95,7 +102,9 @@ def test_configs0_greedy_agreement() -> None:
     print(summary)
     assert worst < REL, summary
     assert counts["mismatch"] == 0, summary
-    assert counts["agree"] >= 0.97 * total, summary
+    # greedy agreement on the tokens whose top two logits are further apart than the bf16
+    # tolerance (near ties are counted, not scored)
+    assert counts["agree"] / (counts["agree"] + counts["mismatch"]) >= 0.99, summary
     assert gpu_fp32 >= oracle_fp32 - 2, summary
 
 
@@ -114,7 +123,8 @@ def test_ouro14b_cb_prefill_decode_matches_oracle(fullsize) -> None:
     kv = model.make_kv_cache(num_pages, S.PAGE)
     dev = model.device
     counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
-    fp32_agree, worst_logits, worst_hidden = 0, 0.0, 0.0
+    fp32_agree = 0
+    report = []
     for i, step in enumerate(range(-1, S.CB_DECODE)):
         ids = torch.from_numpy(fx["cb_decode_ids"][step]) if step >= 0 else None
         b = S.cb_batch(step, ids, table)
@@ -128,19 +138,30 @@ def test_ouro14b_cb_prefill_decode_matches_oracle(fullsize) -> None:
         rows = model._lm_rows(model.forward_coda(h, db, kv), db)
         logits = ops.gemm(rows, model.lm_head_w).float().cpu()
         want_h = S.from_bf16_bits(fx["cb_bf16_hidden"][i])
-        worst_hidden = max(worst_hidden, rel_err(rows.cpu(), want_h))
+        h32 = torch.from_numpy(fx["cb_fp32_hidden"][i])
         rel, verdicts = S.logits_match(
             logits, torch.from_numpy(fx["cb_bf16_probe"][i]), torch.from_numpy(fx["cb_bf16_top_v"][i]),
             torch.from_numpy(fx["cb_bf16_top_i"][i]), torch.from_numpy(fx["cb_bf16_scale"][i]))
-        worst_logits = max(worst_logits, rel)
+        cols = S.probe_columns(logits.shape[1])
+        probe32 = torch.from_numpy(fx["cb_fp32_probe"][i])
+        got_h = rows.float().cpu()
+        report.append({
+            "logits_vs_bf16": rel, "logits_vs_fp32": rel_err(logits[:, cols], probe32),
+            "logits_floor": rel_err(torch.from_numpy(fx["cb_bf16_probe"][i]), probe32),
+            "hidden_vs_bf16": rel_err(got_h, want_h), "hidden_vs_fp32": rel_err(got_h, h32),
+            "hidden_floor": rel_err(want_h, h32)})
         for v in verdicts:
             counts[v] += 1
         fp32_agree += int((logits.argmax(-1).numpy() == fx["cb_fp32_top_i"][i][:, 0]).sum())
     summary = (f"Ouro-1.4B CB: prefill + {S.CB_DECODE} decode steps x {len(S.CB_PROMPTS)} rows; "
-               f"vs bf16 oracle {counts}; vs fp32 oracle {fp32_agree}; rel err logits "
-               f"{worst_logits:.4f}, hidden {worst_hidden:.4f}")
+               f"vs bf16 oracle {counts}; vs fp32 oracle {fp32_agree} agree; per step "
+               + "; ".join(", ".join(f"{k} {v:.4f}" for k, v in r.items()) for r in report))
     print(summary)
-    assert worst_logits < REL and worst_hidden < REL, summary
+    for r in report:
+        for what in ("logits", "hidden"):
+            floor = r[f"{what}_floor"]
+            assert r[f"{what}_vs_fp32"] <= max(REL, 1.5 * floor), summary
+            assert r[f"{what}_vs_bf16"] <= max(REL, 2.0 * floor), summary
     assert counts["mismatch"] == 0, summary
     assert ops.device_error_word(reset=True) == 0
     del model, kv
@@ -168,7 +189,7 @@ def test_ouro14b_cdb_engine_matches_oracle(fullsize) -> None:
     toks, deps = eng.out_tokens.cpu(), eng.out_depths.cpu()
     b, k_out = len(sc.prompts), sc.k
     counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
-    worst = 0.0
+    report = []
     for r in range(b):
         assert deps[r, :k_out].tolist() == fx["cdb_depths"][r].tolist() == sc.replay[r].tolist()
         for k in range(k_out):
@@ -176,11 +197,16 @@ def test_ouro14b_cdb_engine_matches_oracle(fullsize) -> None:
                     float(fx["cdb_scale"][r, k]))
             counts[token_matches(int(toks[r, k]), int(fx["cdb_preds"][r, k]), topk)] += 1
             want = S.from_bf16_bits(fx["cdb_hidden"][r, k])
-            worst = max(worst, rel_err(got_hidden[(r, k)], want))
-    summary = f"Ouro-1.4B CDB: {b} rows x {k_out} outputs vs the oracle {counts}; hidden {worst:.4f}"
+            h32 = torch.from_numpy(fx["cdb_fp32_hidden"][r, k])
+            got = got_hidden[(r, k)].float()
+            report.append((rel_err(got, want), rel_err(got, h32), rel_err(want, h32)))
+    summary = (f"Ouro-1.4B CDB: {b} rows x {k_out} outputs vs the oracle {counts}; hidden "
+               "(vs bf16, vs fp32, floor) " + "; ".join(f"{a:.4f} {c:.4f} {f:.4f}"
+                                                        for a, c, f in report))
     print(summary)
     assert counts["mismatch"] == 0, summary
-    assert worst < REL, summary
+    for vs_bf16, vs_fp32, floor in report:
+        assert vs_fp32 <= max(REL, 1.5 * floor) and vs_bf16 <= max(REL, 2.0 * floor), summary
     assert np.array_equal(kv.slot_map.cpu().numpy(), fx["cdb_slot_map"])
     assert np.array_equal(kv.completed_depth.cpu().numpy(), fx["cdb_completed_depth"])
     n = int(fx["cdb_free_count"])
@@ -188,4 +214,65 @@ def test_ouro14b_cdb_engine_matches_oracle(fullsize) -> None:
     assert np.array_equal(kv._free_slots.cpu().numpy()[:n], fx["cdb_free_slots"])
     assert ops.device_error_word(reset=True) == 0
     del model, kv, eng
+    _free()
+
+
+# Huginn at full width (configs[4]: hidden 5280, 55 heads x 96, SwiGLU 17920, RoPE 5e4,
+# embedding scale sqrt(5280), q/k/v bias) with one prelude, one core and one coda layer,
+# two recurrences and a reduced vocabulary: every kernel at the shapes configs[4] runs,
+# including the adapter's two-segment GEMM.
+HUGINN_WIDE = LoopedConfig(arch="huginn", hidden=5280, heads=55, kv_heads=55, head_dim=96,
+                           intermediate=17920, vocab=8192, num_prelude_layers=1,
+                           num_core_layers=1, num_coda_layers=1, loop_steps=2,
+                           rope_theta=50000.0, max_position=1024, embed_scale=5280 ** 0.5,
+                           attention_bias=True)
+
+
+def test_huginn_full_width_layers_match_oracle() -> None:
+    from loop_sglang_b200.model import DeviceBatch
+    from oracle.model import Batch
+
+    cfg, page, prompts, steps = HUGINN_WIDE, 16, [24, 40], 2
+    w32 = make_weights(cfg, 9, dtype=torch.float32)
+    model = gpu_model(cfg, w32, "shared")
+    oracle = LoopedModel(cfg, with_fp32_matrices({k: v.to(torch.bfloat16) for k, v in w32.items()}),
+                         "shared")
+    del w32
+    b = len(prompts)
+    pages_per = (max(prompts) + steps + page) // page
+    table = (1 + torch.arange(b).view(-1, 1) * pages_per + torch.arange(pages_per)).to(torch.int32)
+    num_pages = b * pages_per + 1
+    kv = model.make_kv_cache(num_pages, page)
+    pool = PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads, cfg.head_dim,
+                       torch.bfloat16)
+    g = torch.Generator().manual_seed(4)
+    ids = torch.cat([torch.randint(0, cfg.vocab, (n,), generator=g) for n in prompts]).to(torch.int32)
+    lens = torch.tensor(prompts, dtype=torch.int32)
+    counts = {"agree": 0, "near_tie": 0, "mismatch": 0}
+    for step in range(-1, steps):
+        if step < 0:
+            pos = torch.cat([torch.arange(n) for n in prompts]).to(torch.int32)
+            rows = torch.cat([torch.full((n,), r) for r, n in enumerate(prompts)])
+            seq, cu = lens.clone(), torch.zeros(b + 1, dtype=torch.int32)
+            cu[1:] = torch.cumsum(lens, 0)
+        else:
+            pos, rows = (lens + step).to(torch.int32), torch.arange(b)
+            seq, cu = lens + step + 1, torch.arange(b + 1, dtype=torch.int32)
+        loc = (table[rows, (pos // page).long()] * page + pos % page).to(torch.int32)
+        ob = Batch(ids, pos, loc, table.clone(), seq.to(torch.int32), cu, step < 0)
+        db = DeviceBatch(ids.cuda(), pos.cuda(), loc.cuda(), table.cuda(), ob.cache_seqlens.cuda(),
+                         cu.cuda(), step < 0, max_seqlen=pages_per * page)
+        got = model.forward(db, kv).float().cpu()
+        ref = oracle.forward(ob, pool).float()
+        err = rel_err(got, ref)
+        assert err < REL, f"Huginn full width, step {step}: logits rel err {err:.4f}"
+        for v in verdict_full(got, ref):
+            counts[v] += 1
+        ids = ref.argmax(-1).to(torch.int32)
+    print(f"Huginn full width: {counts}")
+    assert counts["mismatch"] == 0, counts
+    from loop_sglang_b200 import ops
+
+    assert ops.device_error_word(reset=True) == 0
+    del model, kv
     _free()
