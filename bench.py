@@ -722,6 +722,8 @@ def run_b200(args) -> None:
 
 
 # ------------------------------------------------------- CDB workload --
+E2E_STEPS = 30  # steps of the host-buffer e2e leg (CDB), after the timed device steps
+
 # Ouro-1.4B with early exit under continuous-depth batching, exit
 # threshold 0.2, last-exited KV; 512 requests, prompt U[256, 1024], 512 outputs. The exit
 # steps follow 15/25/30/30% at loop steps 1-4, prescribed per output token (the reference's
@@ -837,17 +839,21 @@ def run_b200_cdb(args) -> None:
     torch.cuda.empty_cache()
     rng = np.random.default_rng(SEED)
     prompts = rng.integers(CDB_PROMPT_RANGE[0], CDB_PROMPT_RANGE[1] + 1, CDB_NUM_REQS)
-    steps_total = args.warmup + args.steps + 1 + (args.steps if not args.no_e2e else 0) + 1
+    e2e_steps = 0 if args.no_e2e else min(args.steps, E2E_STEPS)
+    steps_total = args.warmup + args.steps + 1 + e2e_steps + 1
     ctx = prompts + CDB_MID  # tokens before the one being decoded
     gen_depth = cdb_depths(CDB_NUM_REQS * CDB_MID, SEED + 1).reshape(CDB_NUM_REQS, CDB_MID)
     # exit depths of the outputs to come (the replay depths of the run)
     out_cap = steps_total + 8
     future_all = cdb_depths(CDB_NUM_REQS * out_cap, SEED + 2).reshape(CDB_NUM_REQS, out_cap)
     exits = (np.cumsum(future_all, axis=1) <= steps_total).sum(1)  # outputs finished in the run
+    # the versions those outputs keep: each reserves a full-depth token and keeps its exit
+    # depth's versions once it exits (the rest go back to the shared free stack)
+    kept = np.array([future_all[r, :exits[r]].sum() for r in range(CDB_NUM_REQS)])
     # version slots a request holds: prompt tokens keep every loop step (prefill runs at full
     # depth), generated ones their exit depth; plus the token being decoded and one fresh
     # full-depth token per output the run finishes (reserved before the exit aliases)
-    need = prompts * 4 + gen_depth.sum(1) + 4 * (exits + 2)
+    need = prompts * 4 + gen_depth.sum(1) + kept + 4 * 2  # + the token in flight, + margin
     max_len = int(ctx.max()) + steps_total + 2
     slot_bytes = 2 * cfg.num_core_layers * model.hkv * cfg.head_dim * 2
     free, _ = torch.cuda.mem_get_info(dev)
@@ -921,7 +927,7 @@ def run_b200_cdb(args) -> None:
         p1 = int(eng.produced.item())
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
-        for _ in range(args.steps):
+        for _ in range(e2e_steps):
             with torch.cuda.stream(s):
                 eng.rpi.copy_(host_rows, non_blocking=True)
                 eng.replay()

@@ -181,6 +181,27 @@ int lsb_gemm_concat(void* y, int64_t ldy, const void* x1, int64_t ldx1, const vo
                     int64_t ldx2, const void* w, int64_t ldw, const void* bias, int64_t M,
                     int64_t N, int64_t K1, int64_t K2, int32_t epilogue, void* stream);
 
+/* Greedy sampling fused into the LM-head GEMM (layers/embedding.py:89-111 +
+ * model_executor/sample.py:108-112): for every row m of x and every 128-entry
+ * vocabulary tile t of w [N, K], pairs[m * ld_pairs + t] = {float value, int32
+ * index} of the largest bf16-rounded logit in the tile (first index on ties), so
+ * the [M, N] logits are never written. ld_pairs >= lsb_gemm_argmax_tiles(N)
+ * (the tile count rounded up to even, so a row of pairs is a multiple of 16
+ * bytes); pairs 8-byte aligned. Tensor-parallel ranks pass their own vocabulary
+ * range's valid row count as N (padding rows are never scored) and all-gather
+ * the pairs instead of the logits. */
+int64_t lsb_gemm_argmax_tiles(int64_t N);
+int lsb_gemm_argmax(void* pairs, int64_t ld_pairs, const void* x, int64_t ldx, const void* w,
+                    int64_t ldw, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* out[m] = the global index of the best pair of row m over `shards` blocks of
+ * pairs [shards][rows][ld_pairs] (the first `tiles` of each row scored), shard
+ * s covering global indices s*shard_cols ..: the argmax of the gathered,
+ * permuted logits of layers/embedding.py:99-111 with torch.argmax's first-index
+ * rule. Unscored tiles must hold value -inf. */
+int lsb_argmax_pairs(int32_t* out, const void* pairs, int64_t shards, int64_t rows,
+                     int64_t tiles, int64_t ld_pairs, int64_t shard_cols, void* stream);
+
 /* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
  * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
  * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */

@@ -46,6 +46,15 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kSmemPerSm = 228 * 1024;
 
+// Internal epilogue of the LM head: per row and 128-entry vocabulary tile, the largest
+// bf16-rounded logit and its index (greedy sampling without writing the logits).
+constexpr int kEpiArgmax = 4;
+
+struct ArgmaxPair {
+  float value;
+  int32_t index;
+};
+
 struct GemmParams {
   bf16* y;
   int64_t ldy;
@@ -401,7 +410,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
         const int col = n0 + 4 * qi;
         float o0 = a.x, o1 = a.y, o2 = a.z, o3 = a.w;
-        if (EPI != LSB_EPI_NONE) {
+        if (EPI == kEpiArgmax) {
+          // greedy sampling over the tile's 128 vocabulary entries of this row: the largest
+          // bf16-rounded logit, the first index on ties (torch.argmax over the bf16
+          // logits); the 32 lanes of the warp hold the row's 32 quads
+          const float v4[4] = {round_bf16(o0), round_bf16(o1), round_bf16(o2), round_bf16(o3)};
+          float best = -INFINITY;
+          int best_i = 0x7fffffff;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (col + e < p.N && v4[e] > best) { best = v4[e]; best_i = col + e; }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (ob > best || (ob == best && oi < best_i)) { best = ob; best_i = oi; }
+          }
+          if (lane == 0) {
+            ArgmaxPair pr;
+            pr.value = best;
+            pr.index = best_i;
+            reinterpret_cast<ArgmaxPair*>(y)[static_cast<int64_t>(m0 + m) * ldy + tile_n] = pr;
+          }
+          continue;
+        }
+        if (EPI == LSB_EPI_BIAS || EPI == LSB_EPI_BIAS_AFTER_ROUND) {
           const float b0 = col < p.N ? __bfloat162float(p.bias[col]) : 0.f;
           const float b1 = col + 1 < p.N ? __bfloat162float(p.bias[col + 1]) : 0.f;
           const float b2 = col + 2 < p.N ? __bfloat162float(p.bias[col + 2]) : 0.f;
@@ -514,13 +547,15 @@ using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                         const CUtensorMap, GemmParams);
 
 Kernel kernel_for(bool cluster, int epilogue, bool ar = false) {
-  static const Kernel kernels[2][4] = {
+  static const Kernel kernels[2][5] = {
       {gemm_tcgen05_kernel<LSB_EPI_NONE, false, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, false>,
        gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false, false>,
-       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false, false>},
+       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false, false>,
+       gemm_tcgen05_kernel<kEpiArgmax, false, false>},
       {gemm_tcgen05_kernel<LSB_EPI_NONE, true, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, false>,
        gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true, false>,
-       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true, false>}};
+       gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true, false>,
+       gemm_tcgen05_kernel<kEpiArgmax, true, false>}};
   static const Kernel ar_kernels[2][2] = {
       {gemm_tcgen05_kernel<LSB_EPI_NONE, false, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, true>},
       {gemm_tcgen05_kernel<LSB_EPI_NONE, true, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, true>}};
@@ -534,10 +569,10 @@ constexpr int kMaxSmem = 227 * 1024;
 // the launch and the occupancy queries below).
 int configure(bool cluster, int epilogue, bool ar = false) {
   static std::mutex mu;
-  static uint64_t done[64] = {0};  // bit (ar*8 + cluster*4 + epilogue) per device
+  static uint64_t done[64] = {0};  // bit (ar*16 + cluster*8 + epilogue) per device
   int dev = 0;
   LSB_CUDA(cudaGetDevice(&dev));
-  const uint64_t bit = uint64_t(1) << ((ar ? 8 : 0) + (cluster ? 4 : 0) + epilogue);
+  const uint64_t bit = uint64_t(1) << ((ar ? 16 : 0) + (cluster ? 8 : 0) + epilogue);
   std::lock_guard<std::mutex> lock(mu);
   if (dev < 64 && (done[dev] & bit)) return LSB_OK;
   LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue, ar),
@@ -726,11 +761,16 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   LSB_REQUIRE(K + K2 < (int64_t(1) << 31), "gemm: dimension too large");
   LSB_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 2),
               "gemm: x and w must be 16-byte aligned");
-  LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue <= LSB_EPI_SWIGLU, "gemm: bad epilogue");
-  LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_SWIGLU || bias,
+  LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue <= kEpiArgmax, "gemm: bad epilogue");
+  LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_SWIGLU || epilogue == kEpiArgmax ||
+                  bias,
               "gemm: bias required");
-  const int64_t out_cols = epilogue == LSB_EPI_SWIGLU ? N / 2 : N;
+  // the argmax epilogue writes one (value, index) pair per row and 128-column tile
+  const int64_t out_cols = epilogue == LSB_EPI_SWIGLU ? N / 2
+                           : epilogue == kEpiArgmax  ? (N + kBM - 1) / kBM
+                                                     : N;
   LSB_REQUIRE(ldy >= out_cols, "gemm: ldy too small");
+  LSB_REQUIRE(epilogue != kEpiArgmax || aligned(y, 8), "gemm: argmax pairs must be 8-byte aligned");
   if (M <= 0) return LSB_OK;
   // The all-reduce variant waits on the same CTA of every rank: its whole grid must be
   // resident at once, so it keeps one CTA per SM and at most one wave.
@@ -810,6 +850,65 @@ extern "C" int lsb_gemm_concat(void* y, int64_t ldy, const void* x1, int64_t ldx
                                int32_t epilogue, void* stream) {
   const Segment2 seg{x2, ldx2, K2};
   return gemm_impl(y, ldy, x1, ldx1, w, ldw, bias, M, N, K1, epilogue, nullptr, stream, &seg);
+}
+
+extern "C" int64_t lsb_gemm_argmax_tiles(int64_t N) {
+  const int64_t tiles = (N + kBM - 1) / kBM;
+  return tiles + (tiles & 1);  // even: a row of pairs is a multiple of 16 bytes
+}
+
+extern "C" int lsb_gemm_argmax(void* pairs, int64_t ld_pairs, const void* x, int64_t ldx,
+                               const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                               void* stream) {
+  return gemm_impl(pairs, ld_pairs, x, ldx, w, ldw, nullptr, M, N, K, kEpiArgmax, nullptr,
+                   stream);
+}
+
+namespace lsb {
+namespace {
+
+// One warp per row: the best of every shard's tile pairs; the global index of a shard's
+// entry is shard * shard_cols + its index, ties go to the smaller global index.
+__global__ void argmax_pairs_kernel(int32_t* __restrict__ out, const ArgmaxPair* __restrict__ pairs,
+                                    int shards, int rows, int tiles, int64_t ld,
+                                    int64_t shard_cols) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float best = -INFINITY;
+  int64_t best_i = INT64_MAX;
+  for (int j = lane; j < shards * tiles; j += 32) {
+    const int sh = j / tiles, tt = j - sh * tiles;
+    const ArgmaxPair pr = pairs[(static_cast<int64_t>(sh) * rows + row) * ld + tt];
+    const int64_t g = static_cast<int64_t>(sh) * shard_cols + pr.index;
+    if (pr.value > best || (pr.value == best && g < best_i)) { best = pr.value; best_i = g; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (ob > best || (ob == best && oi < best_i)) { best = ob; best_i = oi; }
+  }
+  if (lane == 0) out[row] = best_i == INT64_MAX ? 0 : static_cast<int32_t>(best_i);
+}
+
+}  // namespace
+}  // namespace lsb
+
+extern "C" int lsb_argmax_pairs(int32_t* out, const void* pairs, int64_t shards, int64_t rows,
+                                int64_t tiles, int64_t ld_pairs, int64_t shard_cols,
+                                void* stream) {
+  LSB_REQUIRE(out && pairs && shards > 0 && tiles > 0 && ld_pairs >= tiles && shard_cols > 0,
+              "argmax_pairs: bad arguments");
+  LSB_REQUIRE(shards * tiles < (int64_t(1) << 31) && rows < (int64_t(1) << 31),
+              "argmax_pairs: too many pairs");
+  if (rows <= 0) return LSB_OK;
+  const int per_block = 8;
+  argmax_pairs_kernel<<<static_cast<unsigned>((rows + per_block - 1) / per_block), 32 * per_block,
+                        0, as_stream(stream)>>>(out, static_cast<const ArgmaxPair*>(pairs),
+                                                static_cast<int>(shards), static_cast<int>(rows),
+                                                static_cast<int>(tiles), ld_pairs, shard_cols);
+  return check_launch("lsb_argmax_pairs");
 }
 
 extern "C" int lsb_gemm_allreduce(lsb_comm* comm, void* y, int64_t ldy, const void* x,

@@ -250,6 +250,7 @@ class LoopedDecoder:
                                           self.device)
         self.scale = cfg.head_dim ** -0.5
         self.core_names = [f"model.layers.{i}" for i in range(cfg.num_core_layers)]
+        self._pairs: dict[int, torch.Tensor] = {}  # greedy-sampling pairs per row count
 
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """LinearOProj / LinearRowParallel (layers/linear.py:103-107, 124-128): the local
@@ -470,14 +471,22 @@ class LoopedDecoder:
 
     def greedy(self, hidden: torch.Tensor, batch: DeviceBatch | None,
                out: torch.Tensor | None = None) -> torch.Tensor:
-        """LM head + greedy sampling (sample.py:108-112) into int32 ``out``: with shards,
-        the local logits are all-gathered over NVLink and reduced by one sharded argmax."""
-        logits = ops.gemm(self._lm_rows(hidden, batch), self.lm_head_w)
-        if self.world == 1:
-            return ops.argmax(logits, out=out)
-        g = self.comm.all_gather(logits)
-        return ops.argmax_sharded(g, self.world, logits.shape[0], self.vocab_local,
-                                  self.cfg.vocab, out=out)
+        """LM head + greedy sampling (embedding.py:89-111, sample.py:108-112) into int32
+        ``out``, fused: the LM-head GEMM's epilogue keeps only the best logit of every
+        128-entry vocabulary tile per row, so the logits are never written; with shards,
+        only those (value, index) pairs are all-gathered over NVLink, then one reduction
+        picks each row's token (first index on ties, as torch.argmax)."""
+        rows = self._lm_rows(hidden, batch)
+        m = rows.shape[0]
+        pairs = self._pairs.get(m)
+        if pairs is None:  # kept per row count: graph replays reuse the same buffer
+            pairs = ops.argmax_pairs_buffer(m, self.vocab_local, rows.device)
+            self._pairs[m] = pairs
+        ops.gemm_argmax(rows, self.lm_head_w, pairs, n_valid=self.vocab_len)
+        tiles = -(-self.vocab_len // 128)
+        if self.world > 1:
+            pairs = self.comm.all_gather(pairs)
+        return ops.argmax_pairs(pairs, self.world, m, tiles, self.vocab_local, out=out)
 
     def forward(self, batch: DeviceBatch, kv) -> torch.Tensor:
         """Full-depth pass (base.py:148-164)."""

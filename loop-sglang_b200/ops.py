@@ -29,7 +29,8 @@ __all__ = [
     "rmsnorm", "fused_add_rmsnorm", "sandwich_norm", "rope_store_kv", "rope_only", "store_kv",
     "paged_attention",
     "gemm", "gemm_concat", "linear", "swiglu_interleave", "ouro_step_exit", "huginn_step_exit", "embedding",
-    "gather_rows", "argmax", "argmax_sharded", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
+    "gather_rows", "argmax", "argmax_sharded", "gemm_argmax", "argmax_pairs",
+    "argmax_pairs_buffer", "silu_and_mul", "last_exited_resolve", "last_exited_reserve",
     "last_exited_release", "cdb_route", "cdb_admit", "device_error_word", "Workspace", "prepare_batch_inputs",
     "set_metadata",
     "LSB_EPI_NONE", "LSB_EPI_BIAS", "LSB_EPI_BIAS_AFTER_ROUND", "LSB_EPI_SWIGLU",
@@ -313,6 +314,43 @@ def gather_rows(src: torch.Tensor, index: torch.Tensor,
     out = torch.empty(index.numel(), src.shape[1], dtype=src.dtype, device=src.device) if out is None else out
     call("lsb_gather_rows", out.data_ptr(), src.data_ptr(), index.data_ptr(), index.numel(),
          src.shape[1], _stream())
+    return out
+
+
+def argmax_pairs_buffer(rows: int, n: int, device, shards: int = 1) -> torch.Tensor:
+    """A [shards * rows, tiles, 2] fp32 buffer of (value, index) pairs for ``gemm_argmax``
+    over ``n`` vocabulary entries, every value -inf (tiles never scored keep it)."""
+    tiles = int(lib().lsb_gemm_argmax_tiles(n))
+    return torch.full((shards * rows, tiles, 2), float("-inf"), dtype=torch.float32,
+                      device=device)
+
+
+def gemm_argmax(x: torch.Tensor, w: torch.Tensor, pairs: torch.Tensor,
+                n_valid: int | None = None) -> torch.Tensor:
+    """The LM-head GEMM with greedy sampling in its epilogue: per row and 128-entry
+    vocabulary tile, the largest bf16-rounded logit and its index (first on ties) into
+    ``pairs`` (``argmax_pairs_buffer``); the logits are not written. ``n_valid`` scores
+    only the first rows of ``w`` (a tensor-parallel rank's padded vocabulary range)."""
+    _need(x, BF16, "x", contiguous=False)
+    _need(w, BF16, "w", contiguous=False)
+    _need(pairs, torch.float32, "pairs")
+    m, k = x.shape
+    n = w.shape[0] if n_valid is None else n_valid
+    if w.shape[1] != k or pairs.shape[0] < m or pairs.dim() != 3 or pairs.shape[2] != 2:
+        raise ValueError("gemm_argmax: bad shapes")
+    call("lsb_gemm_argmax", pairs.data_ptr(), pairs.shape[1], x.data_ptr(),
+         _row_stride(x, "x"), w.data_ptr(), _row_stride(w, "w"), m, n, k, _stream())
+    return pairs
+
+
+def argmax_pairs(pairs: torch.Tensor, shards: int, rows: int, tiles: int, shard_cols: int,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy tokens from ``gemm_argmax`` pairs of ``shards`` vocabulary ranges of
+    ``shard_cols`` entries each, stored shard-major [shards * rows, ld, 2]."""
+    _need(pairs, torch.float32, "pairs")
+    out = torch.empty(rows, dtype=torch.int32, device=pairs.device) if out is None else out
+    call("lsb_argmax_pairs", out.data_ptr(), pairs.data_ptr(), shards, rows, tiles,
+         pairs.shape[1], shard_cols, _stream())
     return out
 
 

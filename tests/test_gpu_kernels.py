@@ -314,6 +314,43 @@ def test_gemm_concat_matches_linear_of_cat(m: int, n: int, k1: int, k2: int) -> 
     no_device_errors()
 
 
+@pytest.mark.parametrize("m", [3, 143, 263])
+def test_gemm_argmax_equals_argmax_of_logits(m: int) -> None:
+    """The LM head with greedy sampling in its epilogue picks exactly torch.argmax of the
+    bf16 logits the plain GEMM writes, ties included (duplicate vocabulary rows within a
+    tile and across tiles: the first index wins), with and without a vocabulary split."""
+    g = gen(m)
+    n, k = 4096 + 96, 512  # a partial last tile
+    x = bf(torch.randn(m, k, generator=g))
+    w = bf(torch.randn(n, k, generator=g) * 0.05)
+    w[700] = w[3000] = w[4100] = w[200]  # the same logit at four indices, three tiles
+    x[0] = bf(w[200].float() * 40)       # row 0 prefers them: its argmax is a tie -> 200
+    w[130] = w[131]                      # a tie inside one tile
+    x[1] = bf(w[131].float() * 40)
+    xd, wd = x.to(DEV), w.to(DEV)
+    logits = ops.gemm(xd, wd)
+    want = torch.argmax(logits.float(), dim=-1).to(torch.int32).cpu()
+    assert int(want[0]) in (200, 700, 3000, 4100) and int(want[1]) in (130, 131)
+    pairs = ops.argmax_pairs_buffer(m, n, DEV)
+    ops.gemm_argmax(xd, wd, pairs)
+    got = ops.argmax_pairs(pairs, 1, m, -(-n // 128), n)
+    assert torch.equal(got.cpu(), want)
+    # two vocabulary shards of 2176 rows (the second padded with zero rows past n_valid),
+    # stored shard-major as the all-gather leaves them
+    half = 2176
+    w2 = torch.zeros(2 * half, k, dtype=torch.bfloat16)
+    w2[:n] = w
+    shards = []
+    for s in range(2):
+        valid = min(half, n - s * half)
+        p = ops.argmax_pairs_buffer(m, half, DEV)
+        ops.gemm_argmax(xd, w2[s * half:(s + 1) * half].contiguous().to(DEV), p, n_valid=valid)
+        shards.append(p)
+    got2 = ops.argmax_pairs(torch.cat(shards), 2, m, -(-half // 128), half)
+    assert torch.equal(got2.cpu(), want)
+    no_device_errors()
+
+
 def test_gemm_rejects_bad_shapes() -> None:
     x = torch.zeros(4, 100, dtype=torch.bfloat16, device=DEV)  # row stride 200 B: not TMA-able
     w = torch.zeros(128, 100, dtype=torch.bfloat16, device=DEV)

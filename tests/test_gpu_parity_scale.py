@@ -220,7 +220,9 @@ def test_ouro14b_cdb_engine_matches_oracle(fullsize) -> None:
 # Huginn at full width (configs[4]: hidden 5280, 55 heads x 96, SwiGLU 17920, RoPE 5e4,
 # embedding scale sqrt(5280), q/k/v bias) with one prelude, one core and one coda layer,
 # two recurrences and a reduced vocabulary: every kernel at the shapes configs[4] runs,
-# including the adapter's two-segment GEMM.
+# including the adapter's two-segment GEMM. At this width bf16 arithmetic alone moves the
+# logits by about 6% (the bf16 oracle against the same computation in fp32), so the CUDA
+# path is held to the same floor-relative bounds as the full-size Ouro cases.
 HUGINN_WIDE = LoopedConfig(arch="huginn", hidden=5280, heads=55, kv_heads=55, head_dim=96,
                            intermediate=17920, vocab=8192, num_prelude_layers=1,
                            num_core_layers=1, num_coda_layers=1, loop_steps=2,
@@ -235,9 +237,10 @@ def test_huginn_full_width_layers_match_oracle() -> None:
     cfg, page, prompts, steps = HUGINN_WIDE, 16, [24, 40], 2
     w32 = make_weights(cfg, 9, dtype=torch.float32)
     model = gpu_model(cfg, w32, "shared")
-    oracle = LoopedModel(cfg, with_fp32_matrices({k: v.to(torch.bfloat16) for k, v in w32.items()}),
-                         "shared")
-    del w32
+    wb = {k: v.to(torch.bfloat16) for k, v in w32.items()}
+    oracle = LoopedModel(cfg, with_fp32_matrices(wb), "shared")
+    exact = LoopedModel(cfg, {k: v.float() for k, v in wb.items()}, "shared")
+    del w32, wb
     b = len(prompts)
     pages_per = (max(prompts) + steps + page) // page
     table = (1 + torch.arange(b).view(-1, 1) * pages_per + torch.arange(pages_per)).to(torch.int32)
@@ -245,6 +248,8 @@ def test_huginn_full_width_layers_match_oracle() -> None:
     kv = model.make_kv_cache(num_pages, page)
     pool = PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads, cfg.head_dim,
                        torch.bfloat16)
+    pool32 = PagedKVPool(oracle.num_kv_layers, num_pages, page, cfg.kv_heads, cfg.head_dim,
+                         torch.float32)
     g = torch.Generator().manual_seed(4)
     ids = torch.cat([torch.randint(0, cfg.vocab, (n,), generator=g) for n in prompts]).to(torch.int32)
     lens = torch.tensor(prompts, dtype=torch.int32)
@@ -264,8 +269,13 @@ def test_huginn_full_width_layers_match_oracle() -> None:
                          cu.cuda(), step < 0, max_seqlen=pages_per * page)
         got = model.forward(db, kv).float().cpu()
         ref = oracle.forward(ob, pool).float()
-        err = rel_err(got, ref)
-        assert err < REL, f"Huginn full width, step {step}: logits rel err {err:.4f}"
+        ref32 = exact.forward(ob, pool32).float()
+        floor = rel_err(ref, ref32)
+        err, err32 = rel_err(got, ref), rel_err(got, ref32)
+        msg = (f"Huginn full width, step {step}: logits rel err vs bf16 oracle {err:.4f}, vs "
+               f"fp32 {err32:.4f}, bf16 oracle vs fp32 {floor:.4f}")
+        print(msg)
+        assert err32 <= max(REL, 1.5 * floor) and err <= max(REL, 2.0 * floor), msg
         for v in verdict_full(got, ref):
             counts[v] += 1
         ids = ref.argmax(-1).to(torch.int32)
