@@ -171,6 +171,13 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
              const void* bias, int64_t M, int64_t N, int64_t K, int32_t epilogue,
              void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Tile plan used by later lsb_gemm* calls of this process, for benchmarks and
+ * tuning: 0 automatic (the default), 1 one wide tile of all tokens for
+ * 257..384 tokens (two MMAs of up to 192 tokens per K step, one CTA per SM),
+ * 2 tiles of at most 96 tokens for 257..512 tokens, 3 one CTA per SM for
+ * every tile size. No counterpart in the reference (its cuBLAS heuristics). */
+int lsb_gemm_force_plan(int32_t mode);
+
 /* y[M, N] = [x1 | x2] . w^T (+ bias) with w [N, K1 + K2]: the product over the
  * concatenation of two activation tensors along K without materialising it (the
  * K loop reads x1 and w's first K1 columns, then x2 and the last K2). Replaces

@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -63,7 +64,10 @@ struct GemmParams {
   // K blocks taken from the first (tmap_w, tmap_x) pair; the rest come from the second
   // pair (a product over the concatenation [x | x2] of two activation tensors along K)
   int kb1;
-  int bn, stages, splits, epilogue;
+  // tokens per tile; a tile wider than one MMA's N (256) is issued as `halves` MMAs of
+  // bh = bn / halves tokens each, into adjacent TMEM columns, its activation tile
+  // loaded as that many TMA boxes
+  int bn, bh, halves, stages, splits, epilogue;
   uint32_t idesc;
   int* error_flag;
   CommDev comm;  // row-parallel all-reduce (AR variants only)
@@ -246,8 +250,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         else tma_load_2d(dst, &tmap_w2, bar, (kb - p.kb1) * kBK, n0);
       };
       auto load_x = [&](uint8_t* dst, uint64_t* bar, int kb) {
-        if (kb < p.kb1) tma_load_2d(dst, &tmap_x, bar, kb * kBK, m0);
-        else tma_load_2d(dst, &tmap_x2, bar, (kb - p.kb1) * kBK, m0);
+        for (int h = 0; h < p.halves; ++h) {
+          uint8_t* d = dst + h * p.bh * kBK * 2;
+          if (kb < p.kb1) tma_load_2d(d, &tmap_x, bar, kb * kBK, m0 + h * p.bh);
+          else tma_load_2d(d, &tmap_x2, bar, (kb - p.kb1) * kBK, m0 + h * p.bh);
+        }
       };
       for (int i = 0; i < pre; ++i) {
         mbar_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
@@ -279,12 +286,17 @@ __global__ void __launch_bounds__(kThreads, 2)
         asm volatile("tcgen05.fence::after_thread_sync;");
         const uint8_t* a_tile = smem + s * stage_bytes;
         const uint64_t adesc = smem_desc(a_tile);
-        const uint64_t bdesc = smem_desc(a_tile + kABytes);
+        for (int h = 0; h < p.halves; ++h) {
+          // half h: tokens h*bh .. h*bh+bh-1 (rows of the B tile, 128 bytes each; bh is a
+          // multiple of 16, so the half starts on a 1024-byte swizzle atom) into TMEM
+          // columns h*bh ..
+          const uint64_t bdesc = smem_desc(a_tile + kABytes + h * p.bh * kBK * 2);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          // advance 16 bf16 = 32 bytes along K inside the swizzle atom
-          umma_f16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, p.idesc,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // advance 16 bf16 = 32 bytes along K inside the swizzle atom
+            umma_f16(tmem_base + static_cast<uint32_t>(h * p.bh), adesc + 2 * kk, bdesc + 2 * kk,
+                     p.idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -526,9 +538,12 @@ int make_tmap(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_
 }
 
 struct Plan {
-  int bn, stages, splits, tiles_n, tiles_m;
+  int bn, halves, stages, splits, tiles_n, tiles_m;
   size_t smem;
 };
+
+// Plan selection for benchmarks and tuning (lsb_gemm_force_plan): 0 automatic.
+std::atomic<int> g_force_plan{0};
 
 int num_sms() {
   static int sms = 0;
@@ -645,8 +660,48 @@ size_t smem_for(int stages, int stage_bytes) {
 // ingest of weight and activation tiles, not the pipeline depth, then limits the
 // main loop. A split is only used when all clusters of the grid run at once; a
 // cluster left for a second wave would double the kernel's time.
-Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
+// Plans lsb_gemm_force_plan can select (automatic otherwise).
+constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3;
+// Token counts a single wide tile (two MMA halves) covers: its fp32 tile, bn x 128 x 4
+// bytes, must fit in the drained stage buffers of one CTA's shared memory.
+constexpr int kWideMax = 384;
+
+// One tile column of all M tokens (256 < M <= 384): the weights are streamed once and the
+// activations read once per 128-row weight tile, with one CTA per SM (its accumulator
+// takes all 512 TMEM columns) and the K loop split over clusters to fill the SMs.
+Plan wide_plan(int64_t M, int64_t N, int64_t K) {
   Plan pl;
+  pl.bn = static_cast<int>((M + 31) / 32 * 32);
+  pl.halves = 2;
+  const int stage_bytes = kABytes + pl.bn * kBK * 2;
+  const int min_stages = (pl.bn * kBM * 4 + stage_bytes - 1) / stage_bytes;
+  int stages = (220 * 1024) / stage_bytes;
+  if (stages > kMaxStages) stages = kMaxStages;
+  if (stages < min_stages) stages = min_stages;
+  pl.stages = stages;
+  pl.smem = smem_for(stages, stage_bytes);
+  pl.tiles_n = static_cast<int>((N + kBM - 1) / kBM);
+  pl.tiles_m = 1;
+  const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
+  const int sms = num_sms();
+  int limit = sms / pl.tiles_n;
+  if (limit > kMaxSplits) limit = kMaxSplits;
+  if (limit > kblocks) limit = kblocks;
+  pl.splits = 1;
+  for (int sp = limit; sp >= 2; --sp)
+    if (pl.tiles_n <= max_active_clusters(sp, pl.smem)) {
+      pl.splits = sp;
+      break;
+    }
+  return pl;
+}
+
+Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
+  const int force = g_force_plan.load(std::memory_order_relaxed);
+  if (M > 256 && M <= kWideMax && !single_wave && (force == kPlanAuto || force == kPlanWide))
+    return wide_plan(M, N, K);
+  Plan pl;
+  pl.halves = 1;
   // tokens per tile: up to 256 tokens one tile; for decode batches of 257-512 tokens,
   // balanced tiles of at most 96 (263 -> 3 x 96, 512 -> 6 x 96): past one tile every weight
   // tile is read again per token tile anyway (from L2), and narrow tiles let two or three
@@ -685,7 +740,8 @@ Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   pl.smem = smem_a;
 
   const size_t smem_b = smem_for(3, stage_bytes);
-  if (!single_wave && 2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
+  if (!single_wave && force != kPlanOnePerSm &&
+      2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
     const int split_b = tiles < 2 * sms ? best_split(2 * sms / tiles, smem_b) : 1;
     if (static_cast<int64_t>(tiles) * split_b > sms) {
       pl.stages = 3;
@@ -717,6 +773,12 @@ extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
   out[2] = pl.splits;
   out[3] = pl.stages;
   out[4] = static_cast<int32_t>(pl.smem);
+  return LSB_OK;
+}
+
+extern "C" int lsb_gemm_force_plan(int32_t mode) {
+  LSB_REQUIRE(mode >= kPlanAuto && mode <= kPlanOnePerSm, "gemm_force_plan: mode %d", mode);
+  g_force_plan.store(mode, std::memory_order_relaxed);
   return LSB_OK;
 }
 
@@ -778,11 +840,12 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   const int64_t kb2 = (K2 + kBK - 1) / kBK;
   Plan pl = plan_for(M, N, (kb1 + kb2) * kBK, comm != nullptr);
   CUtensorMap tw, tx, tw2, tx2;
+  const int bh = pl.bn / pl.halves;  // activation rows per TMA box and per MMA
   if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
-  if (int rc = make_tmap(&tx, x, M, K, ldx, pl.bn)) return rc;
+  if (int rc = make_tmap(&tx, x, M, K, ldx, bh)) return rc;
   if (seg2) {  // each segment's last K block is zero-filled past its own width
     if (int rc = make_tmap(&tw2, static_cast<const bf16*>(w) + K, N, K2, ldw, kBM)) return rc;
-    if (int rc = make_tmap(&tx2, seg2->x2, M, K2, seg2->ldx2, pl.bn)) return rc;
+    if (int rc = make_tmap(&tx2, seg2->x2, M, K2, seg2->ldx2, bh)) return rc;
   } else {
     tw2 = tw;
     tx2 = tx;
@@ -796,10 +859,12 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   p.K = static_cast<int>((kb1 + kb2) * kBK);  // sets the K-block count of the whole loop
   p.kb1 = static_cast<int>(kb1);
   p.bn = pl.bn;
+  p.bh = bh;
+  p.halves = pl.halves;
   p.stages = pl.stages;
   p.splits = pl.splits;
   p.epilogue = epilogue;
-  p.idesc = make_idesc(pl.bn);
+  p.idesc = make_idesc(bh);
   p.error_flag = lsb_device_error_flag();
   const bool ar = comm != nullptr;
   if (ar) {

@@ -312,6 +312,9 @@ def main(argv=None) -> None:
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
     gm.add_argument("--cublas", action="store_true",
                     help="also time torch.matmul (cuBLAS) on the same shapes and weights")
+    gm.add_argument("--plan", type=int, default=0, choices=[0, 1, 2, 3],
+                    help="tile plan: 0 automatic, 1 one wide tile (257-384 tokens), 2 tiles "
+                         "of <= 96 tokens, 3 one CTA per SM")
     ga = sub.add_parser("gemm_ar")
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
@@ -360,8 +363,12 @@ def main(argv=None) -> None:
     if args.kernel == "attention":
         print(json.dumps(bench_attention(args, ops)), flush=True)
     else:
+        ops.check(ops.lib().lsb_gemm_force_plan(args.plan), "gemm_force_plan")
         for name in args.shape:
-            print(json.dumps(bench_gemm(args, ops, name)), flush=True)
+            line = bench_gemm(args, ops, name)
+            line["plan"] = args.plan
+            line["tile_plan"] = ops.gemm_plan(args.tokens, *tp_shape(name, args.tp)[:2])
+            print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

@@ -17,6 +17,7 @@ from oracle import ops as O
 
 load_package()
 from loop_sglang_b200 import ops  # noqa: E402
+from loop_sglang_b200._lib import check  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
@@ -272,6 +273,34 @@ def test_gemm(m: int, n: int, k: int) -> None:
     for _ in range(2):
         got = ops.gemm(x.to(DEV), w.to(DEV))
         close(got, ref)
+    no_device_errors()
+
+
+@pytest.mark.parametrize("plan", [1, 2, 3])
+@pytest.mark.parametrize("m,n,k,epi", [
+    (263, 6144, 2048, "none"), (300, 2048, 5632, "none"), (384, 1024, 2048, "swiglu"),
+    (289, 640, 352, "bias"), (143, 2048, 2048, "none")])
+def test_gemm_every_plan(plan: int, m: int, n: int, k: int, epi: str) -> None:
+    """Each tile plan (one wide tile with two MMA halves, 96-token tiles, one CTA per SM)
+    gives the oracle's product, fused epilogues included."""
+    g = gen(m + n + k + plan)
+    x = bf(torch.randn(m, k, generator=g))
+    w = bf(torch.randn(n, k, generator=g) * 0.05)
+    b = bf(torch.randn(n, generator=g))
+    check(ops.lib().lsb_gemm_force_plan(plan), "force_plan")
+    try:
+        for _ in range(2):
+            if epi == "swiglu":
+                got = ops.gemm(x.to(DEV), ops.swiglu_interleave(w.to(DEV)),
+                               epilogue=ops.LSB_EPI_SWIGLU)
+                close(got, O.silu_and_mul(O.linear(x, w)))
+            elif epi == "bias":
+                close(ops.gemm(x.to(DEV), w.to(DEV), b.to(DEV), ops.LSB_EPI_BIAS),
+                      O.linear(x, w, b))
+            else:
+                close(ops.gemm(x.to(DEV), w.to(DEV)), O.linear(x, w))
+    finally:
+        check(ops.lib().lsb_gemm_force_plan(0), "force_plan")
     no_device_errors()
 
 

@@ -51,15 +51,16 @@ def rel_err(got: torch.Tensor, ref: torch.Tensor) -> float:
     return float((got.float() - ref).abs().max() / ref.abs().max().clamp_min(1e-6))
 
 
-def verdict_full(got: torch.Tensor, ref: torch.Tensor) -> list[str]:
-    """Per row: 'agree', 'near_tie' or 'mismatch' of the greedy token against full logits."""
+def verdict_full(got: torch.Tensor, ref: torch.Tensor, tol: float = REL) -> list[str]:
+    """Per row: 'agree', 'near_tie' (the reference's logit of the CUDA path's token within
+    ``tol`` x max |logit| of its maximum) or 'mismatch' of the greedy token."""
     g, r = got.float().argmax(-1), ref.float().argmax(-1)
     scale = ref.float().abs().max(-1).values
     out = []
     for i in range(got.shape[0]):
         if int(g[i]) == int(r[i]):
             out.append("agree")
-        elif ref[i, g[i]] >= ref[i, r[i]] - REL * scale[i]:
+        elif ref[i, g[i]] >= ref[i, r[i]] - tol * scale[i]:
             out.append("near_tie")
         else:
             out.append("mismatch")
@@ -276,7 +277,9 @@ def test_huginn_full_width_layers_match_oracle() -> None:
                f"fp32 {err32:.4f}, bf16 oracle vs fp32 {floor:.4f}")
         print(msg)
         assert err32 <= max(REL, 1.5 * floor) and err <= max(REL, 2.0 * floor), msg
-        for v in verdict_full(got, ref):
+        # a token is decided only where its margin exceeds what bf16 arithmetic itself
+        # moves the logits here (the floor)
+        for v in verdict_full(got, ref, tol=max(REL, floor)):
             counts[v] += 1
         ids = ref.argmax(-1).to(torch.int32)
     print(f"Huginn full width: {counts}")
