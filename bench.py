@@ -393,6 +393,37 @@ def cpu_decode_sample(steps: int, batch: int, threads: int, model_cfg: dict | No
             "p50_step_s": statistics.median(times)}
 
 
+def cpu_prefill_sample(tokens: int, threads: int) -> dict:
+    """The oracle on a bounded prefill sample: one prompt of ``tokens`` random ids at full
+    depth (Ouro-1.4B, depth-indexed KV in 16-token pages)."""
+    from oracle import model as om
+
+    torch.set_num_threads(threads)
+    cfg = om.LoopedConfig(**OURO_14B)
+    t0 = time.perf_counter()
+    mdl = om.LoopedModel(cfg, om.with_fp32_matrices(om.make_weights(cfg, seed=SEED)),
+                         "depth_indexed")
+    pages = (tokens + PAGE - 1) // PAGE
+    pool = om.PagedKVPool(mdl.num_kv_layers, pages + 1, PAGE, cfg.kv_heads, cfg.head_dim,
+                          torch.bfloat16)
+    table = torch.arange(1, pages + 1, dtype=torch.int32).view(1, -1)
+    pos = torch.arange(tokens, dtype=torch.int32)
+    loc = (table[0, (pos // PAGE).long()] * PAGE + pos % PAGE).to(torch.int32)
+    ids = torch.randint(0, cfg.vocab, (tokens,), generator=torch.Generator().manual_seed(2),
+                        dtype=torch.int32)
+    b = om.Batch(ids, pos, loc, table, torch.tensor([tokens], dtype=torch.int32),
+                 torch.tensor([0, tokens], dtype=torch.int32), True)
+    setup = time.perf_counter() - t0
+    t = time.perf_counter()
+    mdl.forward(b, pool)
+    total = time.perf_counter() - t
+    return {"value": tokens / total, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"one {tokens}-token prompt prefilled at full depth through the CPU "
+                       f"oracle in torch bf16/fp32, {threads} threads; setup {setup:.0f}s "
+                       "untimed"),
+            "p50_step_s": total}
+
+
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -407,6 +438,9 @@ def run_reference(args) -> None:
         base = cpu_decode_sample(min(steps, 2), 1, threads, OURO_26B,
                                  np.array([RADIX_PREFIX + RADIX_SUFFIX + RADIX_MID]), "Ouro-2.6B")
         metric, workload = RADIX_METRIC, RADIX_WORKLOAD
+    elif args.workload == "prefill":
+        base = cpu_prefill_sample(512, threads)
+        metric, workload = PREFILL_METRIC, PREFILL_WORKLOAD
     elif args.workload == "huginn":
         rng = np.random.default_rng(SEED)
         ctx = rng.integers(HUGINN_PROMPT_RANGE[0], HUGINN_PROMPT_RANGE[1] + 1, 8) + HUGINN_MID
@@ -1025,6 +1059,174 @@ def run_b200_cdb(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+# ------------------------------------------------------------------ prefill --
+# Prefill of configs[1]'s requests (Ouro-1.4B, depth-indexed KV in 16-token pages, prompts
+# U[512, 2048]): a step is one full-depth forward of PREFILL_REQS whole prompts in one
+# batch (4 loop steps x 24 layers, LM head on each request's last token). Tensor-bound:
+# the roofline is the GEMMs' bf16 FLOP rate.
+PREFILL_REQS = 8  # ~10k tokens: the attention kernel's per-(row, head group) split counters
+PREFILL_METRIC = "prefill tok/s, Ouro-1.4B full depth (configs[1] prompts), TP over the job's GPUs"
+PREFILL_WORKLOAD = ("configs[1] prompts: Ouro-1.4B random-init bf16, 8 requests with prompt "
+                    "U[512,2048] prefilled together at full depth (4 loop steps x 24 layers), "
+                    "depth-indexed KV in 16-token pages")
+
+
+def run_b200_prefill(args) -> None:
+    from __graft_entry__ import load_package
+
+    load_package()
+    from loop_sglang_b200 import ops
+    from loop_sglang_b200.comm import B200Communicator
+    from loop_sglang_b200.model import DeviceBatch, LoopedConfig, LoopedDecoder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = LoopedConfig(**OURO_14B)
+    prompts = request_lengths()[: args.batch or PREFILL_REQS]
+    n_tok = int(prompts.sum())
+    comm = None
+    if world > 1:
+        comm = B200Communicator(rank, world, n_tok * cfg.hidden)
+    weights = gpu_weights(cfg, dev, SEED)
+    model = LoopedDecoder(cfg, weights, "depth_indexed", dev, comm=comm)
+    del weights
+    torch.cuda.empty_cache()
+    b = prompts.size
+    pages_per = (prompts + PAGE - 1) // PAGE
+    num_pages = int(pages_per.sum()) + 1
+    kv = model.make_kv_cache(num_pages, PAGE)
+    table = torch.zeros(b, int(pages_per.max()), dtype=torch.int32)
+    off = 1
+    for r, n in enumerate(pages_per):
+        table[r, :n] = torch.arange(off, off + n, dtype=torch.int32)
+        off += int(n)
+    pos = torch.cat([torch.arange(n, dtype=torch.int32) for n in prompts])
+    rows = torch.cat([torch.full((int(n),), r) for r, n in enumerate(prompts)])
+    loc = (table[rows, (pos // PAGE).long()] * PAGE + pos % PAGE).to(torch.int32)
+    cu = torch.zeros(b + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.as_tensor(prompts, dtype=torch.int32), 0)
+    ids = torch.randint(0, cfg.vocab, (n_tok,), generator=torch.Generator().manual_seed(SEED),
+                        dtype=torch.int32)
+    batch = DeviceBatch(ids.to(dev), pos.to(dev), loc.to(dev), table.to(dev),
+                        torch.as_tensor(prompts, dtype=torch.int32).to(dev), cu.to(dev), True,
+                        max_seqlen=int(table.shape[1]) * PAGE)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    from loop_sglang_b200 import _lib
+
+    with torch.cuda.stream(s):
+        before = _lib.launch_count()
+        for _ in range(args.warmup):
+            model.forward(batch, kv)
+        launches = (_lib.launch_count() - before) // max(1, args.warmup)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(dev) as clocks, torch.cuda.stream(s):
+        ev[0].record(s)
+        for k in range(args.steps):
+            model.forward(batch, kv)
+            ev[k + 1].record(s)
+        s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    total_ms = ev[0].elapsed_time(ev[-1])
+    clk = clocks.summary()
+    # e2e: host ids in, the last tokens' greedy ids out, every step
+    host_ids = ids.pin_memory()
+    host_out = torch.zeros(b, dtype=torch.int32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(args.steps):
+            batch.input_ids.copy_(host_ids, non_blocking=True)
+            toks = model.greedy(model.forward_coda(_full_depth(model, batch, kv), batch, kv), batch)
+            host_out.copy_(toks, non_blocking=True)
+            s.synchronize()
+        e1.record(s)
+        s.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    # the dominant kernel: the gate_up GEMM (+ SwiGLU) of one layer at this token count
+    x = torch.randn(n_tok, cfg.hidden, device=dev).to(torch.bfloat16)
+    lw = model.layers["model.layers.0"]
+    out = torch.empty(n_tok, lw.gate_up.shape[0] // 2, dtype=torch.bfloat16, device=dev)
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            ops.gemm(x, lw.gate_up, epilogue=ops.LSB_EPI_SWIGLU, out=out)
+        g0.record(s)
+        for _ in range(10):
+            ops.gemm(x, lw.gate_up, epilogue=ops.LSB_EPI_SWIGLU, out=out)
+        g1.record(s)
+        s.synchronize()
+    gemm_s = g0.elapsed_time(g1) / 1000.0 / 10
+    t_max, e2e_max = total_ms, e2e_ms
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        t_max, e2e_max = float(t[0]), float(t[1])
+    pj = ROOT / "MEASURED_PEAKS.json"
+    peak_tf = float(json.loads(pj.read_text())["bf16_tflops_sustained"]) if pj.exists() else 1400.0
+    gemm_flops = 2.0 * n_tok * lw.gate_up.shape[0] * cfg.hidden
+    params = sum(t.numel() for lw2 in model.layers.values() for t in (lw2.qkv, lw2.o, lw2.gate_up,
+                                                                        lw2.down))
+    step_flops = 2.0 * n_tok * params * cfg.loop_steps * world  # whole model over the ranks
+    step_s = t_max / 1000.0 / args.steps
+    line = {
+        "metric": PREFILL_METRIC, "value": n_tok * args.steps / (t_max / 1000.0), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_max / args.steps, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded random-init weights and token ids",
+        "config": {"workload": PREFILL_WORKLOAD, "model": "Ouro-1.4B architecture (random init)",
+                   "global_batch": b, "prompt_tokens": n_tok, "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2 (~%d GB of activations and KV per step)"
+                         % (n_tok * 96 * 8192 // 10**9)},
+        "roofline": {"bound": "tensor", "achieved": round(gemm_flops / gemm_s / 1e12, 1),
+                     "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": round(gemm_flops / gemm_s / 1e12 / peak_tf, 4), "traffic": None,
+                     "kernel": f"gemm (gate_up + SwiGLU, {n_tok} tokens, timed alone)",
+                     "peak_kind": "measured (sustained)" if pj.exists() else "fallback",
+                     "step_frac": round(step_flops / step_s / 1e12 / peak_tf / world, 4)},
+        "e2e": {"value": n_tok * args.steps / (e2e_max / 1000.0), "unit": "tok/s",
+                "h2d_bytes_per_step": n_tok * 4, "d2h_bytes_per_step": b * 4},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk,
+    }
+    err = ops.device_error_word(reset=False)
+    if err:
+        line["device_error_word"] = err
+    line["ranks"] = rank_info(world, rank, local, dev)
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_prefill_sample(512, os.cpu_count() or 1)
+            line["cpu_baseline"].pop("p50_step_s", None)
+        except Exception as exc:  # reported, never silently dropped
+            line["cpu_baseline"] = {"value": None, "error": repr(exc)}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _full_depth(model, batch, kv):
+    h, inj = model.forward_prelude(batch, kv)
+    for step in range(model.cfg.loop_steps):
+        h = model.core_step(h, step, inj, batch, kv)
+    return h
+
+
 # ---------------------------------------------------------- Huginn replicas --
 # Huginn-0125 architecture (hidden 5280, 55 heads x 96, prelude 2 +
 # core 4 x 32 recurrences + coda 2, SwiGLU 17920, vocab 65536, RoPE 5e4), random-init bf16,
@@ -1239,13 +1441,15 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer e2e leg")
     ap.add_argument("--no-parity", action="store_true",
                     help="skip the parity stamp (greedy tokens vs the CPU oracle)")
-    ap.add_argument("--workload", choices=["cdb", "cb", "radix", "huginn"], default="cdb",
+    ap.add_argument("--workload", choices=["cdb", "cb", "radix", "huginn", "prefill"],
+                    default="cdb",
                     help="cdb: configs[2] (the metric's); cb: configs[1] full-depth CB; "
                          "radix: configs[3] (Ouro-2.6B, shared prefixes); huginn: configs[4] "
                          "(one Huginn replica per GPU)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"cdb": 120, "cb": 40, "radix": 20, "huginn": 25}[args.workload]
+        args.steps = {"cdb": 120, "cb": 40, "radix": 20, "huginn": 25,
+                      "prefill": 10}[args.workload]
     if args.steps < 1:
         ap.error("--steps must be >= 1")
     if args.warmup < 3:
@@ -1256,6 +1460,8 @@ def main() -> None:
         run_b200_cdb(args)
     elif args.workload == "huginn":
         run_b200_huginn(args)
+    elif args.workload == "prefill":
+        run_b200_prefill(args)
     else:
         run_b200(args)  # cb and radix
 

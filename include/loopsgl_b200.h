@@ -173,9 +173,10 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
 
 /* Tile plan used by later lsb_gemm* calls of this process, for benchmarks and
  * tuning: 0 automatic (the default), 1 one wide tile of all tokens for
- * 257..384 tokens (two MMAs of up to 192 tokens per K step, one CTA per SM),
- * 2 tiles of at most 96 tokens for 257..512 tokens, 3 one CTA per SM for
- * every tile size. No counterpart in the reference (its cuBLAS heuristics). */
+ * 257..384 tokens (two MMAs of up to 192 tokens per K step, one CTA per SM;
+ * never chosen automatically), 2 tiles of at most 96 tokens for 257..512
+ * tokens, 3 one CTA per SM for every tile size. No counterpart in the
+ * reference (its cuBLAS heuristics). */
 int lsb_gemm_force_plan(int32_t mode);
 
 /* y[M, N] = [x1 | x2] . w^T (+ bias) with w [N, K1 + K2]: the product over the

@@ -47,6 +47,10 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr int kSmemPerSm = 228 * 1024;
 
+// Tuning switches (lsb_gemm_force_plan mode bits 4..): K loop in order instead of
+// rotated per tile; L2 hints on the TMA loads; epilogue warps wait with back-off.
+constexpr int kFlagNoRotate = 1, kFlagCacheHints = 2, kFlagSleepWait = 4;
+
 // Internal epilogue of the LM head: per row and 128-entry vocabulary tile, the largest
 // bf16-rounded logit and its index (greedy sampling without writing the logits).
 constexpr int kEpiArgmax = 4;
@@ -68,10 +72,34 @@ struct GemmParams {
   // bh = bn / halves tokens each, into adjacent TMEM columns, its activation tile
   // loaded as that many TMA boxes
   int bn, bh, halves, stages, splits, epilogue;
+  int flags;  // kFlag* tuning switches (lsb_gemm_force_plan's high bits)
   uint32_t idesc;
   int* error_flag;
   CommDev comm;  // row-parallel all-reduce (AR variants only)
 };
+
+// L2 policy hints for the TMA loads (createpolicy): the weights are streamed once
+// (evict first), the activation tiles are read by every weight tile (evict last).
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map,
+                                                 uint64_t* bar, int x, int y, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(pol)
+      : "memory");
+}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
@@ -207,7 +235,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   // different block spreads those reads over all of x instead of having every CTA
   // hit the same L2 lines at the same moment. (The fp32 sum order per tile changes
   // with it; results stay deterministic.)
-  const int rot = nk > 0 ? static_cast<int>((static_cast<int64_t>(tile_n) * 7 + tile_m * 3) % nk) : 0;
+  const int rot = nk > 0 && !(p.flags & kFlagNoRotate)
+                      ? static_cast<int>((static_cast<int64_t>(tile_n) * 7 + tile_m * 3) % nk)
+                      : 0;
   uint32_t tmem_cols = 32;
   while (tmem_cols < static_cast<uint32_t>(p.bn)) tmem_cols <<= 1;
 
@@ -245,15 +275,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int pre = nk < stages ? nk : stages;
       // K block of pipeline step i, and the tensor-map pair and K offset it reads
       auto kb_of = [&](int i) { return kb_begin + (i + rot) % nk; };
+      const bool hints = p.flags & kFlagCacheHints;
+      const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
       auto load_w = [&](uint8_t* dst, uint64_t* bar, int kb) {
-        if (kb < p.kb1) tma_load_2d(dst, &tmap_w, bar, kb * kBK, n0);
-        else tma_load_2d(dst, &tmap_w2, bar, (kb - p.kb1) * kBK, n0);
+        const CUtensorMap* map = kb < p.kb1 ? &tmap_w : &tmap_w2;
+        const int kx = (kb < p.kb1 ? kb : kb - p.kb1) * kBK;
+        if (hints) tma_load_2d_hint(dst, map, bar, kx, n0, pol_w);
+        else tma_load_2d(dst, map, bar, kx, n0);
       };
       auto load_x = [&](uint8_t* dst, uint64_t* bar, int kb) {
+        const CUtensorMap* map = kb < p.kb1 ? &tmap_x : &tmap_x2;
+        const int kx = (kb < p.kb1 ? kb : kb - p.kb1) * kBK;
         for (int h = 0; h < p.halves; ++h) {
           uint8_t* d = dst + h * p.bh * kBK * 2;
-          if (kb < p.kb1) tma_load_2d(d, &tmap_x, bar, kb * kBK, m0 + h * p.bh);
-          else tma_load_2d(d, &tmap_x2, bar, (kb - p.kb1) * kBK, m0 + h * p.bh);
+          if (hints) tma_load_2d_hint(d, map, bar, kx, m0 + h * p.bh, pol_x);
+          else tma_load_2d(d, map, bar, kx, m0 + h * p.bh);
         }
       };
       for (int i = 0; i < pre; ++i) {
@@ -306,6 +342,13 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Phase 1: accumulator (TMEM lanes = weight rows) -> red[token][row] in fp32.
     const int q = warp & 3;
     const int row = 32 * q + lane;
+    if ((p.flags & kFlagSleepWait) && nk > 0) {
+      // the main loop takes microseconds: poll the accumulator barrier with back-off
+      // instead of keeping four warps spinning next to the producer and MMA threads
+      const uint32_t addr = smem_u32(tmem_full);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(addr, 0) && clock64() - t0 < kTimeoutCycles) __nanosleep(256);
+    }
     have_acc = nk > 0 && mbar_wait(tmem_full, 0, p.error_flag);
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
@@ -697,8 +740,11 @@ Plan wide_plan(int64_t M, int64_t N, int64_t K) {
 }
 
 Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
-  const int force = g_force_plan.load(std::memory_order_relaxed);
-  if (M > 256 && M <= kWideMax && !single_wave && (force == kPlanAuto || force == kPlanWide))
+  // The wide tile is taken only when asked for: at the Ouro-1.4B decode shapes it was
+  // measured slower than 96-token tiles (263 tokens, the layer's four GEMMs: 79.5 vs
+  // 60.9 us), its one-CTA-per-SM grids leaving a third of the SMs idle.
+  const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
+  if (M > 256 && M <= kWideMax && !single_wave && force == kPlanWide)
     return wide_plan(M, N, K);
   Plan pl;
   pl.halves = 1;
@@ -777,7 +823,8 @@ extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
 }
 
 extern "C" int lsb_gemm_force_plan(int32_t mode) {
-  LSB_REQUIRE(mode >= kPlanAuto && mode <= kPlanOnePerSm, "gemm_force_plan: mode %d", mode);
+  LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanOnePerSm && (mode >> 4) < 8,
+              "gemm_force_plan: mode %d", mode);
   g_force_plan.store(mode, std::memory_order_relaxed);
   return LSB_OK;
 }
@@ -864,6 +911,7 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   p.stages = pl.stages;
   p.splits = pl.splits;
   p.epilogue = epilogue;
+  p.flags = g_force_plan.load(std::memory_order_relaxed) >> 4;
   p.idesc = make_idesc(bh);
   p.error_flag = lsb_device_error_flag();
   const bool ar = comm != nullptr;

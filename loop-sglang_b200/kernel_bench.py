@@ -156,6 +156,11 @@ def bench_gemm(args, ops, name: str) -> dict:
     def launch(i):
         ops.gemm(x, ws[i % copies], None, epi, out=y)
 
+    if args.cublas_only:  # a process that launches only cuBLAS's kernel (profiler captures)
+        yc = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        us_c = _time_graph(lambda i: torch.matmul(x, ws[i % copies].t(), out=yc), args.reps)
+        return {"kernel": "cublas", "shape": name, "tokens": m, "N": n, "K": k,
+                "us_cublas": round(us_c, 2)}
     us = _time_graph(launch, args.reps)
     nbytes = w_bytes + m * k * 2 + m * cols * 2
     flops = 2.0 * m * n * k
@@ -312,9 +317,13 @@ def main(argv=None) -> None:
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
     gm.add_argument("--cublas", action="store_true",
                     help="also time torch.matmul (cuBLAS) on the same shapes and weights")
-    gm.add_argument("--plan", type=int, default=0, choices=[0, 1, 2, 3],
-                    help="tile plan: 0 automatic, 1 one wide tile (257-384 tokens), 2 tiles "
-                         "of <= 96 tokens, 3 one CTA per SM")
+    gm.add_argument("--cublas-only", action="store_true",
+                    help="time only torch.matmul (cuBLAS), launching no kernel of this library")
+    gm.add_argument("--plan", type=int, nargs="+", default=[0],
+                    help="tile plans to time (lsb_gemm_force_plan modes): 0 automatic, 1 one "
+                         "wide tile (257-384 tokens), 2 tiles of <= 96 tokens, 3 one CTA per "
+                         "SM; + 16 x tuning flags (1 K loop unrotated, 2 L2 hints, 4 "
+                         "epilogue back-off)")
     ga = sub.add_parser("gemm_ar")
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
@@ -363,12 +372,14 @@ def main(argv=None) -> None:
     if args.kernel == "attention":
         print(json.dumps(bench_attention(args, ops)), flush=True)
     else:
-        ops.check(ops.lib().lsb_gemm_force_plan(args.plan), "gemm_force_plan")
-        for name in args.shape:
-            line = bench_gemm(args, ops, name)
-            line["plan"] = args.plan
-            line["tile_plan"] = ops.gemm_plan(args.tokens, *tp_shape(name, args.tp)[:2])
-            print(json.dumps(line), flush=True)
+        for plan in args.plan:
+            ops.check(ops.lib().lsb_gemm_force_plan(plan), "gemm_force_plan")
+            for name in args.shape:
+                line = bench_gemm(args, ops, name)
+                line["plan"] = plan
+                line["tile_plan"] = ops.gemm_plan(args.tokens, *tp_shape(name, args.tp)[:2])
+                print(json.dumps(line), flush=True)
+        ops.check(ops.lib().lsb_gemm_force_plan(0), "gemm_force_plan")
 
 
 if __name__ == "__main__":

@@ -34,10 +34,12 @@ import pytest
 import torch
 
 import scale_scenarios as S
+from __graft_entry__ import load_package
 from cdb_lockstep import gpu_run, make_scenario, token_matches
 from oracle.model import LoopedConfig, LoopedModel, PagedKVPool, make_weights, with_fp32_matrices
 from replay import device_batch, gpu_model, load
 
+load_package()
 pytestmark = pytest.mark.gpu
 
 REL = 2e-2
