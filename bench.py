@@ -211,12 +211,12 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int,
     small KV pool of the model's own policy, then decoded for 3 steps, each step fed the
     CUDA path's own greedy tokens; the oracle (bf16 rounding points) runs the same
     prefill and steps on rank 0. A token agrees when the argmaxes match; it is a near tie
-    when they differ but the oracle's logit of the CUDA path's token is within 2e-2 x
-    max |logit| of its maximum (bf16 reduction order may take either); anything else is
-    a mismatch. ``agree_decided`` leaves the near ties out. The oracle also runs in fp32
-    arithmetic on the same weights: after 96 layer passes of a random-init model two bf16
-    computations that differ only in summation order drift apart by about as much as
-    either drifts from fp32, so ``vs_fp32`` puts the logit error in that context.
+    when they differ but the oracle's logit of the CUDA path's token is within the bf16
+    noise of its maximum -- the larger of 2e-2 x max |logit| and the step's distance
+    between the bf16 oracle and the same computation in fp32 (after 96 layer passes of a
+    random-init model bf16 arithmetic alone moves the logits by ~10% of their range, so
+    either token may win); anything else is a mismatch. ``agree_decided`` leaves the near
+    ties out. ``vs_fp32`` compares both bf16 computations with the fp32 one.
     Collective over the ranks: every rank runs the CUDA part.
     """
     from oracle import model as om
@@ -302,14 +302,18 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int,
         scale = ref.abs().max(-1).values
         worst = max(worst, rel(got[i], ref))
         worst_exact = max(worst_exact, rel(got[i], exact[i]))
-        floor = max(floor, rel(ref, exact[i]))
+        step_floor = rel(ref, exact[i])
+        floor = max(floor, step_floor)
+        # a token is decided only where the oracle's top-two margin exceeds what bf16
+        # arithmetic itself moves the logits at this step (at least 2e-2 of max |logit|)
+        tol = max(2e-2, step_floor)
         gi, ri = got[i].argmax(-1), ref.argmax(-1)
         agree_exact += int((gi == exact[i].argmax(-1)).sum())
         oracle_exact += int((ri == exact[i].argmax(-1)).sum())
         for r in range(b):
             if int(gi[r]) == int(ri[r]):
                 counts["agree"] += 1
-            elif ref[r, gi[r]] >= ref[r, ri[r]] - 2e-2 * scale[r]:
+            elif ref[r, gi[r]] >= ref[r, ri[r]] - tol * scale[r]:
                 counts["near_tie"] += 1
             else:
                 counts["mismatch"] += 1

@@ -123,6 +123,13 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
                         int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
                         void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Kernel selection of later lsb_paged_attention calls of this process, for
+ * benchmarks and tuning: 0 automatic (calls with several query rows per request
+ * take the tensor-core kernel, decode calls the streaming or per-CTA kernel),
+ * 1 the tensor-core kernel for every call, 2 never. No counterpart in the
+ * reference. */
+int lsb_attention_force_kernel(int32_t mode);
+
 /* lsb_paged_attention for callers that cannot allocate device memory (a plugin
  * whose host framework owns all device memory and passes only inputs and
  * outputs, or a loop that must not pay cudaMalloc's device-wide
@@ -178,6 +185,9 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
  * tokens, 3 one CTA per SM for every tile size. No counterpart in the
  * reference (its cuBLAS heuristics). */
 int lsb_gemm_force_plan(int32_t mode);
+/* Largest token-tile width later lsb_gemm* calls may use (0 automatic; else a
+ * multiple of 16 in 16..256), for the same benchmarks and tuning. */
+int lsb_gemm_force_tile_tokens(int32_t tokens);
 
 /* y[M, N] = [x1 | x2] . w^T (+ bias) with w [N, K1 + K2]: the product over the
  * concatenation of two activation tensors along K without materialising it (the

@@ -57,6 +57,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_gemm_plan": (ctypes.c_int, [I64, I64, I64, P]),
     "lsb_gemm_argmax_tiles": (I64, [I64]),
     "lsb_gemm_force_plan": (ctypes.c_int, [I32]),
+    "lsb_gemm_force_tile_tokens": (ctypes.c_int, [I32]),
+    "lsb_attention_force_kernel": (ctypes.c_int, [I32]),
     "lsb_gemm_argmax": (ctypes.c_int, [P, I64, P, I64, P, I64, I64, I64, I64, P]),
     "lsb_argmax_pairs": (ctypes.c_int, [P, P, I64, I64, I64, I64, I64, P]),
     "lsb_gemm_concat": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, P, I64, I64, I64, I64,
@@ -146,6 +148,8 @@ _launches = 0
 _NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "lsb_ipc_handle",
                  "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy",
                  "lsb_gemm_plan", "lsb_gemm_argmax_tiles", "lsb_gemm_force_plan",
+                 "lsb_gemm_force_tile_tokens",
+                 "lsb_attention_force_kernel",
                  "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
                  "lsb_radix_insert", "lsb_radix_lock", "lsb_radix_indices", "lsb_radix_evict",
                  "lsb_radix_size_info", "lsb_radix_check"}

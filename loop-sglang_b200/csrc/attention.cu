@@ -14,6 +14,9 @@
 // one split writes fp32 partials (unnormalised output, running max, sum) to the
 // workspace; the last CTA of the row to finish (a per-row arrival counter)
 // merges them and resets the counter, so one launch serves a whole layer.
+#include <atomic>
+
+#include "attention_prefill.cuh"
 #include "common.cuh"
 #include "mbarrier.cuh"
 
@@ -896,6 +899,16 @@ bool stream_eligible(int32_t hq, int32_t hkv, int32_t d) {
 
 using namespace lsb;
 
+// Kernel selection for benchmarks and tuning (lsb_attention_force_kernel): 0 automatic,
+// 1 the tensor-core kernel for every call, 2 never.
+static std::atomic<int> g_attention_force{0};
+
+extern "C" int lsb_attention_force_kernel(int32_t mode) {
+  LSB_REQUIRE(mode >= 0 && mode <= 2, "attention_force_kernel: mode %d", mode);
+  g_attention_force.store(mode, std::memory_order_relaxed);
+  return LSB_OK;
+}
+
 // The streaming kernel runs when its stage fits and its per-(row, warp) counters fit
 // the counter region; otherwise the per-CTA kernel does.
 static bool use_stream(int64_t rows, int32_t hq, int32_t hkv, int32_t d, int32_t page_size,
@@ -947,6 +960,33 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
               "paged_attention: strides must be multiples of 8 elements");
   LSB_REQUIRE(slot_stride >= (int64_t)hkv * head_dim, "paged_attention: slot stride too small");
   if (rows <= 0) return LSB_OK;
+  const int force = g_attention_force.load(std::memory_order_relaxed);
+  if ((rows > num_reqs && force != 2) || force == 1) {
+    // requests with several query rows (prefill, extend): QK^T and PV on the tensor cores
+    PrefillParams pp;
+    pp.out = static_cast<bf16*>(out);
+    pp.out_stride = out_stride;
+    pp.q = static_cast<const bf16*>(q);
+    pp.q_stride = q_stride;
+    pp.k_cache = static_cast<const bf16*>(k_cache);
+    pp.v_cache = static_cast<const bf16*>(v_cache);
+    pp.slot_stride = slot_stride;
+    pp.num_slots = num_slots;
+    pp.page_table = page_table;
+    pp.pt_stride = pt_stride;
+    pp.cache_seqlens = cache_seqlens;
+    pp.cu_seqlens_q = cu_seqlens_q;
+    pp.num_reqs = static_cast<int>(num_reqs);
+    pp.hq = hq;
+    pp.hkv = hkv;
+    pp.page_size = page_size;
+    pp.max_seqlen = max_seqlen;
+    pp.scale_log2 = scale * kLog2e;
+    pp.error_flag = lsb_device_error_flag();
+    // a request's query rows are at most its keys (<= max_seqlen) and at most all rows
+    const int64_t max_q = rows < max_seqlen ? rows : max_seqlen;
+    return launch_prefill_attention(pp, max_q, head_dim, as_stream(stream));
+  }
   if (use_stream(rows, hq, hkv, head_dim, page_size, slot_stride)) {
     const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
     const int64_t splits = (max_seqlen + chunk - 1) / chunk;

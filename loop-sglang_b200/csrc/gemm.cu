@@ -587,6 +587,8 @@ struct Plan {
 
 // Plan selection for benchmarks and tuning (lsb_gemm_force_plan): 0 automatic.
 std::atomic<int> g_force_plan{0};
+// Largest token-tile width the planner may use (lsb_gemm_force_tile_tokens): 0 automatic.
+std::atomic<int> g_force_tile{0};
 
 int num_sms() {
   static int sms = 0;
@@ -757,7 +759,10 @@ Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   // tile fewest times. A single-wave plan (the fused all-reduce, whose CTAs must all be
   // resident) keeps 256-token tiles too: its caller sizes each launch's rows for them.
   const bool narrow = M > 256 && M <= 512 && !single_wave;
-  const int64_t m_tiles = narrow ? (M + 95) / 96 : (M + 255) / 256;
+  const int forced_tile = single_wave ? 0 : g_force_tile.load(std::memory_order_relaxed);
+  const int64_t m_tiles = forced_tile ? (M + forced_tile - 1) / forced_tile
+                          : narrow    ? (M + 95) / 96
+                                      : (M + 255) / 256;
   int64_t bn = (((M + m_tiles - 1) / m_tiles + 15) / 16) * 16;
   if (bn > 256) bn = 256;
   if (bn < 16) bn = 16;
@@ -826,6 +831,13 @@ extern "C" int lsb_gemm_force_plan(int32_t mode) {
   LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanOnePerSm && (mode >> 4) < 8,
               "gemm_force_plan: mode %d", mode);
   g_force_plan.store(mode, std::memory_order_relaxed);
+  return LSB_OK;
+}
+
+extern "C" int lsb_gemm_force_tile_tokens(int32_t tokens) {
+  LSB_REQUIRE(tokens == 0 || (tokens >= 16 && tokens <= 256 && tokens % 16 == 0),
+              "gemm_force_tile_tokens: %d (0, or a multiple of 16 in 16..256)", tokens);
+  g_force_tile.store(tokens, std::memory_order_relaxed);
   return LSB_OK;
 }
 

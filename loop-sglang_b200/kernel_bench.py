@@ -309,6 +309,8 @@ def main(argv=None) -> None:
     at.add_argument("--shared-prefix", type=int, default=0,
                     help="tokens of each row's context shared with its group (page multiple)")
     at.add_argument("--groups", type=int, default=4, help="prefix groups (rows interleaved)")
+    at.add_argument("--force", type=int, nargs="+", default=[0],
+                    help="kernel selections to time: 0 automatic, 1 tensor-core kernel, 2 not")
     gm = sub.add_parser("gemm")
     gm.add_argument("--tokens", type=int, default=143)
     gm.add_argument("--shape", nargs="+", default=["qkv", "o", "gate_up", "down"],
@@ -317,6 +319,8 @@ def main(argv=None) -> None:
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
     gm.add_argument("--cublas", action="store_true",
                     help="also time torch.matmul (cuBLAS) on the same shapes and weights")
+    gm.add_argument("--tile", type=int, nargs="+", default=[0],
+                    help="largest token-tile widths to time (0 automatic)")
     gm.add_argument("--cublas-only", action="store_true",
                     help="time only torch.matmul (cuBLAS), launching no kernel of this library")
     gm.add_argument("--plan", type=int, nargs="+", default=[0],
@@ -370,16 +374,24 @@ def main(argv=None) -> None:
               flush=True)
         return
     if args.kernel == "attention":
-        print(json.dumps(bench_attention(args, ops)), flush=True)
+        for mode in args.force:
+            ops.check(ops.lib().lsb_attention_force_kernel(mode), "attention_force_kernel")
+            line = bench_attention(args, ops)
+            line["force"] = mode
+            print(json.dumps(line), flush=True)
+        ops.check(ops.lib().lsb_attention_force_kernel(0), "attention_force_kernel")
     else:
-        for plan in args.plan:
-            ops.check(ops.lib().lsb_gemm_force_plan(plan), "gemm_force_plan")
-            for name in args.shape:
-                line = bench_gemm(args, ops, name)
-                line["plan"] = plan
-                line["tile_plan"] = ops.gemm_plan(args.tokens, *tp_shape(name, args.tp)[:2])
-                print(json.dumps(line), flush=True)
+        for tile in args.tile:
+            ops.check(ops.lib().lsb_gemm_force_tile_tokens(tile), "gemm_force_tile_tokens")
+            for plan in args.plan:
+                ops.check(ops.lib().lsb_gemm_force_plan(plan), "gemm_force_plan")
+                for name in args.shape:
+                    line = bench_gemm(args, ops, name)
+                    line["plan"], line["tile"] = plan, tile
+                    line["tile_plan"] = ops.gemm_plan(args.tokens, *tp_shape(name, args.tp)[:2])
+                    print(json.dumps(line), flush=True)
         ops.check(ops.lib().lsb_gemm_force_plan(0), "gemm_force_plan")
+        ops.check(ops.lib().lsb_gemm_force_tile_tokens(0), "gemm_force_tile_tokens")
 
 
 if __name__ == "__main__":

@@ -168,6 +168,25 @@ def test_paged_attention(d: int, page: int, mode: str) -> None:
     no_device_errors()
 
 
+@pytest.mark.parametrize("hq,hkv,d", [(16, 16, 128), (8, 2, 64), (55, 55, 96), (4, 4, 32)])
+@pytest.mark.parametrize("page", [1, 16])
+def test_paged_attention_prefill_tensor_cores(hq: int, hkv: int, d: int, page: int) -> None:
+    """Prefill and extend rows (several query rows per request) take the mma.sync kernel:
+    fresh prompts longer than one 64-row block and one 64-key tile, a request with a
+    cached prefix, a decode row in the same batch, a request with no rows."""
+    g = gen(hq * d + page)
+    q_lens, kv_lens = [130, 64, 1, 77, 0], [130, 200, 50, 300, 9]
+    q, kc, vc, table, seq, cu = _paged_case(g, hq, hkv, d, page, q_lens, kv_lens)
+    scale = d ** -0.5
+    ref = O.paged_attention(q, kc, vc, table, seq, cu, scale)
+    kd = kc.to(DEV).view(-1, hkv * d)
+    vd = vc.to(DEV).view(-1, hkv * d)
+    got = ops.paged_attention(q.to(DEV), kd, vd, table.to(DEV), seq.to(DEV), cu.to(DEV), page,
+                              int(table.shape[1] * page), scale, hkv)
+    close(got, ref)
+    no_device_errors()
+
+
 @pytest.mark.parametrize("hq,hkv,d,page", [
     (55, 55, 96, 16),   # Huginn heads: a stage would exceed 64 KB -> per-CTA kernel
     (40, 8, 64, 16),    # 3 heads per consumer warp (streaming kernel, 4-head variant)
