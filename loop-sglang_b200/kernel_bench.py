@@ -144,6 +144,10 @@ def bench_gemm(args, ops, name: str) -> dict:
     """One ``y = x . w^T`` launch with the weight streamed from HBM (rotating copies)."""
     dev = torch.device("cuda", torch.cuda.current_device())
     n, k, swiglu = tp_shape(name, args.tp)
+    if args.n:
+        n = args.n
+    if args.k:
+        k = args.k
     m = args.tokens
     w_bytes = n * k * 2
     copies = max(2, math.ceil(2 * L2_BYTES / w_bytes))
@@ -319,6 +323,8 @@ def main(argv=None) -> None:
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
     gm.add_argument("--cublas", action="store_true",
                     help="also time torch.matmul (cuBLAS) on the same shapes and weights")
+    gm.add_argument("--n", type=int, default=0, help="override the shape's output rows")
+    gm.add_argument("--k", type=int, default=0, help="override the shape's reduction size")
     gm.add_argument("--tile", type=int, nargs="+", default=[0],
                     help="largest token-tile widths to time (0 automatic)")
     gm.add_argument("--cublas-only", action="store_true",
