@@ -3,20 +3,24 @@
 // The weight is the A operand: a CTA owns 128 weight rows (the UMMA M) and up
 // to 256 tokens (the UMMA N, `bn`), so a decode batch of B <= 256 tokens is one
 // tile column and every weight byte is streamed from HBM exactly once per call.
-// Warp roles in a CTA of 192 threads:
+// Warp roles in a CTA of 256 threads:
 //   warp 0      TMA producer: 128x64 weight tile + bn x 64 activation tile per
 //               stage into 128-byte-swizzled shared memory, mbarrier tx counts;
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
 //               (kind::f16, fp32 accumulator in TMEM, 4 MMAs of K=16 per stage),
 //               tcgen05.commit frees each stage and finally signals the epilogue;
-//   warps 2..5  epilogue: tcgen05.ld of the 128 x bn accumulator (warp w reads
-//               TMEM lanes 32*(w%4)..+31) into a token-major fp32 tile in shared
-//               memory (the drained stage buffers), then coalesced 8-byte stores
-//               of 4 output columns per thread with the fused bias / SwiGLU.
+//   all 8 warps epilogue, once the accumulator is complete: tcgen05.ld of the
+//               128 x bn accumulator (warp w reads TMEM lanes 32*(w%4)..+31, the
+//               16-column chunks of its half w/4) into token-major fp32 rows in
+//               shared memory (the drained stage buffers), then coalesced 8-byte
+//               stores of 4 output columns per thread with the fused bias / SwiGLU.
+//               The producer and MMA warps, idle by then, take part too.
 // When the tile grid alone cannot fill the SMs the K loop is split over the S
-// CTAs of a thread-block cluster: each computes a K range, and after a cluster
-// barrier every CTA sums one slice of the tile over the S shared-memory tiles
-// (distributed shared memory, fixed order: deterministic) and stores it.
+// CTAs of a thread-block cluster: each computes a K range, and CTA s finishes
+// token slice s of the tile. Each CTA pushes its fp32 partials of the other slices
+// into their owners' shared memory (distributed shared-memory stores, which do not
+// wait on a round trip the way remote loads do); after a cluster barrier every CTA
+// sums its S partials from its own shared memory in split order (deterministic).
 // The weight stream does not depend on the previous kernel, so the producer
 // issues the first stages' weight loads before griddepcontrol.wait (programmatic
 // dependent launch) and only the activation loads after it.
@@ -41,7 +45,7 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kMaxStages = 8;
 constexpr int kMaxSplits = 8;  // portable cluster size
@@ -129,14 +133,6 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t addr, uint32_t rank) {
   return out;
 }
 
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr));
-  return v;
-}
-
 // K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row atoms 1024 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc(const void* tile) {
   const uint64_t addr = smem_u32(tile);
@@ -176,9 +172,6 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-__device__ __forceinline__ void epi_barrier() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-}
 
 // Four consecutive output columns col..col+3 of token m (bf16), 8-byte store when
 // aligned and in range, else element by element.
@@ -219,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* empty = full + kMaxStages;
   uint64_t* tmem_full = empty + kMaxStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full + 1);
-  // After the main loop the drained stage buffers hold the token-major fp32 tile.
+  // After the main loop the drained stage buffers receive the epilogue's fp32 partials.
   float* red = reinterpret_cast<float*>(smem);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -338,49 +331,88 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (ok) umma_commit(tmem_full);
     }
-  } else {
-    // Phase 1: accumulator (TMEM lanes = weight rows) -> red[token][row] in fp32.
-    const int q = warp & 3;
+  }
+  __syncwarp();
+  // The tile's valid tokens are finished in S token slices, one per CTA of the cluster:
+  // CTA `split` owns tokens [split * per, split * per + per) and receives every CTA's
+  // fp32 partial of them in its drained stage buffers, as recv[src][token - slice start]
+  // [weight row] (S = 1: the whole tile, recv[0][token][row]).
+  const int tokens = p.M - m0 < p.bn ? p.M - m0 : p.bn;
+  const int per = (tokens + S - 1) / S;
+  {
+    // Phase 1 (every warp): accumulator (TMEM lanes = weight rows) -> the owners' recv
+    // buffers in fp32; warp w drains the 16-column chunks w/4, w/4 + 2, ... of lanes
+    // 32*(w%4).. . Partials of other CTAs' slices are pushed with distributed-shared-
+    // memory stores (fire and forget) instead of being pulled by the owner later.
+    const int q = warp & 3, half = warp >> 2;
     const int row = 32 * q + lane;
     if ((p.flags & kFlagSleepWait) && nk > 0) {
       // the main loop takes microseconds: poll the accumulator barrier with back-off
-      // instead of keeping four warps spinning next to the producer and MMA threads
+      // instead of keeping six warps spinning next to the producer and MMA threads
       const uint32_t addr = smem_u32(tmem_full);
       const long long t0 = clock64();
       while (!mbar_try_wait(addr, 0) && clock64() - t0 < kTimeoutCycles) __nanosleep(256);
     }
-    have_acc = nk > 0 && mbar_wait(tmem_full, 0, p.error_flag);
+    // warp-uniform (the TMEM loads below are .sync.aligned): a lane whose bounded wait
+    // gave up makes the whole warp treat the accumulator as absent
+    have_acc = __all_sync(0xffffffffu, nk > 0 && mbar_wait(tmem_full, 0, p.error_flag));
     asm volatile("tcgen05.fence::after_thread_sync;");
+    // Every MMA of this CTA has completed, so its stage buffers are no longer read: they
+    // may now receive the peers' partials (the wait below holds the stores back until
+    // every CTA of the cluster is that far).
+    if (CLUSTER) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16);
-    // Double-buffered: the load of columns c0+16.. is in flight while columns
-    // c0.. are stored (tcgen05.wait::ld waits for every earlier load).
+    const uint32_t recv_addr = smem_u32(red);
+    // Stores the 16 tokens c0.. of this thread's weight row to their owners.
+    auto put16 = [&](int c0, const uint32_t* v) {
+      if (!CLUSTER) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < tokens) red[(c0 + j) * kBM + row] = __uint_as_float(v[j]);
+        return;
+      }
+      int o = c0 / per, jl = c0 - o * per;  // owner and its slice index of token c0
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (c0 + j < tokens) {
+          const uint32_t a = recv_addr + 4u * static_cast<uint32_t>((split * per + jl) * kBM + row);
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(a, o)),
+                       "f"(__uint_as_float(v[j]))
+                       : "memory");
+        }
+        if (++jl == per) jl = 0, ++o;
+      }
+    };
+    // Double-buffered: the load of the next chunk is in flight while this one is
+    // stored (tcgen05.wait::ld waits for every earlier load).
     uint32_t va[16], vb[16];
-    if (have_acc) {
-      tmem_ld16_issue(taddr, va);
-      tmem_ld_wait();
+    const int c_first = 16 * half;
+    if (have_acc && c_first < p.bn) {
+      tmem_ld16_issue(taddr + c_first, va);
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) va[j] = 0u, vb[j] = 0u;
     }
-    for (int c0 = 0; c0 < p.bn; c0 += 32) {
-      const bool more_b = c0 + 16 < p.bn, more_a = c0 + 32 < p.bn;
-      if (have_acc && more_b) tmem_ld16_issue(taddr + c0 + 16, vb);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) red[(c0 + j) * kBM + row] = __uint_as_float(va[j]);
+    if (CLUSTER) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (have_acc && c_first < p.bn) tmem_ld_wait();
+    for (int c0 = c_first; c0 < tokens; c0 += 64) {
+      const bool more_b = c0 + 32 < tokens, more_a = c0 + 64 < tokens;
+      if (have_acc && more_b) tmem_ld16_issue(taddr + c0 + 32, vb);
+      put16(c0, va);
       if (have_acc) tmem_ld_wait();
       if (!more_b) break;
-      if (have_acc && more_a) tmem_ld16_issue(taddr + c0 + 32, va);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) red[(c0 + 16 + j) * kBM + row] = __uint_as_float(vb[j]);
+      if (have_acc && more_a) tmem_ld16_issue(taddr + c0 + 64, va);
+      put16(c0 + 32, vb);
       if (have_acc) tmem_ld_wait();
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
-  if (CLUSTER) cluster_sync_all();
+  if (CLUSTER) cluster_sync_all();  // every partial has landed in its owner's buffer
   else __syncthreads();
 
-  if (warp >= 2) {
-    // Phase 2: 4-column quads of the output rows, summed over the cluster's tiles.
+  {
+    // Phase 2: 4-column quads of this CTA's token slice, summed over the S partials in
+    // split order (deterministic), all from this CTA's own shared memory.
     // Specialised at compile time (epilogue kind, one tile or a cluster): a generic
     // loop with runtime branches compiles to a several times slower sequence.
     constexpr bool kSwiglu = EPI == LSB_EPI_SWIGLU;
@@ -388,63 +420,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     bf16* const y = p.y;
     const int64_t ldy = p.ldy;
     const int ncols = kSwiglu ? p.N / 2 : p.N;
-    const int t = threadIdx.x - 64;
-    const int tokens = p.M - m0 < p.bn ? p.M - m0 : p.bn;
-    int tb = 0, te = tokens;
-    if (CLUSTER) {  // each CTA of the cluster finishes a token slice of the tile
-      const int per = (tokens + S - 1) / S;
-      tb = split * per;
-      te = tb + per < tokens ? tb + per : tokens;
-    }
+    const int t = threadIdx.x;
+    const int tb = split * per;
+    const int te = tb + per < tokens ? tb + per : tokens;
     const int count = te > tb ? (te - tb) << kQuadShift : 0;
-    const uint32_t red_addr = smem_u32(red);
     uint32_t ar_epoch = 0;  // this call's all-reduce epoch (AR variants)
     if (AR) {
       asm volatile("griddepcontrol.wait;" ::: "memory");
       ar_epoch = comm_epoch(p.comm, kOpGemmAllReduce);
     }
-    // kU quads per thread and pass: with every split's loads of all of them issued
-    // before the sums, kU x S distributed-shared-memory loads are in flight.
-    constexpr int kU = kSwiglu ? 1 : 2;
-    for (int base = t; base < count; base += 128 * kU) {
+    constexpr int kU = kSwiglu ? 2 : 4;  // quads per thread and pass
+    const int src_stride = per * kBM;    // floats between two sources' partials
+    for (int base = t; base < count; base += kThreads * kU) {
       float4 acc[kU], accu[kU];
-      if (!CLUSTER) {
 #pragma unroll
-        for (int u2 = 0; u2 < kU; ++u2) {
-          const int idx = base + 128 * u2;
-          const int off = (tb + (idx >> kQuadShift)) * kBM + 4 * (idx & ((1 << kQuadShift) - 1));
-          if (idx < count) {
-            acc[u2] = *reinterpret_cast<const float4*>(red + off);
-            if (kSwiglu) accu[u2] = *reinterpret_cast<const float4*>(red + off + 64);
-          }
-        }
-      } else {
-        float4 xs[kU][kMaxSplits], gs[kU][kMaxSplits];
+      for (int u2 = 0; u2 < kU; ++u2) {
+        acc[u2] = make_float4(0.f, 0.f, 0.f, 0.f);
+        accu[u2] = acc[u2];
+      }
 #pragma unroll
-        for (int s2 = 0; s2 < kMaxSplits; ++s2) {
+      for (int src = 0; src < (CLUSTER ? kMaxSplits : 1); ++src) {
+        if (src < S) {
 #pragma unroll
           for (int u2 = 0; u2 < kU; ++u2) {
-            const int idx = base + 128 * u2;
-            const int off = (tb + (idx >> kQuadShift)) * kBM + 4 * (idx & ((1 << kQuadShift) - 1));
-            if (s2 < S && idx < count) {
-              xs[u2][s2] = ld_cluster_f4(map_rank(red_addr + 4u * off, s2));
-              if (kSwiglu) gs[u2][s2] = ld_cluster_f4(map_rank(red_addr + 4u * (off + 64), s2));
-            }
-          }
-        }
-        // summed in split order: deterministic
-#pragma unroll
-        for (int u2 = 0; u2 < kU; ++u2) {
-          acc[u2] = make_float4(0.f, 0.f, 0.f, 0.f);
-          accu[u2] = acc[u2];
-#pragma unroll
-          for (int s2 = 0; s2 < kMaxSplits; ++s2) {
-            if (s2 < S) {
-              acc[u2].x += xs[u2][s2].x; acc[u2].y += xs[u2][s2].y;
-              acc[u2].z += xs[u2][s2].z; acc[u2].w += xs[u2][s2].w;
+            const int idx = base + kThreads * u2;
+            const int off = src * src_stride + (idx >> kQuadShift) * kBM +
+                            4 * (idx & ((1 << kQuadShift) - 1));
+            if (idx < count) {
+              const float4 v = *reinterpret_cast<const float4*>(red + off);
+              acc[u2].x += v.x; acc[u2].y += v.y; acc[u2].z += v.z; acc[u2].w += v.w;
               if (kSwiglu) {
-                accu[u2].x += gs[u2][s2].x; accu[u2].y += gs[u2][s2].y;
-                accu[u2].z += gs[u2][s2].z; accu[u2].w += gs[u2][s2].w;
+                const float4 g = *reinterpret_cast<const float4*>(red + off + 64);
+                accu[u2].x += g.x; accu[u2].y += g.y; accu[u2].z += g.z; accu[u2].w += g.w;
               }
             }
           }
@@ -452,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
 #pragma unroll
       for (int u2 = 0; u2 < kU; ++u2) {
-      const int idx = base + 128 * u2;
+      const int idx = base + kThreads * u2;
       if (idx >= count) break;
       const int qi = idx & ((1 << kQuadShift) - 1);
       const int m = tb + (idx >> kQuadShift);
@@ -515,24 +522,18 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   }
-  if (CLUSTER) cluster_sync_all();  // peers may still be reading this CTA's tile
-  if (AR && warp >= 2) {
+  if (AR) {
     // Row-parallel all-reduce of this CTA's region (rows m0+tb..m0+te of the tile's
     // 128 columns) with the same CTA of every rank, over NVLink.
-    const int t = threadIdx.x - 64;
-    const int tokens = p.M - m0 < p.bn ? p.M - m0 : p.bn;
-    int tb = 0, te = tokens;
-    if (CLUSTER) {
-      const int per = (tokens + S - 1) / S;
-      tb = split * per;
-      te = tb + per < tokens ? tb + per : tokens;
-      if (te < tb) te = tb;
-    }
+    const int t = threadIdx.x;
+    const int tb = split * per;
+    int te = tb + per < tokens ? tb + per : tokens;
+    if (te < tb) te = tb;
     const uint32_t epoch = comm_epoch(p.comm, kOpGemmAllReduce);
     const int w = p.N - n0 < kBM ? p.N - n0 : kBM;
     comm_complete(p.comm, tile_n % p.comm.world, epoch, p.y, p.ldy, m0 + tb, m0 + te, n0, w,
-                  p.N, t, 128, p.error_flag);
-    epi_barrier();
+                  p.N, t, kThreads, p.error_flag);
+    __syncthreads();
     if (t == 0) comm_finish(p.comm, kOpGemmAllReduce, epoch, gridDim.x * gridDim.y);
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
@@ -692,6 +693,13 @@ int max_active_clusters(int splits, size_t smem) {
   return n;
 }
 
+// The epilogue's receive buffers, S token slices of up to ceil(bn / S) tokens from each of
+// the S sources (fp32, 128 weight rows), reuse the drained stage buffers.
+bool recv_fits(int bn, int splits, int stages, int stage_bytes) {
+  const int64_t per = (bn + splits - 1) / splits;
+  return static_cast<int64_t>(splits) * per * kBM * 4 <= static_cast<int64_t>(stages) * stage_bytes;
+}
+
 size_t smem_for(int stages, int stage_bytes) {
   return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * kMaxStages + 1) * 8 + 16;
 }
@@ -699,7 +707,7 @@ size_t smem_for(int stages, int stage_bytes) {
 // Tile shape, pipeline depth and split-K factor. Two layouts are considered:
 //  * one CTA per SM: as many stages as fit (up to 8); the K loop is split over a
 //    cluster only as far as tiles x splits <= SMs and every cluster is co-resident;
-//  * two CTAs per SM: 3 stages (the least that still holds the fp32 tile for the
+//  * two CTAs per SM: 3 stages (the least that still hold the fp32 partials for the
 //    epilogue), splits up to 2 x SMs / tiles.
 // The second is taken when it puts more CTAs than SMs on the device: the per-SM
 // ingest of weight and activation tiles, not the pipeline depth, then limits the
@@ -707,8 +715,8 @@ size_t smem_for(int stages, int stage_bytes) {
 // cluster left for a second wave would double the kernel's time.
 // Plans lsb_gemm_force_plan can select (automatic otherwise).
 constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3;
-// Token counts a single wide tile (two MMA halves) covers: its fp32 tile, bn x 128 x 4
-// bytes, must fit in the drained stage buffers of one CTA's shared memory.
+// Token counts a single wide tile (two MMA halves) covers: its fp32 partials, about
+// bn x 128 x 4 bytes, must fit in the drained stage buffers of one CTA's shared memory.
 constexpr int kWideMax = 384;
 
 // One tile column of all M tokens (256 < M <= 384): the weights are streamed once and the
@@ -734,7 +742,8 @@ Plan wide_plan(int64_t M, int64_t N, int64_t K) {
   if (limit > kblocks) limit = kblocks;
   pl.splits = 1;
   for (int sp = limit; sp >= 2; --sp)
-    if (pl.tiles_n <= max_active_clusters(sp, pl.smem)) {
+    if (recv_fits(pl.bn, sp, stages, stage_bytes) &&
+        pl.tiles_n <= max_active_clusters(sp, pl.smem)) {
       pl.splits = sp;
       break;
     }
@@ -750,15 +759,16 @@ Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
     return wide_plan(M, N, K);
   Plan pl;
   pl.halves = 1;
-  // tokens per tile: up to 256 tokens one tile; for decode batches of 257-512 tokens,
-  // balanced tiles of at most 96 (263 -> 3 x 96, 512 -> 6 x 96): past one tile every weight
-  // tile is read again per token tile anyway (from L2), and narrow tiles let two or three
-  // CTAs share an SM, which evens out the waves (the Ouro layer's four GEMMs: 64.4 us at 263
-  // tokens as 2 x 144, 57.4 us as 3 x 96; 63.5 -> 57.7 us at 512 tokens of a TP=2 rank).
+  // tokens per tile: up to 192 tokens one tile; for decode batches of 193-512 tokens,
+  // balanced tiles of at most 96 (200 -> 3 x 80, 263 -> 3 x 96, 512 -> 6 x 96): narrow tiles
+  // let two CTAs share an SM, whose combined pipeline depth raises the SM's ingest of weight
+  // and activation tiles, the main loop's bound at these sizes (the Ouro layer's four GEMMs:
+  // 64.4 us at 263 tokens as 2 x 144, 57.4 us as 3 x 96; 63.5 -> 57.7 us at 512 tokens of a
+  // TP=2 rank; 61.1 -> 57.0 us at 256 tokens and 60.9 -> 57.8 us at 200 tokens).
   // Larger token counts (prefill, tensor-bound) keep 256-token tiles, which read each weight
   // tile fewest times. A single-wave plan (the fused all-reduce, whose CTAs must all be
   // resident) keeps 256-token tiles too: its caller sizes each launch's rows for them.
-  const bool narrow = M > 256 && M <= 512 && !single_wave;
+  const bool narrow = M > 192 && M <= 512 && !single_wave;
   const int forced_tile = single_wave ? 0 : g_force_tile.load(std::memory_order_relaxed);
   const int64_t m_tiles = forced_tile ? (M + forced_tile - 1) / forced_tile
                           : narrow    ? (M + 95) / 96
@@ -778,24 +788,31 @@ Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   if (stages_a > kMaxStages) stages_a = kMaxStages;
   if (stages_a < 3) stages_a = 3;
   const size_t smem_a = smem_for(stages_a, stage_bytes);
-  auto best_split = [&](int limit, size_t smem) {
+  auto best_split = [&](int limit, int stages, size_t smem) {
     if (limit > kMaxSplits) limit = kMaxSplits;
     if (limit > kblocks) limit = kblocks;
     for (int sp = limit; sp >= 2; --sp)
-      if (tiles <= max_active_clusters(sp, smem)) return sp;
+      if (recv_fits(pl.bn, sp, stages, stage_bytes) && tiles <= max_active_clusters(sp, smem))
+        return sp;
     return 1;
   };
-  const int split_a = tiles < sms ? best_split(sms / tiles, smem_a) : 1;
+  const int split_a = tiles < sms ? best_split(sms / tiles, stages_a, smem_a) : 1;
   pl.stages = stages_a;
   pl.splits = split_a;
   pl.smem = smem_a;
 
-  const size_t smem_b = smem_for(3, stage_bytes);
+  // two CTAs per SM: as many stages as two such CTAs' shared memory allows (4 for tiles of
+  // up to 80 tokens, else 3)
+  int stages_b = 3;
+  while (stages_b < kMaxStages &&
+         2 * (smem_for(stages_b + 1, stage_bytes) + 1024) <= static_cast<size_t>(kSmemPerSm))
+    ++stages_b;
+  const size_t smem_b = smem_for(stages_b, stage_bytes);
   if (!single_wave && force != kPlanOnePerSm &&
       2 * (smem_b + 1024) <= static_cast<size_t>(kSmemPerSm)) {
-    const int split_b = tiles < 2 * sms ? best_split(2 * sms / tiles, smem_b) : 1;
+    const int split_b = tiles < 2 * sms ? best_split(2 * sms / tiles, stages_b, smem_b) : 1;
     if (static_cast<int64_t>(tiles) * split_b > sms) {
-      pl.stages = 3;
+      pl.stages = stages_b;
       pl.splits = split_b;
       pl.smem = smem_b;
     }
@@ -934,6 +951,9 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   } else {
     memset(&p.comm, 0, sizeof(p.comm));
   }
+  LSB_REQUIRE(recv_fits(pl.bn, pl.splits, pl.stages, kABytes + pl.bn * kBK * 2),
+              "gemm: plan leaves no room for the epilogue (bn=%d, splits=%d, stages=%d)", pl.bn,
+              pl.splits, pl.stages);
   const bool cluster = pl.splits > 1;
   if (int rc = configure(cluster, epilogue, ar)) return rc;
   Kernel kernel = kernel_for(cluster, epilogue, ar);
