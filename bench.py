@@ -601,6 +601,7 @@ def run_b200(args) -> None:
     sched = torch.stack([base_seq + 1 + s for s in range(steps_total + 1)])  # incl. new token
     eng.ids.copy_(torch.randint(0, cfg.vocab, (bs,), device=dev, dtype=torch.int32))
     eng.set_batch(rows, sched[0])
+    prefix_groups = eng.share_prefixes() if radix else 0
     eng.capture()
     setup_s = time.perf_counter() - t0
     log(f"[bench] rank {rank}: batch {bs}, pool {num_pages} pages, setup {setup_s:.1f}s, "
@@ -657,13 +658,18 @@ def run_b200(args) -> None:
     reps = 20
     with torch.cuda.stream(s):
         out = torch.empty_like(q)
+
+        def attend():  # the step's attention call (shared prefixes read once per group)
+            ops.paged_attention_shared_prefix(q, kc, vc, eng.page_table, eng.cache_seqlens,
+                                              eng.cu_q, PAGE, eng.batch.max_seqlen,
+                                              cfg.head_dim ** -0.5, model.hkv,
+                                              eng.batch.prefix_groups, out=out)
+
         for _ in range(3):
-            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+            attend()
         a0.record(s)
         for _ in range(reps):
-            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+            attend()
         a1.record(s)
         s.synchronize()
     attn_s = a0.elapsed_time(a1) / 1000.0 / reps
@@ -724,6 +730,7 @@ def run_b200(args) -> None:
                      "step_bytes": step_bytes, "nvlink_bytes_per_step": nvlink_bytes,
                      "combined_step_frac": round(ideal_s / step_s, 4)},
         **({"radix": {"shared_prefix_tokens_matched": shared_hits,
+                      "prefix_groups": prefix_groups,
                       "kv_tokens_unique": kv_tokens,
                       "kv_tokens_per_row_sum": int(ctx.sum().item())}} if radix else {}),
         "e2e": {"value": tokens / (e2e_max / 1000.0), "unit": "tok/s",
@@ -1353,13 +1360,18 @@ def run_b200_huginn(args) -> None:
     reps = 20
     with torch.cuda.stream(s):
         out = torch.empty_like(q)
+
+        def attend():  # the step's attention call (shared prefixes read once per group)
+            ops.paged_attention_shared_prefix(q, kc, vc, eng.page_table, eng.cache_seqlens,
+                                              eng.cu_q, PAGE, eng.batch.max_seqlen,
+                                              cfg.head_dim ** -0.5, model.hkv,
+                                              eng.batch.prefix_groups, out=out)
+
         for _ in range(3):
-            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+            attend()
         a0.record(s)
         for _ in range(reps):
-            ops.paged_attention(q, kc, vc, eng.page_table, eng.cache_seqlens, eng.cu_q, PAGE,
-                                eng.batch.max_seqlen, cfg.head_dim ** -0.5, model.hkv, out=out)
+            attend()
         a1.record(s)
         s.synchronize()
     attn_s = a0.elapsed_time(a1) / 1000.0 / reps

@@ -130,6 +130,37 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
  * reference. */
 int lsb_attention_force_kernel(int32_t mode);
 
+/* Decode attention (one query row per request) where groups of rows share
+ * leading KV pages -- a radix-cache prefix: the reference's cache manager points
+ * every request that matched a prefix at one copy of its pages
+ * (kvcache/radix_cache.py:92-99, 133-147, attention/fa.py:82-93 reads them per
+ * row). Each group's shared keys are read once for all of its rows (QK^T and PV
+ * on the tensor cores, split into partials), each row's own keys by the decode
+ * kernel, which merges both parts by their softmax statistics; the result equals
+ * lsb_paged_attention on the same arguments. Groups in CSR form, int32 device
+ * arrays: group_ptr [num_groups + 1] into group_rows (member row indices; a row
+ * in at most one group), group_prefix [num_groups] (shared keys of the group:
+ * the first group_prefix keys of every member's page table are the same pages,
+ * and no member's context is shorter), row_prefix [rows] (group_prefix of the
+ * row's group, 0 for rows in none; must agree with the groups).
+ * max_group_rows / max_group_prefix bound the groups' sizes. Needs the
+ * streaming decode kernel's layouts (a packed pool, at most 64 query heads):
+ * otherwise LSB_ERR_UNSUPPORTED. Workspace:
+ * lsb_paged_attention_shared_prefix_workspace_size bytes, zeroed once. A call
+ * with no groups is lsb_paged_attention. No counterpart in the reference. */
+int64_t lsb_paged_attention_shared_prefix_workspace_size(int64_t rows, int32_t hq,
+                                                         int32_t head_dim, int64_t max_seqlen,
+                                                         int64_t max_group_prefix);
+int lsb_paged_attention_shared_prefix(
+    void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_cache,
+    const void* v_cache, int64_t slot_stride, int64_t num_slots, const int32_t* page_table,
+    int64_t pt_stride, const int32_t* cache_seqlens, const int32_t* cu_seqlens_q,
+    int64_t num_reqs, int64_t rows, int32_t hq, int32_t hkv, int32_t head_dim,
+    int32_t page_size, int64_t max_seqlen, float scale, const int32_t* group_ptr,
+    const int32_t* group_rows, const int32_t* group_prefix, const int32_t* row_prefix,
+    int64_t num_groups, int64_t max_group_rows, int64_t max_group_prefix, void* workspace,
+    int64_t workspace_bytes, void* stream);
+
 /* lsb_paged_attention for callers that cannot allocate device memory (a plugin
  * whose host framework owns all device memory and passes only inputs and
  * outputs, or a loop that must not pay cudaMalloc's device-wide

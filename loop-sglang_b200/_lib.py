@@ -52,6 +52,11 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                            I32, I32, I32, I32, I64, F, P, I64, P]),
     "lsb_paged_attention_noalloc": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64, P, P,
                                                    I64, I64, I32, I32, I32, I32, I64, F, P]),
+    "lsb_paged_attention_shared_prefix_workspace_size": (c_int64, [I64, I32, I32, I64, I64]),
+    "lsb_paged_attention_shared_prefix": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64,
+                                                         P, P, I64, I64, I32, I32, I32, I32, I64,
+                                                         F, P, P, P, P, I64, I64, I64, P, I64,
+                                                         P]),
     "lsb_gemm_workspace_size": (c_int64, [I64, I64, I64]),
     "lsb_gemm": (ctypes.c_int, [P, I64, P, I64, P, I64, P, I64, I64, I64, I32, P, I64, P]),
     "lsb_gemm_plan": (ctypes.c_int, [I64, I64, I64, P]),
@@ -160,9 +165,14 @@ def launch_count() -> int:
     return _launches
 
 
+# entry points that enqueue more than one kernel per call
+_MULTI_LAUNCH = {"lsb_paged_attention_shared_prefix": 2}
+
+
 def call(name: str, *args) -> None:
-    """Invoke a launching entry point; every such call enqueues exactly one kernel."""
+    """Invoke a launching entry point and count the kernels it enqueues (one, unless listed
+    in ``_MULTI_LAUNCH``)."""
     global _launches
     check(getattr(lib(), name)(*args), name)
     if name not in _NOT_LAUNCHES:
-        _launches += 1
+        _launches += _MULTI_LAUNCH.get(name, 1)

@@ -338,7 +338,8 @@ constexpr int kRowCounterBase = 2;  // counters[0]: next item, [1]: CTAs finishe
 enum : int { kItemFirst = 1, kItemLast = 2, kStreamExit = 4 };
 
 struct StageHdr {
-  int row, split, nsplit, t0, ntok, flags, qbuf, pad;
+  int row, split, nsplit, t0, ntok, flags, qbuf;
+  int pre;  // the row's partials from its group's shared prefix (parts 0 .. pre-1)
   uint64_t valid;  // bit i: key t0 + i has a slot inside the pool
 };
 
@@ -358,6 +359,12 @@ struct StreamParams {
   int chunk, max_splits, stages;
   int sub;              // blocks of stream_tokens(D) keys per stage
   int warps_per_head;   // consumer warps sharing a query head (1 when hq >= 16)
+  int64_t parts;        // partial slots per (row, head)
+  // Shared prefixes (null: none): keys [0, row_prefix[r]) of row r are covered by
+  // ceil(row_prefix[r] / prefix_chunk) partials a kernel launched before this one wrote
+  // (parts 0..); this kernel streams the rest and its merge takes those partials in.
+  const int32_t* row_prefix;
+  int prefix_chunk;
   int64_t max_seqlen;
   float scale_log2;
   Workspace ws;
@@ -476,9 +483,15 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         if (lane == 0 && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SEQLEN);
         kv_len = cap;
       }
-      const int nsplit = kv_len > 0 ? static_cast<int>((kv_len + p.chunk - 1) / p.chunk) : 1;
+      int kb0 = 0, pre = 0;
+      if (p.row_prefix) {
+        kb0 = p.row_prefix[row];
+        if (kb0 > 0) pre = (kb0 + p.prefix_chunk - 1) / p.prefix_chunk;
+      }
+      const int64_t span = kv_len - kb0;
+      const int nsplit = span > 0 ? static_cast<int>((span + p.chunk - 1) / p.chunk) : 1;
       if (split >= nsplit) continue;
-      const int k_begin = split * p.chunk;
+      const int k_begin = kb0 + split * p.chunk;
       const int k_end = static_cast<int>(kv_len < k_begin + p.chunk ? kv_len : k_begin + p.chunk);
       const int p_first = pow2 ? (k_begin >> pshift) : k_begin / p.page_size;
       if (k_end > k_begin) {
@@ -525,6 +538,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         h.ntok = ntok;
         h.flags = (t0 == k_begin ? kItemFirst : 0) | (t0 + T >= k_end ? kItemLast : 0);
         h.qbuf = qb;
+        h.pre = pre;
         if (scatter) {
           int64_t slot[kMaxStageTokens / 32];
           uint64_t valid = 0;
@@ -637,7 +651,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
     const bool dim_ok = c < kVec;
     const int group_base = lane & ~(kLanes - 1);
     const int qpk = p.hq / p.hkv;
-    const int64_t parts = static_cast<int64_t>(p.max_splits) * G;  // partials per (row, head)
+    const int64_t parts = p.parts;  // partial slots per (row, head)
     int heads[HPW];     // this warp's query heads (p.hq: none)
     int head_off[HPW];  // byte offset of the head's KV head and 8-dim vector in a key row
 #pragma unroll
@@ -763,7 +777,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         }
       }
       const bool writer = g == 0 && dim_ok;
-      if (hd.nsplit == 1 && G == 1) {
+      if (hd.nsplit == 1 && G == 1 && hd.pre == 0) {
 #pragma unroll
         for (int j = 0; j < HPW; ++j) {
           const int h = head_of(j);
@@ -777,12 +791,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         }
         continue;
       }
-      const int64_t nparts = static_cast<int64_t>(hd.nsplit) * G;
+      const int64_t nown = static_cast<int64_t>(hd.nsplit) * G;  // this kernel's partials
+      const int64_t nparts = hd.pre + nown;                      // merged with the prefix's
 #pragma unroll
       for (int j = 0; j < HPW; ++j) {
         const int h = head_of(j);
         if (h < p.hq && writer) {
-          const int64_t idx = (row * p.hq + h) * parts + static_cast<int64_t>(hd.split) * G + wsub;
+          const int64_t idx = (row * p.hq + h) * parts + hd.pre + static_cast<int64_t>(hd.split) * G + wsub;
           float4* po = reinterpret_cast<float4*>(p.ws.partial_o + idx * D + 8 * c);
           po[0] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
           po[1] = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
@@ -801,7 +816,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         if (lane == 0) {
           int* counter = p.ws.counters + kRowCounterBase + row * p.hq + h;
           const int prev = atomicAdd(counter, 1);
-          last = prev == nparts - 1;
+          last = prev == nown - 1;
           if (last) *counter = 0;  // every partial has arrived: reset for the next launch
         }
         if (!__shfl_sync(0xffffffffu, last, 0)) continue;
@@ -939,6 +954,112 @@ extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, 
   return bytes;
 }
 
+// The streaming kernel's launch. row_prefix (nullable): per row, the leading keys a kernel
+// launched before this one has covered with ceil(row_prefix / prefix_chunk) partials (at
+// most prefix_parts) in this workspace; this launch streams the rest and merges.
+static int stream_attention(void* out, int64_t out_stride, const void* q, int64_t q_stride,
+                            const void* k_cache, const void* v_cache, int64_t slot_stride,
+                            int64_t num_slots, const int32_t* page_table, int64_t pt_stride,
+                            const int32_t* cache_seqlens, const int32_t* cu_seqlens_q,
+                            int64_t num_reqs, int64_t rows, int32_t hq, int32_t hkv,
+                            int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
+                            const int32_t* row_prefix, int prefix_chunk, int64_t prefix_parts,
+                            void* workspace, int64_t workspace_bytes, void* stream) {
+  const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
+  const int64_t splits = (max_seqlen + chunk - 1) / chunk;
+  LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
+              "paged_attention: max_seqlen too large");
+  const int wph = stream_warps_per_head(hq);
+  const int64_t parts = splits * wph + prefix_parts;  // partial slots per (row, head)
+  const int64_t need = workspace_bytes_for(rows, hq, head_dim, parts);
+  LSB_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+              "paged_attention: workspace of %lld bytes needed", (long long)need);
+  StreamParams sp;
+  sp.out = static_cast<bf16*>(out);
+  sp.out_stride = out_stride;
+  sp.q = static_cast<const bf16*>(q);
+  sp.q_stride = q_stride;
+  sp.k_cache = static_cast<const bf16*>(k_cache);
+  sp.v_cache = static_cast<const bf16*>(v_cache);
+  sp.slot_stride = slot_stride;
+  sp.num_slots = num_slots;
+  sp.page_table = page_table;
+  sp.pt_stride = pt_stride;
+  sp.cache_seqlens = cache_seqlens;
+  sp.cu_seqlens_q = cu_seqlens_q;
+  sp.num_reqs = static_cast<int>(num_reqs);
+  sp.rows = static_cast<int>(rows);
+  sp.hq = hq;
+  sp.hkv = hkv;
+  sp.page_size = page_size;
+  sp.chunk = static_cast<int>(chunk);
+  sp.max_splits = static_cast<int>(splits);
+  sp.max_seqlen = max_seqlen;
+  sp.scale_log2 = scale * kLog2e;
+  sp.ws = carve(workspace, rows, hq, head_dim, parts);
+  sp.parts = parts;
+  sp.row_prefix = row_prefix;
+  sp.prefix_chunk = prefix_chunk;
+  sp.warps_per_head = wph;
+  sp.error_flag = lsb_device_error_flag();
+  // blocks per stage: about 64 KB of K+V per stage, at most 64 keys
+  const int tb = stream_tokens(head_dim);
+  int sub = kStreamStageBudget / (2 * tb * hkv * head_dim * 2);
+  if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
+  if (sub < 1) sub = 1;
+  sp.sub = sub;
+  const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0, sub);
+  int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
+  if (stages > kMaxStreamStages) stages = kMaxStreamStages;
+  LSB_REQUIRE(stages >= 2, "paged_attention: stage of %d bytes too large", probe.stage_bytes);
+  sp.stages = stages;
+  const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages, sub);
+  const int64_t items = rows * splits;
+  const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
+  const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
+  auto launch = [&](auto kernel) -> int {
+    LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  lay.total));
+    kernel<<<grid, kStreamThreads, lay.total, as_stream(stream)>>>(sp);
+    return check_launch("lsb_paged_attention");
+  };
+#define LSB_STREAM_DISPATCH(DIM)                                                  \
+  if (head_dim == DIM) {                                                        \
+    if (hpw == 1) return launch(paged_attention_stream_kernel<DIM, 1>);         \
+    if (hpw == 2) return launch(paged_attention_stream_kernel<DIM, 2>);         \
+    return launch(paged_attention_stream_kernel<DIM, 4>);                       \
+  }
+  LSB_STREAM_DISPATCH(32)
+  LSB_STREAM_DISPATCH(64)
+  LSB_STREAM_DISPATCH(96)
+  LSB_STREAM_DISPATCH(128)
+#undef LSB_STREAM_DISPATCH
+  return fail(LSB_ERR_UNSUPPORTED, "paged_attention: head_dim %d", head_dim);
+}
+
+// Keys per split of a group's shared prefix: enough (group, split, head) CTAs for two per
+// SM, at most 256 keys and at least 64 (one key tile).
+static int prefix_chunk_for(int64_t max_prefix, int64_t num_groups, int64_t max_group_rows,
+                            int32_t hq) {
+  const int64_t row_blocks = (max_group_rows + 63) / 64;
+  int chunk = 256;
+  while (chunk > 64 &&
+         (max_prefix + chunk - 1) / chunk * num_groups * row_blocks * hq < 2 * num_sms_attention())
+    chunk >>= 1;
+  return chunk;
+}
+
+extern "C" int64_t lsb_paged_attention_shared_prefix_workspace_size(int64_t rows, int32_t hq,
+                                                                    int32_t head_dim,
+                                                                    int64_t max_seqlen,
+                                                                    int64_t max_group_prefix) {
+  if (rows <= 0 || hq <= 0 || head_dim <= 0 || max_seqlen <= 0 || max_group_prefix < 0) return 0;
+  const int64_t sc = stream_chunk_for(rows, max_seqlen, head_dim, hq);  // most splits
+  const int64_t parts = (max_seqlen + sc - 1) / sc * stream_warps_per_head(hq) +
+                        (max_group_prefix + 63) / 64;  // the smallest prefix split
+  return workspace_bytes_for(rows, hq, head_dim, parts);
+}
+
 extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
                                    int64_t q_stride, const void* k_cache, const void* v_cache,
                                    int64_t slot_stride, int64_t num_slots,
@@ -987,73 +1108,11 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
     const int64_t max_q = rows < max_seqlen ? rows : max_seqlen;
     return launch_prefill_attention(pp, max_q, head_dim, as_stream(stream));
   }
-  if (use_stream(rows, hq, hkv, head_dim, page_size, slot_stride)) {
-    const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
-    const int64_t splits = (max_seqlen + chunk - 1) / chunk;
-    LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
-                "paged_attention: max_seqlen too large");
-    const int wph = stream_warps_per_head(hq);
-    const int64_t need = workspace_bytes_for(rows, hq, head_dim, splits * wph);
-    LSB_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
-                "paged_attention: workspace of %lld bytes needed", (long long)need);
-    StreamParams sp;
-    sp.out = static_cast<bf16*>(out);
-    sp.out_stride = out_stride;
-    sp.q = static_cast<const bf16*>(q);
-    sp.q_stride = q_stride;
-    sp.k_cache = static_cast<const bf16*>(k_cache);
-    sp.v_cache = static_cast<const bf16*>(v_cache);
-    sp.slot_stride = slot_stride;
-    sp.num_slots = num_slots;
-    sp.page_table = page_table;
-    sp.pt_stride = pt_stride;
-    sp.cache_seqlens = cache_seqlens;
-    sp.cu_seqlens_q = cu_seqlens_q;
-    sp.num_reqs = static_cast<int>(num_reqs);
-    sp.rows = static_cast<int>(rows);
-    sp.hq = hq;
-    sp.hkv = hkv;
-    sp.page_size = page_size;
-    sp.chunk = static_cast<int>(chunk);
-    sp.max_splits = static_cast<int>(splits);
-    sp.max_seqlen = max_seqlen;
-    sp.scale_log2 = scale * kLog2e;
-    sp.ws = carve(workspace, rows, hq, head_dim, splits * wph);
-    sp.warps_per_head = wph;
-    sp.error_flag = lsb_device_error_flag();
-    // blocks per stage: about 64 KB of K+V per stage, at most 64 keys
-    const int tb = stream_tokens(head_dim);
-    int sub = kStreamStageBudget / (2 * tb * hkv * head_dim * 2);
-    if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
-    if (sub < 1) sub = 1;
-    sp.sub = sub;
-    const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0, sub);
-    int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
-    if (stages > kMaxStreamStages) stages = kMaxStreamStages;
-    LSB_REQUIRE(stages >= 2, "paged_attention: stage of %d bytes too large", probe.stage_bytes);
-    sp.stages = stages;
-    const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages, sub);
-    const int64_t items = rows * splits;
-    const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
-    const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
-    auto launch = [&](auto kernel) -> int {
-      LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    lay.total));
-      kernel<<<grid, kStreamThreads, lay.total, as_stream(stream)>>>(sp);
-      return check_launch("lsb_paged_attention");
-    };
-#define LSB_STREAM_DISPATCH(DIM)                                                  \
-    if (head_dim == DIM) {                                                        \
-      if (hpw == 1) return launch(paged_attention_stream_kernel<DIM, 1>);         \
-      if (hpw == 2) return launch(paged_attention_stream_kernel<DIM, 2>);         \
-      return launch(paged_attention_stream_kernel<DIM, 4>);                       \
-    }
-    LSB_STREAM_DISPATCH(32)
-    LSB_STREAM_DISPATCH(64)
-    LSB_STREAM_DISPATCH(96)
-    LSB_STREAM_DISPATCH(128)
-#undef LSB_STREAM_DISPATCH
-  }
+  if (use_stream(rows, hq, hkv, head_dim, page_size, slot_stride))
+    return stream_attention(out, out_stride, q, q_stride, k_cache, v_cache, slot_stride,
+                            num_slots, page_table, pt_stride, cache_seqlens, cu_seqlens_q,
+                            num_reqs, rows, hq, hkv, head_dim, page_size, max_seqlen, scale,
+                            nullptr, 1, 0, workspace, workspace_bytes, stream);
   const int64_t chunk = chunk_for(rows, hq, max_seqlen);
   const int64_t splits = (max_seqlen + chunk - 1) / chunk;
   LSB_REQUIRE(splits <= 65535, "paged_attention: max_seqlen too large");
@@ -1090,4 +1149,80 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
   LSB_CTA_DISPATCH(128)
 #undef LSB_CTA_DISPATCH
   return fail(LSB_ERR_UNSUPPORTED, "paged_attention: head_dim %d", head_dim);
+}
+
+extern "C" int lsb_paged_attention_shared_prefix(
+    void* out, int64_t out_stride, const void* q, int64_t q_stride, const void* k_cache,
+    const void* v_cache, int64_t slot_stride, int64_t num_slots, const int32_t* page_table,
+    int64_t pt_stride, const int32_t* cache_seqlens, const int32_t* cu_seqlens_q,
+    int64_t num_reqs, int64_t rows, int32_t hq, int32_t hkv, int32_t head_dim,
+    int32_t page_size, int64_t max_seqlen, float scale, const int32_t* group_ptr,
+    const int32_t* group_rows, const int32_t* group_prefix, const int32_t* row_prefix,
+    int64_t num_groups, int64_t max_group_rows, int64_t max_group_prefix, void* workspace,
+    int64_t workspace_bytes, void* stream) {
+  if (num_groups <= 0 || max_group_prefix <= 0 || rows <= 0)
+    return lsb_paged_attention(out, out_stride, q, q_stride, k_cache, v_cache, slot_stride,
+                               num_slots, page_table, pt_stride, cache_seqlens, cu_seqlens_q,
+                               num_reqs, rows, hq, hkv, head_dim, page_size, max_seqlen, scale,
+                               workspace, workspace_bytes, stream);
+  LSB_REQUIRE(out && q && k_cache && v_cache && page_table && cache_seqlens && cu_seqlens_q &&
+                  group_ptr && group_rows && group_prefix && row_prefix,
+              "paged_attention_shared_prefix: null pointer");
+  LSB_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 96 || head_dim == 128,
+              "paged_attention_shared_prefix: head_dim %d unsupported", head_dim);
+  LSB_REQUIRE(hq > 0 && hkv > 0 && hq % hkv == 0, "paged_attention_shared_prefix: bad heads");
+  LSB_REQUIRE(page_size > 0 && max_seqlen > 0 && num_reqs > 0 && max_group_rows > 0,
+              "paged_attention_shared_prefix: bad sizes");
+  LSB_REQUIRE(aligned(out, 16) && aligned(q, 16) && aligned(k_cache, 16) && aligned(v_cache, 16),
+              "paged_attention_shared_prefix: tensors must be 16-byte aligned");
+  LSB_REQUIRE(q_stride % 8 == 0 && out_stride % 8 == 0 && slot_stride % 8 == 0 &&
+                  slot_stride >= (int64_t)hkv * head_dim,
+              "paged_attention_shared_prefix: bad strides");
+  if (rows != num_reqs)
+    return fail(LSB_ERR_UNSUPPORTED,
+                "paged_attention_shared_prefix: decode rows only (one query row per request)");
+  if (!use_stream(rows, hq, hkv, head_dim, page_size, slot_stride))
+    return fail(LSB_ERR_UNSUPPORTED,
+                "paged_attention_shared_prefix: needs the streaming decode kernel (packed pool, "
+                "at most %d query heads, %lld counters)",
+                kStreamMaxHeads, (long long)(kCounterCap - kRowCounterBase));
+  LSB_REQUIRE(max_group_prefix <= max_seqlen, "paged_attention_shared_prefix: prefix too long");
+  const int chunk = prefix_chunk_for(max_group_prefix, num_groups, max_group_rows, hq);
+  const int64_t prefix_parts = (max_group_prefix + chunk - 1) / chunk;
+  // the streaming launch checks the workspace; its layout gives the prefix pass's slots
+  const int64_t sc = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
+  const int64_t parts = (max_seqlen + sc - 1) / sc * stream_warps_per_head(hq) + prefix_parts;
+  const int64_t need = workspace_bytes_for(rows, hq, head_dim, parts);
+  LSB_REQUIRE(workspace && workspace_bytes >= need && aligned(workspace, 16),
+              "paged_attention_shared_prefix: workspace of %lld bytes needed", (long long)need);
+  const Workspace ws = carve(workspace, rows, hq, head_dim, parts);
+  GroupPrefixParams gp;
+  gp.q = static_cast<const bf16*>(q);
+  gp.q_stride = q_stride;
+  gp.k_cache = static_cast<const bf16*>(k_cache);
+  gp.v_cache = static_cast<const bf16*>(v_cache);
+  gp.slot_stride = slot_stride;
+  gp.num_slots = num_slots;
+  gp.page_table = page_table;
+  gp.pt_stride = pt_stride;
+  gp.group_ptr = group_ptr;
+  gp.group_rows = group_rows;
+  gp.group_prefix = group_prefix;
+  gp.num_groups = static_cast<int>(num_groups);
+  gp.hq = hq;
+  gp.hkv = hkv;
+  gp.page_size = page_size;
+  gp.prefix_chunk = chunk;
+  gp.scale_log2 = scale * kLog2e;
+  gp.partial_o = ws.partial_o;
+  gp.partial_ml = ws.partial_ml;
+  gp.parts = parts;
+  gp.error_flag = lsb_device_error_flag();
+  if (int rc = launch_group_prefix_attention(gp, max_group_prefix, max_group_rows, head_dim,
+                                             as_stream(stream)))
+    return rc;
+  return stream_attention(out, out_stride, q, q_stride, k_cache, v_cache, slot_stride, num_slots,
+                          page_table, pt_stride, cache_seqlens, cu_seqlens_q, num_reqs, rows, hq,
+                          hkv, head_dim, page_size, max_seqlen, scale, row_prefix, chunk,
+                          prefix_parts, workspace, workspace_bytes, stream);
 }

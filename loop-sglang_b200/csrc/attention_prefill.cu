@@ -82,9 +82,15 @@ __host__ __device__ constexpr int pf_smem_bytes() {
   return (kPfRows + 4 * kPfKeys) * pf_pitch<D>() * 2 + 2 * kPfKeys * 8;
 }
 
-template <int D>
+// GROUP = false: prefill rows (one request's query rows, causal over its keys), output
+// normalised. GROUP = true: decode rows of a shared-prefix group (rows gathered from the
+// member list, keys = one split of the group's prefix, every key visible to every member
+// since the prefix precedes each member's own keys), output as fp32 split partials
+// (unnormalised O, running max and sum, in the decode kernel's log2 domain) into the decode
+// kernel's workspace.
+template <int D, bool GROUP>
 __global__ void __launch_bounds__(kPfWarps * 32, 2)
-    paged_prefill_mma_kernel(PrefillParams p) {
+    paged_prefill_mma_kernel(PrefillParams p, GroupPrefixParams gp) {
   constexpr int P = pf_pitch<D>();
   constexpr int KSTEPS = D / 16;   // k-steps of QK^T
   constexpr int DTILES = D / 8;    // n-tiles of the output
@@ -99,51 +105,82 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q_begin = p.cu_seqlens_q[b];
-  const int q_len = p.cu_seqlens_q[b + 1] - q_begin;
-  const int blk = blockIdx.x;
-  if (blk * kPfRows >= q_len) return;
-  int64_t kv_len = p.cache_seqlens[b];
-  if (kv_len > p.max_seqlen) {
-    if (tid == 0 && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SEQLEN);
-    kv_len = p.max_seqlen;
+  const int blk = GROUP ? 0 : blockIdx.x;
+  // keys [key_base, key_end) of the page table row pt_row; rows_here query rows
+  int64_t key_base = 0, key_end = 0, first_row = 0, pre = 0;
+  int rows_here = 0, member0 = 0;
+  const int32_t* pt_row = nullptr;
+  const bf16* const qbase = GROUP ? gp.q : p.q;
+  const int64_t q_stride = GROUP ? gp.q_stride : p.q_stride;
+  const bf16* const k_cache = GROUP ? gp.k_cache : p.k_cache;
+  const bf16* const v_cache = GROUP ? gp.v_cache : p.v_cache;
+  const int64_t slot_stride = GROUP ? gp.slot_stride : p.slot_stride;
+  const int64_t num_slots = GROUP ? gp.num_slots : p.num_slots;
+  const int page_size = GROUP ? gp.page_size : p.page_size;
+  const int hq = GROUP ? gp.hq : p.hq;
+  const int kvh = h / (hq / (GROUP ? gp.hkv : p.hkv));
+  const float scale_log2 = GROUP ? gp.scale_log2 : p.scale_log2;
+  int* const error_flag = GROUP ? gp.error_flag : p.error_flag;
+  if (GROUP) {
+    const int row_blocks = gridDim.z / gp.num_groups;
+    const int grp = blockIdx.z / row_blocks, rb = blockIdx.z - grp * row_blocks;
+    const int gbeg = gp.group_ptr[grp], gend = gp.group_ptr[grp + 1];
+    member0 = gbeg + rb * kPfRows;
+    rows_here = min(kPfRows, gend - member0);
+    key_base = static_cast<int64_t>(blockIdx.x) * gp.prefix_chunk;
+    const int64_t prefix = gp.group_prefix[grp];
+    if (rows_here <= 0 || key_base >= prefix) return;
+    key_end = key_base + gp.prefix_chunk < prefix ? key_base + gp.prefix_chunk : prefix;
+    pt_row = gp.page_table + static_cast<int64_t>(gp.group_rows[gbeg]) * gp.pt_stride;
+  } else {
+    const int b = blockIdx.z;
+    const int q_begin = p.cu_seqlens_q[b];
+    const int q_len = p.cu_seqlens_q[b + 1] - q_begin;
+    if (blk * kPfRows >= q_len) return;
+    int64_t kv_len = p.cache_seqlens[b];
+    if (kv_len > p.max_seqlen) {
+      if (tid == 0 && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SEQLEN);
+      kv_len = p.max_seqlen;
+    }
+    first_row = q_begin + static_cast<int64_t>(blk) * kPfRows;
+    rows_here = min(kPfRows, q_len - blk * kPfRows);
+    // causal limit of the block's last row (exclusive end of the keys it reads)
+    pre = kv_len - q_len;  // keys before the request's first query row
+    key_end = pre + blk * kPfRows + rows_here;
+    if (key_end > kv_len) key_end = kv_len;
+    if (key_end < 0) key_end = 0;
+    pt_row = p.page_table + static_cast<int64_t>(b) * p.pt_stride;
   }
-  const int kvh = h / (p.hq / p.hkv);
-  const int64_t first_row = q_begin + static_cast<int64_t>(blk) * kPfRows;
-  const int rows_here = min(kPfRows, q_len - blk * kPfRows);
-  // causal limit of the block's last row (exclusive end of the keys it reads)
-  const int64_t pre = kv_len - q_len;  // keys before the request's first query row
-  int64_t key_end = pre + blk * kPfRows + rows_here;
-  if (key_end > kv_len) key_end = kv_len;
-  if (key_end < 0) key_end = 0;
-  const int ntiles = static_cast<int>((key_end + kPfKeys - 1) / kPfKeys);
-  const int32_t* pt_row = p.page_table + static_cast<int64_t>(b) * p.pt_stride;
-  const bool pow2 = (p.page_size & (p.page_size - 1)) == 0;
-  const int pshift = __ffs(p.page_size) - 1;
+  const int ntiles = static_cast<int>((key_end - key_base + kPfKeys - 1) / kPfKeys);
+  const bool pow2 = (page_size & (page_size - 1)) == 0;
+  const int pshift = __ffs(page_size) - 1;
+  // query row of tile row r (r < rows_here)
+  auto q_row = [&](int r) -> int64_t {
+    return GROUP ? static_cast<int64_t>(gp.group_rows[member0 + r]) : first_row + r;
+  };
 
   // ---- Q tile (rows past the request load as zeros) -> shared memory
   for (int i = tid; i < kPfRows * CHUNKS; i += kPfWarps * 32) {
     const int r = i / CHUNKS, c = i - r * CHUNKS;
     const bool ok = r < rows_here;
-    const bf16* src = p.q + (ok ? (first_row + r) * p.q_stride : 0) + static_cast<int64_t>(h) * D + 8 * c;
+    const bf16* src = qbase + (ok ? q_row(r) * q_stride : 0) + static_cast<int64_t>(h) * D + 8 * c;
     cp_async16(sq + r * P + 8 * c, src, ok);
   }
   cp_async_commit();
 
   // ---- K/V tile loader: keys [t0, t0 + 64) into buffer `buf`
   auto load_tile = [&](int tile, int buf) {
-    const int64_t t0 = static_cast<int64_t>(tile) * kPfKeys;
+    const int64_t t0 = key_base + static_cast<int64_t>(tile) * kPfKeys;
     int64_t* slots = s_slot + buf * kPfKeys;
     if (tid < kPfKeys) {
       const int64_t t = t0 + tid;
       int64_t slot = -1;
       if (t < key_end) {
-        const int64_t pg = pow2 ? (t >> pshift) : t / p.page_size;
+        const int64_t pg = pow2 ? (t >> pshift) : t / page_size;
         const int64_t page = pt_row[pg];
-        slot = page * p.page_size + (t - pg * p.page_size);
-        if (slot < 0 || slot >= p.num_slots) {
-          if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+        slot = page * page_size + (t - pg * page_size);
+        if (slot < 0 || slot >= num_slots) {
+          if (error_flag) atomicOr(error_flag, LSB_DEVERR_SLOT);
           slot = -2;  // masked like a key past the context
         }
       }
@@ -156,9 +193,9 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
       const int r = i / CHUNKS, c = i - r * CHUNKS;
       const int64_t slot = slots[r];
       const bool ok = slot >= 0;
-      const int64_t off = (ok ? slot * p.slot_stride : 0) + static_cast<int64_t>(kvh) * D + 8 * c;
-      cp_async16(kd + r * P + 8 * c, p.k_cache + off, ok);
-      cp_async16(vd + r * P + 8 * c, p.v_cache + off, ok);
+      const int64_t off = (ok ? slot * slot_stride : 0) + static_cast<int64_t>(kvh) * D + 8 * c;
+      cp_async16(kd + r * P + 8 * c, k_cache + off, ok);
+      cp_async16(vd + r * P + 8 * c, v_cache + off, ok);
     }
     cp_async_commit();
   };
@@ -185,9 +222,10 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
   for (int j = 0; j < DTILES; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m0 = kPfNegBig, m1 = kPfNegBig, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
   const int g = lane >> 2, t4 = lane & 3;
-  // query rows of this thread within the request, and their causal limits (inclusive)
+  // query rows of this thread within the request, and their causal limits (inclusive);
+  // a group's members see every prefix key
   const int qr0 = blk * kPfRows + warp * 16 + g, qr1 = qr0 + 8;
-  const int64_t lim0 = pre + qr0, lim1 = pre + qr1;
+  const int64_t lim0 = GROUP ? INT64_MAX : pre + qr0, lim1 = GROUP ? INT64_MAX : pre + qr1;
 
   // warps whose 16 rows are all past the request's rows (a decode row's block) only help
   // with the copies
@@ -208,7 +246,7 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
     const bf16* const kb = buf ? sk1 : sk0;
     const bf16* const vb = buf ? sv1 : sv0;
     const int64_t* slots = s_slot + buf * kPfKeys;
-    const int64_t t0 = static_cast<int64_t>(tile) * kPfKeys;
+    const int64_t t0 = key_base + static_cast<int64_t>(tile) * kPfKeys;
 
     // S = Q K^T for 16 rows x 64 keys (8 n-tiles of 8 keys)
     float s[8][4];
@@ -236,8 +274,8 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
         const int kcol = 8 * j + 2 * t4 + e;
         const int64_t key = t0 + kcol;
         const bool live = slots[kcol] >= 0;
-        s[j][e] = (live && key <= lim0) ? s[j][e] * p.scale_log2 : kPfNegBig;
-        s[j][2 + e] = (live && key <= lim1) ? s[j][2 + e] * p.scale_log2 : kPfNegBig;
+        s[j][e] = (live && key <= lim0) ? s[j][e] * scale_log2 : kPfNegBig;
+        s[j][2 + e] = (live && key <= lim1) ? s[j][2 + e] * scale_log2 : kPfNegBig;
         mx0 = fmaxf(mx0, s[j][e]);
         mx1 = fmaxf(mx1, s[j][2 + e]);
       }
@@ -296,8 +334,27 @@ __global__ void __launch_bounds__(kPfWarps * 32, 2)
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
   const int r0 = warp * 16 + g, r1 = r0 + 8;
+  if (GROUP) {
+    // split partials of the members' rows: (O, max, sum) of prefix split blockIdx.x
+    const int64_t part = blockIdx.x;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int r = rr ? r1 : r0;
+      if (r >= rows_here) continue;
+      const int64_t idx = (q_row(r) * hq + h) * gp.parts + part;
+      float* po = gp.partial_o + idx * D;
+#pragma unroll
+      for (int j = 0; j < DTILES; ++j)
+        *reinterpret_cast<float2*>(po + 8 * j + 2 * t4) =
+            make_float2(o[j][2 * rr], o[j][2 * rr + 1]);
+      if (t4 == 0)
+        *reinterpret_cast<float2*>(gp.partial_ml + idx * 2) =
+            make_float2(rr ? m1 : m0, rr ? l1 : l0);
+    }
+    return;
+  }
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
 #pragma unroll
   for (int j = 0; j < DTILES; ++j) {
     const int dim = 8 * j + 2 * t4;
@@ -321,17 +378,42 @@ int launch_prefill_attention(const PrefillParams& p, int64_t max_q_len, int head
               "paged_attention (prefill): grid too large");
   const dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(p.hq),
                   static_cast<unsigned>(p.num_reqs));
+  GroupPrefixParams none{};
   auto launch = [&](auto kernel, int smem) -> int {
     LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kernel<<<grid, kPfWarps * 32, smem, stream>>>(p);
+    kernel<<<grid, kPfWarps * 32, smem, stream>>>(p, none);
     return check_launch("lsb_paged_attention (prefill)");
   };
   switch (head_dim) {
-    case 32: return launch(paged_prefill_mma_kernel<32>, pf_smem_bytes<32>());
-    case 64: return launch(paged_prefill_mma_kernel<64>, pf_smem_bytes<64>());
-    case 96: return launch(paged_prefill_mma_kernel<96>, pf_smem_bytes<96>());
-    case 128: return launch(paged_prefill_mma_kernel<128>, pf_smem_bytes<128>());
+    case 32: return launch(paged_prefill_mma_kernel<32, false>, pf_smem_bytes<32>());
+    case 64: return launch(paged_prefill_mma_kernel<64, false>, pf_smem_bytes<64>());
+    case 96: return launch(paged_prefill_mma_kernel<96, false>, pf_smem_bytes<96>());
+    case 128: return launch(paged_prefill_mma_kernel<128, false>, pf_smem_bytes<128>());
     default: return fail(LSB_ERR_UNSUPPORTED, "paged_attention (prefill): head_dim %d", head_dim);
+  }
+}
+
+int launch_group_prefix_attention(const GroupPrefixParams& gp, int64_t max_prefix,
+                                  int64_t max_group_rows, int head_dim, cudaStream_t stream) {
+  if (gp.num_groups <= 0 || max_prefix <= 0 || max_group_rows <= 0) return LSB_OK;
+  const int64_t splits = (max_prefix + gp.prefix_chunk - 1) / gp.prefix_chunk;
+  const int64_t row_blocks = (max_group_rows + kPfRows - 1) / kPfRows;
+  LSB_REQUIRE(splits < (int64_t(1) << 31) && gp.hq < 65536 && gp.num_groups * row_blocks < 65536,
+              "paged_attention (shared prefix): grid too large");
+  const dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(gp.hq),
+                  static_cast<unsigned>(gp.num_groups * row_blocks));
+  PrefillParams none{};
+  auto launch = [&](auto kernel, int smem) -> int {
+    LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kernel<<<grid, kPfWarps * 32, smem, stream>>>(none, gp);
+    return check_launch("lsb_paged_attention_shared_prefix (prefix)");
+  };
+  switch (head_dim) {
+    case 32: return launch(paged_prefill_mma_kernel<32, true>, pf_smem_bytes<32>());
+    case 64: return launch(paged_prefill_mma_kernel<64, true>, pf_smem_bytes<64>());
+    case 96: return launch(paged_prefill_mma_kernel<96, true>, pf_smem_bytes<96>());
+    case 128: return launch(paged_prefill_mma_kernel<128, true>, pf_smem_bytes<128>());
+    default: return fail(LSB_ERR_UNSUPPORTED, "paged_attention (shared prefix): head_dim %d", head_dim);
   }
 }
 

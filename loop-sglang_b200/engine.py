@@ -19,6 +19,7 @@ import torch
 from . import _lib, ops
 from .kvcache import LastExitedKVCache
 from .model import DeviceBatch, LoopedDecoder
+from .prefix_cache import find_shared_prefixes
 
 
 def align32(n: int) -> int:
@@ -67,6 +68,21 @@ class DecodeEngine:
         """Scheduler inputs of the next step: request rows and lengths (incl. the new token)."""
         self.rpi.copy_(req_rows, non_blocking=True)
         self.seq_lens.copy_(seq_lens, non_blocking=True)
+
+    def share_prefixes(self) -> int:
+        """Find the rows of the current batch whose page tables start with the same pages
+        (requests that matched one radix-cache prefix) and let every attention call read a
+        group's prefix once for all of its rows. Call after ``set_batch`` whenever the batch's
+        rows change, before ``capture``; the groups stay valid while the rows only grow.
+        Returns the number of groups."""
+        ops.set_metadata(self.seq_lens, None, self.req_to_token, self.rpi, self.max_pages,
+                         self.page, True, self.cache_seqlens, self.cu_k, self.cu_q,
+                         self.page_table)
+        groups = find_shared_prefixes(self.page_table.cpu().numpy(),
+                                      self.cache_seqlens.cpu().numpy(), self.page,
+                                      self.model.device)
+        self.batch.prefix_groups = groups
+        return 0 if groups is None else groups.num_groups
 
     # ------------------------------------------------------------------- step --
     def _body(self) -> None:

@@ -121,13 +121,27 @@ def bench_attention(args, ops) -> dict:
                             hkv, out=out)
 
     us = _time_graph(launch, args.reps)
+    extra = {}
+    if sp:
+        # the rows' groups as the engine finds them, each group's prefix read once
+        from loop_sglang_b200.prefix_cache import find_shared_prefixes
+
+        grp = find_shared_prefixes(table.numpy(), ctx.numpy(), page, dev)
+
+        def launch_shared(_i):
+            ops.paged_attention_shared_prefix(q, kv[0], kv[1], table_d, seqlens, cu, page,
+                                              max_seqlen, scale, hkv, grp, out=out)
+
+        extra = {"us_unshared": round(us, 2),
+                 "prefix_groups": 0 if grp is None else grp.num_groups}
+        us = _time_graph(launch_shared, args.reps)
     kv_tokens = int(ctx.sum()) - (rows - min(rows, groups)) * sp * page  # shared pages once
     kv_bytes = kv_tokens * hkv * d * 2 * 2
     nbytes = kv_bytes + rows * hq * d * 2 * 2
     return {"kernel": "paged_attention", "rows": rows, "mean_ctx": float(ctx.float().mean()),
             "heads": hq, "kv_heads": hkv, "head_dim": d, "page_size": page,
             "kv_layer_bytes": slots * hkv * d * 2 * 2, "algorithmic_bytes": nbytes,
-            "shared_prefix": sp * page, "groups": groups,
+            "shared_prefix": sp * page, "groups": groups, **extra,
             "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
             "per_row_GBps": round((int(ctx.sum()) * hkv * d * 4 + rows * hq * d * 4) / us / 1e3, 1)}
 

@@ -118,6 +118,9 @@ class DeviceBatch:
     fixed_page_table: torch.Tensor | None = None
     fixed_out_loc: torch.Tensor | None = None
     last_indices: torch.Tensor | None = field(default=None)  # int64 [B] for prefill LM head
+    # decode rows whose page tables start with the same pages (prefix_cache.SharedPrefixGroups):
+    # attention reads each group's shared prefix once for all of its rows
+    prefix_groups: object | None = None
 
     @property
     def size(self) -> int:
@@ -321,8 +324,13 @@ class LoopedDecoder:
         ops.rope_store_kv(qkv, batch.positions, self.cos_sin, self.hq, self.hkv, c.head_dim,
                           kc, vc, out_loc)
         q = qkv[:, : self.hq * c.head_dim].view(-1, self.hq, c.head_dim)
-        o = ops.paged_attention(q, kc, vc, table, batch.cache_seqlens, batch.cu_seqlens_q, page,
-                                batch.max_seqlen, self.scale, self.hkv)
+        if batch.prefix_groups is not None and not batch.is_prefill and table is batch.page_table:
+            o = ops.paged_attention_shared_prefix(q, kc, vc, table, batch.cache_seqlens,
+                                                  batch.cu_seqlens_q, page, batch.max_seqlen,
+                                                  self.scale, self.hkv, batch.prefix_groups)
+        else:
+            o = ops.paged_attention(q, kc, vc, table, batch.cache_seqlens, batch.cu_seqlens_q,
+                                    page, batch.max_seqlen, self.scale, self.hkv)
         return self._row_parallel(o.view(-1, self.hq * c.head_dim), lw.o)
 
     def _mlp(self, lw: _Layer, x: torch.Tensor) -> torch.Tensor:

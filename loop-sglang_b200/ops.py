@@ -201,6 +201,45 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     return out
 
 
+def paged_attention_shared_prefix(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                                  page_table: torch.Tensor, cache_seqlens: torch.Tensor,
+                                  cu_seqlens_q: torch.Tensor, page_size: int, max_seqlen: int,
+                                  scale: float, hkv: int, groups,
+                                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """``paged_attention`` for decode rows of which groups share leading KV pages
+    (``prefix_cache.SharedPrefixGroups``): each group's shared keys are read once for all of
+    its rows. Same result as ``paged_attention`` on the same arguments."""
+    if groups is None:
+        return paged_attention(q, k_cache, v_cache, page_table, cache_seqlens, cu_seqlens_q,
+                               page_size, max_seqlen, scale, hkv, out)
+    rows, hq, d = q.shape
+    _need(q, BF16, "q", contiguous=False)
+    if q.stride(2) != 1 or q.stride(1) != d:
+        raise ValueError("q heads must be contiguous within a row")
+    for t, n in ((page_table, "page_table"), (cache_seqlens, "cache_seqlens"),
+                 (cu_seqlens_q, "cu_seqlens_q"), (groups.group_ptr, "group_ptr"),
+                 (groups.group_rows, "group_rows"), (groups.group_prefix, "group_prefix"),
+                 (groups.row_prefix, "row_prefix")):
+        _need(t, torch.int32, n, contiguous=(n != "page_table"))
+    if page_table.stride(1) != 1:
+        raise ValueError("page_table must have unit column stride")
+    if groups.row_prefix.numel() != rows:
+        raise ValueError("row_prefix must have one entry per row")
+    out = torch.empty(rows, hq, d, dtype=BF16, device=q.device) if out is None else out
+    nbytes = max(lib().lsb_paged_attention_workspace_size(rows, hq, d, max_seqlen),
+                 lib().lsb_paged_attention_shared_prefix_workspace_size(
+                     rows, hq, d, max_seqlen, groups.max_group_prefix))
+    ws = Workspace.get("attention", nbytes, q.device)
+    call("lsb_paged_attention_shared_prefix", out.data_ptr(), out.stride(0), q.data_ptr(),
+         q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0),
+         k_cache.shape[0], page_table.data_ptr(), page_table.stride(0), cache_seqlens.data_ptr(),
+         cu_seqlens_q.data_ptr(), cache_seqlens.numel(), rows, hq, hkv, d, page_size,
+         max_seqlen, scale, groups.group_ptr.data_ptr(), groups.group_rows.data_ptr(),
+         groups.group_prefix.data_ptr(), groups.row_prefix.data_ptr(), groups.num_groups,
+         groups.max_group_rows, groups.max_group_prefix, _p(ws), ws.numel(), _stream())
+    return out
+
+
 # ------------------------------------------------------------------- GEMM --
 
 def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,

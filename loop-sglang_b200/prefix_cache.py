@@ -216,3 +216,81 @@ def create_prefix_cache(device: torch.device | str, disable_radix_cache: bool = 
     if disable_radix_cache:
         return NoPrefixCache(device=device)
     return RadixPrefixCache(device=device, page_size=page_size)
+
+
+# ------------------------------------------------------- shared-prefix groups --
+
+@dataclass
+class SharedPrefixGroups:
+    """Decode rows grouped by the leading KV pages they share, in the CSR form
+    ``lsb_paged_attention_shared_prefix`` reads (int32 device tensors).
+
+    ``group_rows[group_ptr[g]:group_ptr[g + 1]]`` are group g's member rows, whose first
+    ``group_prefix[g]`` keys are the same pages; ``row_prefix[r]`` is the prefix of row r's
+    group (0 for rows in none).
+    """
+
+    group_ptr: torch.Tensor
+    group_rows: torch.Tensor
+    group_prefix: torch.Tensor
+    row_prefix: torch.Tensor
+    max_group_rows: int
+    max_group_prefix: int
+
+    @property
+    def num_groups(self) -> int:
+        return self.group_ptr.numel() - 1
+
+
+def find_shared_prefixes(page_table: np.ndarray, seq_lens: np.ndarray, page_size: int,
+                         device: torch.device | str, min_pages: int = 1,
+                         max_rows: int = 64) -> SharedPrefixGroups | None:
+    """Groups of decode rows whose page tables start with the same pages.
+
+    What the radix cache gives requests that matched one prefix
+    (kvcache/radix_cache.py:92-99, 133-147): the same page ids at the start of their
+    tables. Rows are keyed by their first page; a group's prefix is the run of whole pages
+    every member has in common, kept inside each member's context minus its last key (so
+    each row keeps keys of its own). Groups of one row or with fewer than ``min_pages``
+    shared pages are dropped, and groups of more than ``max_rows`` rows are cut into groups
+    of at most ``max_rows`` over the same prefix. Host arrays in (taken when a batch is
+    formed: a group stays valid while its rows only grow); None when nothing is shared.
+    """
+    page_table = np.asarray(page_table)
+    seq_lens = np.asarray(seq_lens, dtype=np.int64)
+    rows = page_table.shape[0]
+    whole = (seq_lens - 1) // page_size  # whole pages strictly before each row's last key
+    cand = np.flatnonzero(whole >= max(1, min_pages))
+    if cand.size < 2:
+        return None
+    first = page_table[cand, 0]
+    order = np.argsort(first, kind="stable")
+    cand, first = cand[order], first[order]
+    bounds = np.flatnonzero(np.diff(first)) + 1
+    ptr, members, prefix = [0], [], []
+    row_prefix = np.zeros(rows, np.int32)
+    for rs in np.split(cand, bounds):
+        if rs.size < 2:
+            continue
+        limit = int(whole[rs].min())
+        block = page_table[rs, :limit]
+        same = np.all(block == block[0], axis=0)  # pages common to every member
+        common = limit if same.all() else int(np.argmin(same))
+        if common < min_pages:
+            continue
+        for i in range(0, rs.size, max_rows):
+            part = rs[i:i + max_rows]
+            if part.size < 2:  # a lone remainder reads its prefix itself
+                continue
+            members.extend(part.tolist())
+            ptr.append(len(members))
+            prefix.append(common * page_size)
+            row_prefix[part] = common * page_size
+    if not prefix:
+        return None
+    sizes = np.diff(np.asarray(ptr))
+    dev = torch.device(device)
+    as_i32 = lambda a: torch.as_tensor(np.asarray(a, np.int32), device=dev)  # noqa: E731
+    return SharedPrefixGroups(group_ptr=as_i32(ptr), group_rows=as_i32(members),
+                              group_prefix=as_i32(prefix), row_prefix=as_i32(row_prefix),
+                              max_group_rows=int(sizes.max()), max_group_prefix=int(max(prefix)))
