@@ -220,6 +220,22 @@ int lsb_gemm_force_plan(int32_t mode);
  * multiple of 16 in 16..256), for the same benchmarks and tuning. */
 int lsb_gemm_force_tile_tokens(int32_t tokens);
 
+/* The attention's QKV projection with its RoPE and KV store fused into the GEMM
+ * epilogue: qkv[M, N] = x . w^T (N = (hq + 2 hkv) x head_dim, bf16, rounded as
+ * lsb_gemm rounds), then neox RoPE on the q and k heads exactly as
+ * lsb_rope_store_kv applies it to that output, the rotated k heads and the v
+ * heads also stored into slot out_loc[t] of k_cache / v_cache (slot 0 skipped,
+ * slots outside [0, num_slots) and positions outside [0, max_pos) flagged). qkv
+ * ends with the same contents as lsb_gemm followed by lsb_rope_store_kv. One
+ * launch instead of two. head_dim 128 only (one head per 128-row weight tile;
+ * otherwise LSB_ERR_UNSUPPORTED); no bias.  Replaces models/utils.py:119-131 (the
+ * qkv F.linear) with layers/attention.py:88-90 (RoPE, store_kv). */
+int lsb_gemm_rope_store(void* qkv, int64_t ldq, const void* x, int64_t ldx, const void* w,
+                        int64_t ldw, int64_t M, int64_t N, int64_t K, const int32_t* positions,
+                        const float* cos_sin, int64_t max_pos, void* k_cache, void* v_cache,
+                        int64_t slot_stride, int64_t num_slots, const int32_t* out_loc,
+                        int32_t hq, int32_t hkv, int32_t head_dim, void* stream);
+
 /* y[M, N] = [x1 | x2] . w^T (+ bias) with w [N, K1 + K2]: the product over the
  * concatenation of two activation tensors along K without materialising it (the
  * K loop reads x1 and w's first K1 columns, then x2 and the last K2). Replaces
@@ -442,6 +458,15 @@ int lsb_ipc_close(void* ptr);
 int lsb_comm_create(int32_t rank, int32_t world, void* const* buffers, int64_t max_elems,
                     lsb_comm** comm);
 int lsb_comm_destroy(lsb_comm* comm);
+/* All-reduce protocol of later calls on this communicator (every rank must choose the
+ * same): 0 automatic (one hop for two ranks, else two), 1 one hop -- every rank stores its
+ * partial into every rank's buffer and sums all of them itself (at most 4 ranks; the
+ * same bits on every rank), 2 two hops -- partials to the owner of each region, sums
+ * back from it ((world - 1) / world of the bytes each way). The protocols use the
+ * buffers differently: every rank's earlier calls must have completed (device
+ * synchronise + a host barrier) before any rank's first call under the new one.
+ * No counterpart in the reference (its NCCL picks the algorithm). */
+int lsb_comm_set_protocol(lsb_comm* comm, int32_t mode);
 
 /* In-place sum of x[rows, cols] (row stride ld) over the ranks: the reference's
  * DistributedCommunicator.all_reduce (distributed/impl.py:63-67), used for the

@@ -62,6 +62,9 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_gemm_plan": (ctypes.c_int, [I64, I64, I64, P]),
     "lsb_gemm_argmax_tiles": (I64, [I64]),
     "lsb_gemm_force_plan": (ctypes.c_int, [I32]),
+    "lsb_gemm_rope_store": (ctypes.c_int, [P, I64, P, I64, P, I64, I64, I64, I64, P, P, I64, P,
+                                           P, I64, I64, P, I32, I32, I32, P]),
+    "lsb_comm_set_protocol": (ctypes.c_int, [P, I32]),
     "lsb_gemm_force_tile_tokens": (ctypes.c_int, [I32]),
     "lsb_attention_force_kernel": (ctypes.c_int, [I32]),
     "lsb_gemm_argmax": (ctypes.c_int, [P, I64, P, I64, P, I64, I64, I64, I64, P]),
@@ -154,7 +157,7 @@ _NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "ls
                  "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy",
                  "lsb_gemm_plan", "lsb_gemm_argmax_tiles", "lsb_gemm_force_plan",
                  "lsb_gemm_force_tile_tokens",
-                 "lsb_attention_force_kernel",
+                 "lsb_attention_force_kernel", "lsb_comm_set_protocol",
                  "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
                  "lsb_radix_insert", "lsb_radix_lock", "lsb_radix_indices", "lsb_radix_evict",
                  "lsb_radix_size_info", "lsb_radix_check"}

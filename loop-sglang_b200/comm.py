@@ -76,6 +76,15 @@ class B200Communicator:
     def _stream() -> int:
         return torch.cuda.current_stream().cuda_stream
 
+    def set_protocol(self, mode: int) -> None:
+        """All-reduce protocol of later calls (collective: every rank sets the same): 0
+        automatic (one hop for two ranks), 1 one hop (at most 4 ranks), 2 two hops via region
+        owners. The protocols use the buffers differently, so every rank first finishes its
+        calls in flight (device synchronise + barrier)."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self._group)
+        self._call("lsb_comm_set_protocol", self._comm, int(mode))
+
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         """In-place bf16 sum over the ranks (rows of the last dimension)."""
         if x.dtype != torch.bfloat16 or x.dim() < 1 or x.stride(-1) != 1:

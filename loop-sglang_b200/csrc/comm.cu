@@ -22,9 +22,9 @@ __global__ void __launch_bounds__(kCommThreads)
   const int r1 = r0 + row_tile < rows ? r0 + row_tile : rows;
   const int owner = region % c.world;
   const uint32_t epoch = comm_epoch(c, kOpAllReduce);
-  // this rank's partial of the region -> the owner's recv slot (tagged words)
+  // this rank's partial of the region -> the owner's recv slot (tagged words), or every
+  // rank's (one-shot)
   const int quads = (w + 3) >> 2;
-  uint64_t* dst = c.recv(owner, c.rank);
   for (int idx = t; idx < (r1 - r0) * quads; idx += kCommThreads) {
     const int m = r0 + idx / quads;
     const int col = c0 + 4 * (idx % quads);
@@ -33,7 +33,7 @@ __global__ void __launch_bounds__(kCommThreads)
     bf16 v[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[e] = __float2bfloat16_rn(f[e]);
-    tag_put4(dst, static_cast<int64_t>(m) * cols + col, v, epoch);
+    comm_put4(c, owner, epoch, static_cast<int64_t>(m) * cols + col, v);
   }
   comm_complete(c, owner, epoch, x, ld, r0, r1, c0, w, cols, t, kCommThreads, err);
   __syncthreads();
@@ -140,10 +140,19 @@ extern "C" int lsb_comm_create(int32_t rank, int32_t world, void* const* buffers
   c->dev.rank = rank;
   c->dev.world = world;
   c->dev.max_elems = max_elems;
+  c->dev.oneshot = world == 2;  // one hop for two ranks (the same bytes, half the latency)
   for (int r = 0; r < kCommMaxWorld; ++r)
     c->dev.base[r] = r < world ? static_cast<uint8_t*>(buffers[r]) : nullptr;
   cudaGetDevice(&c->device);
   *out = c;
+  return LSB_OK;
+}
+
+extern "C" int lsb_comm_set_protocol(lsb_comm* comm, int32_t mode) {
+  LSB_REQUIRE(comm && mode >= 0 && mode <= 2, "comm_set_protocol: bad arguments");
+  LSB_REQUIRE(mode != 1 || comm->dev.world <= kOneShotMaxWorld,
+              "comm_set_protocol: one-shot takes at most %d ranks", kOneShotMaxWorld);
+  comm->dev.oneshot = mode == 0 ? comm->dev.world == 2 : mode == 1;
   return LSB_OK;
 }
 

@@ -14,8 +14,15 @@
 // needs that peer's words of the next call to finish it), and the epoch that every
 // rank advances once per call (the last CTA to finish stores it) tells the calls
 // apart: one epoch counter serves every operation, so tags of different operations
-// never coincide. The all-gather keeps per-region flags (release/acquire at system
-// scope). Every wait is bounded and reports LSB_DEVERR_COMM_TIMEOUT instead of hanging.
+// never coincide.
+// With up to four ranks the all-reduce can instead take one hop ("one-shot"): every
+// rank stores its partial as tagged words into its own slot on every rank, and every
+// rank sums all ranks' words of the region in rank order itself (identical bits
+// everywhere). The slots alternate with the epoch's parity (recv slots 4p .. 4p + 3):
+// a rank that finished call k has every peer's partials of call k, so every peer has
+// finished call k - 1 and no longer reads the slots call k + 1 writes.
+// The all-gather keeps per-region flags (release/acquire at system scope). Every wait is
+// bounded and reports LSB_DEVERR_COMM_TIMEOUT instead of hanging.
 #pragma once
 
 #include "common.cuh"
@@ -36,8 +43,11 @@ constexpr int64_t kCommDoneBytes = static_cast<int64_t>(kCommMaxRegions) * sizeo
 constexpr int64_t kCommOpBytes = kCommFlagBytes + kCommDoneBytes;
 constexpr int64_t kCommDataOff = kCommFlagsOff + kCommOps * kCommOpBytes;
 
+constexpr int kOneShotMaxWorld = 4;
+
 struct CommDev {
   int rank, world;
+  int oneshot;        // all-reduce in one hop (world <= kOneShotMaxWorld), else via owners
   int64_t max_elems;  // bf16 elements of one recv slot / the result area / one gather slot
   uint8_t* base[kCommMaxWorld];
 
@@ -55,6 +65,10 @@ struct CommDev {
   // word per element pair of a [rows, cols] output
   __device__ __forceinline__ uint64_t* recv(int r, int src) const {
     return reinterpret_cast<uint64_t*>(base[r] + kCommDataOff) + static_cast<int64_t>(src) * (max_elems / 2);
+  }
+  // one-shot slot of source `src` on rank r for calls of epoch parity `par`
+  __device__ __forceinline__ uint64_t* oneshot_slot(int r, int src, uint32_t par) const {
+    return recv(r, kOneShotMaxWorld * static_cast<int>(par & 1u) + src);
   }
   __device__ __forceinline__ uint64_t* result(int r) const {
     return reinterpret_cast<uint64_t*>(base[r] + kCommDataOff) +
@@ -203,6 +217,18 @@ __device__ __forceinline__ bool tag_get4(const uint64_t* words, int64_t e, uint3
   return true;
 }
 
+// First half of the all-reduce: this rank's partial of four elements (element offset e
+// of the [rows, ncols] output) to the owner of their region, or with one-shot to every
+// rank.
+__device__ __forceinline__ void comm_put4(const CommDev& c, int owner, uint32_t epoch, int64_t e,
+                                          const bf16 v[4]) {
+  if (c.oneshot) {
+    for (int r = 0; r < c.world; ++r) tag_put4(c.oneshot_slot(r, c.rank, epoch), e, v, epoch);
+  } else {
+    tag_put4(c.recv(owner, c.rank), e, v, epoch);
+  }
+}
+
 // Second half of the all-reduce for one region (rows [r0, r1) x columns [c0, c0 + w)
 // of an output with `ncols` columns, a multiple of 4, and row stride `ld`), after this
 // CTA has stored its partial of the region as tagged words into the owner's recv slot
@@ -218,7 +244,17 @@ __device__ __forceinline__ void comm_complete(const CommDev& c, int owner, uint3
     const int col = c0 + 4 * (idx % quads);
     const int64_t e = static_cast<int64_t>(m) * ncols + col;
     bf16 v[4];
-    if (me == owner) {
+    if (c.oneshot) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < W; ++s) {  // rank order: every rank gets the same bits
+        float f[4] = {0.f, 0.f, 0.f, 0.f};
+        tag_get4(c.oneshot_slot(me, s, epoch), e, epoch, f, err);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k] += f[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v[k] = __float2bfloat16_rn(acc[k]);
+    } else if (me == owner) {
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (int s = 0; s < W; ++s) {  // rank order: every rank gets the same bits
         float f[4] = {0.f, 0.f, 0.f, 0.f};

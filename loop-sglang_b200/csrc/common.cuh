@@ -115,6 +115,15 @@ __device__ __forceinline__ bf16x8 pack8(const float* f) {
   return v;
 }
 
+// Neox rotation of one pair (x1 at dim i, x2 at dim i + D/2) by the angle with cosine c
+// and sine s, in fp32 with every product and sum rounded on its own (no fused
+// multiply-add), so every kernel that rotates gets the same bits.
+__device__ __forceinline__ void rope_rotate(float x1, float x2, float c, float s, float& y1,
+                                            float& y2) {
+  y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
 __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }

@@ -58,6 +58,22 @@ constexpr int kFlagNoRotate = 1, kFlagCacheHints = 2, kFlagSleepWait = 4;
 // Internal epilogue of the LM head: per row and 128-entry vocabulary tile, the largest
 // bf16-rounded logit and its index (greedy sampling without writing the logits).
 constexpr int kEpiArgmax = 4;
+// Internal epilogue of the attention's QKV projection with 128-dim heads (one head per
+// 128-column tile): neox RoPE on the q and k heads, and the rotated k and the v heads
+// stored into their paged KV slots as well as into the output.
+constexpr int kEpiRope = 5;
+constexpr int kEpiKinds = 6;
+
+struct RopeParams {
+  const int32_t* positions;
+  const float* cos_sin;  // [max_pos, 128] = cat(cos, sin)
+  int64_t max_pos;
+  bf16* k_cache;
+  bf16* v_cache;
+  int64_t slot_stride, num_slots;
+  const int32_t* out_loc;
+  int hq, hkv;
+};
 
 struct ArgmaxPair {
   float value;
@@ -80,6 +96,7 @@ struct GemmParams {
   uint32_t idesc;
   int* error_flag;
   CommDev comm;  // row-parallel all-reduce (AR variants only)
+  RopeParams rope;  // kEpiRope only
 };
 
 // L2 policy hints for the TMA loads (createpolicy): the weights are streamed once
@@ -416,7 +433,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     // Specialised at compile time (epilogue kind, one tile or a cluster): a generic
     // loop with runtime branches compiles to a several times slower sequence.
     constexpr bool kSwiglu = EPI == LSB_EPI_SWIGLU;
-    constexpr int kQuadShift = kSwiglu ? 4 : 5;  // 16 or 32 quads per token row
+    // SwiGLU pairs weight row r with r + 64 (gate, up); RoPE dim i with i + 64
+    constexpr bool kPair = kSwiglu || EPI == kEpiRope;
+    constexpr int kQuadShift = kPair ? 4 : 5;  // 16 or 32 quads per token row
     bf16* const y = p.y;
     const int64_t ldy = p.ldy;
     const int ncols = kSwiglu ? p.N / 2 : p.N;
@@ -429,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       asm volatile("griddepcontrol.wait;" ::: "memory");
       ar_epoch = comm_epoch(p.comm, kOpGemmAllReduce);
     }
-    constexpr int kU = kSwiglu ? 2 : 4;  // quads per thread and pass
+    constexpr int kU = kPair ? 2 : 4;  // quads per thread and pass
     const int src_stride = per * kBM;    // floats between two sources' partials
     for (int base = t; base < count; base += kThreads * kU) {
       float4 acc[kU], accu[kU];
@@ -449,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             if (idx < count) {
               const float4 v = *reinterpret_cast<const float4*>(red + off);
               acc[u2].x += v.x; acc[u2].y += v.y; acc[u2].z += v.z; acc[u2].w += v.w;
-              if (kSwiglu) {
+              if (kPair) {
                 const float4 g = *reinterpret_cast<const float4*>(red + off + 64);
                 accu[u2].x += g.x; accu[u2].y += g.y; accu[u2].z += g.z; accu[u2].w += g.w;
               }
@@ -469,6 +488,56 @@ __global__ void __launch_bounds__(kThreads, 2)
         store4(y, ldy, m0 + m, tile_n * 64 + 4 * qi, ncols,
                silu_mul(round_bf16(a.x), round_bf16(u.x)), silu_mul(round_bf16(a.y), round_bf16(u.y)),
                silu_mul(round_bf16(a.z), round_bf16(u.z)), silu_mul(round_bf16(a.w), round_bf16(u.w)));
+      } else if (EPI == kEpiRope) {
+        // the projection is rounded to bf16 first (the reference's F.linear output), then
+        // rotated in fp32 and rounded once (layers/attention.py:88-90 on that output)
+        const RopeParams& rp = p.rope;
+        const int64_t tok = m0 + m;
+        const int head = tile_n;  // 128-dim heads: q 0..hq-1, k hq.., v hq+hkv..
+        float x1[4] = {round_bf16(a.x), round_bf16(a.y), round_bf16(a.z), round_bf16(a.w)};
+        float x2[4] = {round_bf16(u.x), round_bf16(u.y), round_bf16(u.z), round_bf16(u.w)};
+        if (head < rp.hq + rp.hkv) {
+          int pos = rp.positions[tok];
+          if (pos < 0 || pos >= rp.max_pos) {
+            if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_POSITION);
+            pos = 0;
+          }
+          const float* cs = rp.cos_sin + static_cast<int64_t>(pos) * 128 + 4 * qi;
+          const float4 c = *reinterpret_cast<const float4*>(cs);
+          const float4 sn = *reinterpret_cast<const float4*>(cs + 64);
+          const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float r1, r2;
+            rope_rotate(x1[e], x2[e], cc[e], ss[e], r1, r2);
+            x1[e] = r1;
+            x2[e] = r2;
+          }
+        }
+        store4(y, ldy, tok, n0 + 4 * qi, ncols, x1[0], x1[1], x1[2], x1[3]);
+        store4(y, ldy, tok, n0 + 64 + 4 * qi, ncols, x2[0], x2[1], x2[2], x2[3]);
+        if (head >= rp.hq) {  // k and v heads: their slot too (slot 0 is padding)
+          const int64_t loc = rp.out_loc[tok];
+          if (loc != 0) {
+            if (loc < 0 || loc >= rp.num_slots) {
+              if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+            } else {
+              const bool is_k = head < rp.hq + rp.hkv;
+              const int kvh = is_k ? head - rp.hq : head - rp.hq - rp.hkv;
+              bf16* dst = (is_k ? rp.k_cache : rp.v_cache) + loc * rp.slot_stride +
+                          static_cast<int64_t>(kvh) * 128 + 4 * qi;
+              const bf162 p0 = __floats2bfloat162_rn(x1[0], x1[1]), p1 = __floats2bfloat162_rn(x1[2], x1[3]);
+              const bf162 p2 = __floats2bfloat162_rn(x2[0], x2[1]), p3 = __floats2bfloat162_rn(x2[2], x2[3]);
+              uint2 lo, hi;
+              lo.x = *reinterpret_cast<const uint32_t*>(&p0);
+              lo.y = *reinterpret_cast<const uint32_t*>(&p1);
+              hi.x = *reinterpret_cast<const uint32_t*>(&p2);
+              hi.y = *reinterpret_cast<const uint32_t*>(&p3);
+              *reinterpret_cast<uint2*>(dst) = lo;
+              *reinterpret_cast<uint2*>(dst + 64) = hi;
+            }
+          }
+        }
       } else {
         const int col = n0 + 4 * qi;
         float o0 = a.x, o1 = a.y, o2 = a.z, o3 = a.w;
@@ -513,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           // goes to the tile owner's recv slot as tagged words, rows of N elements
           const bf16 v4[4] = {__float2bfloat16_rn(o0), __float2bfloat16_rn(o1),
                               __float2bfloat16_rn(o2), __float2bfloat16_rn(o3)};
-          tag_put4(p.comm.recv(tile_n % p.comm.world, p.comm.rank),
-                   static_cast<int64_t>(m0 + m) * p.N + col, v4, ar_epoch);
+          comm_put4(p.comm, tile_n % p.comm.world, ar_epoch,
+                    static_cast<int64_t>(m0 + m) * p.N + col, v4);
         } else {
           store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
         }
@@ -608,15 +677,15 @@ using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                         const CUtensorMap, GemmParams);
 
 Kernel kernel_for(bool cluster, int epilogue, bool ar = false) {
-  static const Kernel kernels[2][5] = {
+  static const Kernel kernels[2][kEpiKinds] = {
       {gemm_tcgen05_kernel<LSB_EPI_NONE, false, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, false>,
        gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false, false>,
        gemm_tcgen05_kernel<LSB_EPI_SWIGLU, false, false>,
-       gemm_tcgen05_kernel<kEpiArgmax, false, false>},
+       gemm_tcgen05_kernel<kEpiArgmax, false, false>, gemm_tcgen05_kernel<kEpiRope, false, false>},
       {gemm_tcgen05_kernel<LSB_EPI_NONE, true, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, false>,
        gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true, false>,
        gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true, false>,
-       gemm_tcgen05_kernel<kEpiArgmax, true, false>}};
+       gemm_tcgen05_kernel<kEpiArgmax, true, false>, gemm_tcgen05_kernel<kEpiRope, true, false>}};
   static const Kernel ar_kernels[2][2] = {
       {gemm_tcgen05_kernel<LSB_EPI_NONE, false, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, true>},
       {gemm_tcgen05_kernel<LSB_EPI_NONE, true, true>, gemm_tcgen05_kernel<LSB_EPI_BIAS, true, true>}};
@@ -876,7 +945,7 @@ struct Segment2 {
 static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w,
                      int64_t ldw, const void* bias, int64_t M, int64_t N, int64_t K,
                      int32_t epilogue, const lsb_comm* comm, void* stream,
-                     const Segment2* seg2 = nullptr) {
+                     const Segment2* seg2 = nullptr, const RopeParams* rope = nullptr) {
   LSB_REQUIRE(y && x && w, "gemm: null pointer");
   LSB_REQUIRE(N > 0 && K > 0, "gemm: empty N or K (N=%lld K=%lld)", (long long)N, (long long)K);
   const int64_t K2 = seg2 ? seg2->K2 : 0;
@@ -899,9 +968,10 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   LSB_REQUIRE(K + K2 < (int64_t(1) << 31), "gemm: dimension too large");
   LSB_REQUIRE(aligned(x, 16) && aligned(w, 16) && aligned(y, 2),
               "gemm: x and w must be 16-byte aligned");
-  LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue <= kEpiArgmax, "gemm: bad epilogue");
+  LSB_REQUIRE(epilogue >= LSB_EPI_NONE && epilogue < kEpiKinds, "gemm: bad epilogue");
+  LSB_REQUIRE((epilogue == kEpiRope) == (rope != nullptr), "gemm: rope parameters mismatch");
   LSB_REQUIRE(epilogue == LSB_EPI_NONE || epilogue == LSB_EPI_SWIGLU || epilogue == kEpiArgmax ||
-                  bias,
+                  epilogue == kEpiRope || bias,
               "gemm: bias required");
   // the argmax epilogue writes one (value, index) pair per row and 128-column tile
   const int64_t out_cols = epilogue == LSB_EPI_SWIGLU ? N / 2
@@ -943,6 +1013,8 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   p.flags = g_force_plan.load(std::memory_order_relaxed) >> 4;
   p.idesc = make_idesc(bh);
   p.error_flag = lsb_device_error_flag();
+  if (rope) p.rope = *rope;
+  else memset(&p.rope, 0, sizeof(p.rope));
   const bool ar = comm != nullptr;
   if (ar) {
     p.comm = comm->dev;
@@ -987,6 +1059,39 @@ extern "C" int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const 
   (void)workspace;
   (void)workspace_bytes;
   return gemm_impl(y, ldy, x, ldx, w, ldw, bias, M, N, K, epilogue, nullptr, stream);
+}
+
+extern "C" int lsb_gemm_rope_store(void* qkv, int64_t ldq, const void* x, int64_t ldx,
+                                   const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                                   const int32_t* positions, const float* cos_sin,
+                                   int64_t max_pos, void* k_cache, void* v_cache,
+                                   int64_t slot_stride, int64_t num_slots,
+                                   const int32_t* out_loc, int32_t hq, int32_t hkv,
+                                   int32_t head_dim, void* stream) {
+  LSB_REQUIRE(positions && cos_sin && k_cache && v_cache && out_loc,
+              "gemm_rope_store: null pointer");
+  if (head_dim != kBM)
+    return fail(LSB_ERR_UNSUPPORTED, "gemm_rope_store: head_dim %d (only %d: one head per tile)",
+                head_dim, kBM);
+  LSB_REQUIRE(hq > 0 && hkv > 0 && N == static_cast<int64_t>(hq + 2 * hkv) * head_dim,
+              "gemm_rope_store: N=%lld is not (hq + 2 hkv) x head_dim", (long long)N);
+  LSB_REQUIRE(max_pos > 0 && slot_stride >= static_cast<int64_t>(hkv) * head_dim &&
+                  slot_stride % 4 == 0 && aligned(k_cache, 8) && aligned(v_cache, 8) &&
+                  aligned(cos_sin, 16),
+              "gemm_rope_store: bad cache or table layout");
+  RopeParams rp;
+  rp.positions = positions;
+  rp.cos_sin = cos_sin;
+  rp.max_pos = max_pos;
+  rp.k_cache = static_cast<bf16*>(k_cache);
+  rp.v_cache = static_cast<bf16*>(v_cache);
+  rp.slot_stride = slot_stride;
+  rp.num_slots = num_slots;
+  rp.out_loc = out_loc;
+  rp.hq = hq;
+  rp.hkv = hkv;
+  return gemm_impl(qkv, ldq, x, ldx, w, ldw, nullptr, M, N, K, kEpiRope, nullptr, stream, nullptr,
+                   &rp);
 }
 
 extern "C" int lsb_gemm_concat(void* y, int64_t ldy, const void* x1, int64_t ldx1,

@@ -63,8 +63,9 @@ __global__ void rope_store_kernel(bf16* __restrict__ qkv, int64_t qkv_stride,
     const float2 s = *reinterpret_cast<const float2*>(cs + half + i);
     const float2 x1 = __bfloat1622float2(*reinterpret_cast<const bf162*>(row + i));
     const float2 x2 = __bfloat1622float2(*reinterpret_cast<const bf162*>(row + half + i));
-    const float2 y1 = make_float2(x1.x * c.x - x2.x * s.x, x1.y * c.y - x2.y * s.y);
-    const float2 y2 = make_float2(x2.x * c.x + x1.x * s.x, x2.y * c.y + x1.y * s.y);
+    float2 y1, y2;
+    rope_rotate(x1.x, x2.x, c.x, s.x, y1.x, y2.x);
+    rope_rotate(x1.y, x2.y, c.y, s.y, y1.y, y2.y);
     const bf162 r1 = __floats2bfloat162_rn(y1.x, y1.y);
     const bf162 r2 = __floats2bfloat162_rn(y2.x, y2.y);
     *reinterpret_cast<bf162*>(row + i) = r1;

@@ -219,12 +219,15 @@ def bench_gemm_ar(args, ops, comm, name: str, nccl=None) -> dict:
     ws = [torch.randn(n, k, dtype=torch.bfloat16, device=dev).mul_(0.02) for _ in range(copies)]
     x = torch.randn(m, k, dtype=torch.bfloat16, device=dev)
     y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    comm.set_protocol(args.protocol)
     dist.barrier()
     us_ar = _time_graph(lambda i: comm.gemm_allreduce(x, ws[i % copies], out=y), args.reps)
     dist.barrier()
     us_local = _time_graph(lambda i: ops.gemm(x, ws[i % copies], out=y), args.reps)
     dist.barrier()
     us_allreduce = _time_graph(lambda i: comm.all_reduce(y), args.reps)
+    comm.set_protocol(0)
+    oneshot = args.protocol == 1 or (args.protocol == 0 and tp == 2)
     us_nccl = us_cublas = 0.0
     if nccl is not None:
         # the reference's path: F.linear (cuBLAS) then an NCCL all-reduce of the result
@@ -242,8 +245,11 @@ def bench_gemm_ar(args, ops, comm, name: str, nccl=None) -> dict:
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl) if nccl is not None else \
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     us_ar, us_local, us_allreduce = float(t[0]), float(t[1]), float(t[2])
-    link = 2 * (tp - 1) / tp * m * n * 2  # bytes each rank sends: partials + sums
+    # bytes each rank sends: its partial to every peer (one hop), or partials to the
+    # owners and sums back (two hops)
+    link = (tp - 1) * m * n * 2 if oneshot else 2 * (tp - 1) / tp * m * n * 2
     out = {"kernel": "gemm_allreduce", "shape": name, "tp": tp, "tokens": m, "N": n, "K": k,
+           "protocol": "one hop" if oneshot else "two hops",
            "us": round(us_ar, 2), "us_local_gemm": round(us_local, 2),
            "us_allreduce_alone": round(us_allreduce, 2),
            "weight_GBps": round(w_bytes / us_ar / 1e3, 1),
@@ -352,6 +358,8 @@ def main(argv=None) -> None:
     ga.add_argument("--tokens", type=int, default=256)
     ga.add_argument("--shape", nargs="+", default=["o", "down"], choices=["o", "down"])
     ga.add_argument("--reps", type=int, default=60)
+    ga.add_argument("--protocol", type=int, default=0, choices=[0, 1, 2],
+                    help="all-reduce protocol: 0 automatic, 1 one hop, 2 two hops via owners")
     ga.add_argument("--vs-nccl", action="store_true",
                     help="also time F.linear (cuBLAS) + an NCCL all-reduce on the same shapes")
     nm = sub.add_parser("norm")

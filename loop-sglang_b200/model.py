@@ -308,11 +308,6 @@ class LoopedDecoder:
         """RopeAttn + AttentionLayer + backend (models/utils.py:119-131,
         layers/attention.py:77-100, attention/fa.py:68-93)."""
         c = self.cfg
-        if lw.qkv_bias is None:
-            qkv = ops.gemm(x, lw.qkv)
-        else:
-            epi = ops.LSB_EPI_BIAS_AFTER_ROUND if huginn else ops.LSB_EPI_BIAS
-            qkv = ops.gemm(x, lw.qkv, lw.qkv_bias, epi)
         out_loc, table, page = batch.out_loc, batch.page_table, getattr(kv, "page_size", 1)
         if isinstance(kv, LastExitedKVCache):
             group = kv.layer_groups[cache_layer]
@@ -321,8 +316,18 @@ class LoopedDecoder:
             else:
                 out_loc, table = batch.fixed_out_loc[group], batch.fixed_page_table[group]
         kc, vc = kv.slots(cache_layer)
-        ops.rope_store_kv(qkv, batch.positions, self.cos_sin, self.hq, self.hkv, c.head_dim,
-                          kc, vc, out_loc)
+        if lw.qkv_bias is None and c.head_dim == 128:
+            # one head per weight tile: RoPE and the KV store run in the GEMM's epilogue
+            qkv = ops.gemm_rope_store(x, lw.qkv, batch.positions, self.cos_sin, self.hq,
+                                      self.hkv, c.head_dim, kc, vc, out_loc)
+        else:
+            if lw.qkv_bias is None:
+                qkv = ops.gemm(x, lw.qkv)
+            else:
+                epi = ops.LSB_EPI_BIAS_AFTER_ROUND if huginn else ops.LSB_EPI_BIAS
+                qkv = ops.gemm(x, lw.qkv, lw.qkv_bias, epi)
+            ops.rope_store_kv(qkv, batch.positions, self.cos_sin, self.hq, self.hkv,
+                              c.head_dim, kc, vc, out_loc)
         q = qkv[:, : self.hq * c.head_dim].view(-1, self.hq, c.head_dim)
         if batch.prefix_groups is not None and not batch.is_prefill and table is batch.page_table:
             o = ops.paged_attention_shared_prefix(q, kc, vc, table, batch.cache_seqlens,

@@ -263,6 +263,34 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     return out
 
 
+def gemm_rope_store(x: torch.Tensor, w: torch.Tensor, positions: torch.Tensor,
+                    cos_sin: torch.Tensor, hq: int, hkv: int, head_dim: int,
+                    k_cache: torch.Tensor, v_cache: torch.Tensor, out_loc: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """The QKV projection with RoPE and the KV store in its epilogue: ``gemm(x, w)`` then
+    ``rope_store_kv`` on the result, in one launch (models/utils.py:119-131,
+    layers/attention.py:88-90). 128-dim heads only (one head per weight tile)."""
+    _need(x, BF16, "x", contiguous=False)
+    _need(w, BF16, "w", contiguous=False)
+    _need(positions, torch.int32, "positions")
+    _need(cos_sin, torch.float32, "cos_sin")
+    _need(k_cache, BF16, "k_cache", contiguous=False)
+    _need(v_cache, BF16, "v_cache", contiguous=False)
+    _need(out_loc, torch.int32, "out_loc")
+    if k_cache.stride(0) != v_cache.stride(0) or k_cache.shape[0] != v_cache.shape[0]:
+        raise ValueError("k_cache and v_cache must share slot count and stride")
+    m, k = x.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"gemm_rope_store: x has K={k}, w has K={w.shape[1]}")
+    out = torch.empty(m, n, dtype=BF16, device=x.device) if out is None else out
+    call("lsb_gemm_rope_store", out.data_ptr(), _row_stride(out, "out"), x.data_ptr(),
+         _row_stride(x, "x"), w.data_ptr(), _row_stride(w, "w"), m, n, k, positions.data_ptr(),
+         cos_sin.data_ptr(), cos_sin.shape[0], k_cache.data_ptr(), v_cache.data_ptr(),
+         k_cache.stride(0), k_cache.shape[0], out_loc.data_ptr(), hq, hkv, head_dim, _stream())
+    return out
+
+
 def gemm_concat(x1: torch.Tensor, x2: torch.Tensor, w: torch.Tensor,
                 bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
     """``F.linear(torch.cat([x1, x2], -1), w, bias)`` without the concatenation

@@ -109,6 +109,60 @@ def test_rope_store(hq: int, hkv: int, d: int) -> None:
     assert torch.equal(vc2[loc[keep].long()].cpu(), ev[loc[keep].long()])
 
 
+@pytest.mark.parametrize("hq,hkv", [(16, 16), (8, 8), (16, 4)])
+@pytest.mark.parametrize("m", [1, 5, 143, 263])
+def test_gemm_rope_store_equals_gemm_then_rope_store(hq: int, hkv: int, m: int) -> None:
+    """The QKV GEMM with RoPE + KV store in its epilogue: the same qkv output and cache
+    contents, bit for bit, as the GEMM followed by rope_store_kv (128-dim heads), and
+    within tolerance of the oracle."""
+    g = gen(hq * 1000 + hkv * 10 + m)
+    d, k = 128, 2048
+    n = (hq + 2 * hkv) * d
+    x = bf(torch.randn(m, k, generator=g))
+    w = bf(torch.randn(n, k, generator=g) * 0.02)
+    pos = torch.randint(0, 4000, (m,), generator=g, dtype=torch.int32)
+    cs = O.rope_cos_sin_cache(d, 4096, 1e6)
+    slots = 2 * m + 8
+    loc = (torch.randperm(slots - 1, generator=g)[:m] + 1).to(torch.int32)
+    loc[::4] = 0  # padding rows: never stored
+    kc0 = bf(torch.randn(slots, hkv * d, generator=g))
+    vc0 = bf(torch.randn(slots, hkv * d, generator=g))
+    xd, wd, posd, csd, locd = x.to(DEV), w.to(DEV), pos.to(DEV), cs.to(DEV), loc.to(DEV)
+    kc1, vc1 = kc0.to(DEV), vc0.to(DEV)
+    qkv1 = ops.gemm(xd, wd)
+    ops.rope_store_kv(qkv1, posd, csd, hq, hkv, d, kc1, vc1, locd)
+    kc2, vc2 = kc0.to(DEV), vc0.to(DEV)
+    qkv2 = ops.gemm_rope_store(xd, wd, posd, csd, hq, hkv, d, kc2, vc2, locd)
+    assert torch.equal(qkv2, qkv1)
+    assert torch.equal(kc2, kc1) and torch.equal(vc2, vc1)
+    # against the oracle: projection, rotation of q and k, the store
+    ref = O.linear(x, w)
+    q = O.apply_rope_neox(pos, ref[:, : hq * d].view(m, hq, d), cs).view(m, -1)
+    kr = O.apply_rope_neox(pos, ref[:, hq * d:(hq + hkv) * d].view(m, hkv, d), cs).view(m, -1)
+    close(qkv2[:, : hq * d], q)
+    close(qkv2[:, hq * d:(hq + hkv) * d], kr)
+    close(qkv2[:, (hq + hkv) * d:], ref[:, (hq + hkv) * d:])
+    no_device_errors()
+    # a position outside the table and a slot outside the pool are flagged, not read/written
+    bad_pos, bad_loc = pos.clone(), loc.clone()
+    bad_pos[0] = 4096
+    bad_loc[-1] = slots + 5 if int(loc[-1]) != 0 else 0
+    ops.gemm_rope_store(xd, wd, bad_pos.to(DEV), csd, hq, hkv, d, kc0.to(DEV), vc0.to(DEV),
+                        bad_loc.to(DEV))
+    word = ops.device_error_word(reset=True)
+    assert word & 1 and (int(bad_loc[-1]) == 0 or word & 2)
+
+
+def test_gemm_rope_store_rejects_other_head_dims() -> None:
+    x = torch.zeros(2, 64, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(3 * 96, 64, dtype=torch.bfloat16, device=DEV)
+    kc = torch.zeros(4, 96, dtype=torch.bfloat16, device=DEV)
+    pos = torch.zeros(2, dtype=torch.int32, device=DEV)
+    cs = torch.zeros(8, 96, dtype=torch.float32, device=DEV)
+    with pytest.raises(Exception, match="head_dim"):
+        ops.gemm_rope_store(x, w, pos, cs, 1, 1, 96, kc, kc.clone(), pos)
+
+
 def test_store_kv_exact_and_bounds() -> None:
     g = gen(3)
     k = bf(torch.randn(5, 2, 8, generator=g))

@@ -59,54 +59,58 @@ def _worker(rank: int, world: int, port: int, errq) -> None:
         def gen(seed: int) -> torch.Generator:
             return torch.Generator().manual_seed(seed)
 
-        # all-reduce: bit-exact against the rank-ordered fp32 sum, on repeated calls
-        for it in range(3):
-            for (m, n) in [(1, 2048), (143, 2048), (7, 100), (64, 4096)]:
-                parts = [_bf(torch.randn(m, n, generator=gen(1000 * it + 10 * r + n))) for r in range(world)]
-                x = parts[rank].to(dev)
-                cm.all_reduce(x)
-                want = torch.zeros(m, n)
-                for p in parts:
-                    want += p.float()
-                assert torch.equal(x.cpu(), _bf(want)), f"all_reduce {m}x{n} call {it}"
-
-        # all-gather: exact concatenation
-        for it in range(3):
-            parts = [_bf(torch.randn(5, 64, generator=gen(77 + it * 10 + r))) for r in range(world)]
-            got = cm.all_gather(parts[rank].to(dev))
-            assert torch.equal(got.cpu(), torch.cat(parts)), f"all_gather call {it}"
-
-        # fused row-parallel GEMM + all-reduce (o_proj / down_proj shards, ragged shapes, bias)
-        # (1100, 2048, 2048): more rows than the communicator's buffer takes at once (512 x
-        # 2048), so the call runs as several complete launches of resident tiles
-        shapes = [(143, 2048, 2048), (143, 2048, 5632), (1, 2048, 2048), (33, 200, 192),
-                  (256, 2048, 512), (1100, 2048, 2048)]
-        for it in range(2):
-            for (m, n, k_full) in shapes:
-                k = k_full // world
-                xs = [_bf(torch.randn(m, k, generator=gen(5 + r + 100 * it))) for r in range(world)]
-                ws = [_bf(torch.randn(n, k, generator=gen(50 + r)) * 0.05) for r in range(world)]
-                bias = _bf(torch.randn(n, generator=gen(9)) * 0.1) if n == 200 else None
-                b_dev = bias.to(dev) if bias is not None else None
-                got = cm.gemm_allreduce(xs[rank].to(dev), ws[rank].to(dev), b_dev)
-                # exact: every rank's partial through the same single-GPU kernel (up to 256
-                # rows both take the same tile plan; larger calls run as several launches
-                # with the fused variant's one-wave plan, checked by tolerance below)
-                if m <= 256:
+        # both all-reduce protocols (two hops via owners, one hop), then the default; calls
+        # alternate between them on the same buffers and epochs
+        for proto in (2, 1, 0):
+            cm.set_protocol(proto)
+            # all-reduce: bit-exact against the rank-ordered fp32 sum, on repeated calls
+            for it in range(3):
+                for (m, n) in [(1, 2048), (143, 2048), (7, 100), (64, 4096)]:
+                    parts = [_bf(torch.randn(m, n, generator=gen(1000 * it + 10 * r + n))) for r in range(world)]
+                    x = parts[rank].to(dev)
+                    cm.all_reduce(x)
                     want = torch.zeros(m, n)
-                    for r in range(world):
-                        part = ops.linear(xs[r].to(dev), ws[r].to(dev), b_dev)
-                        want += part.float().cpu()
-                    assert torch.equal(got.cpu(), _bf(want)), \
-                        f"gemm_allreduce {m}x{n}x{k_full} call {it}"
-                ref = sum(xs[r].float() @ ws[r].float().t() for r in range(world))
-                if bias is not None:
-                    ref = ref + world * bias.float()
-                # bf16 partials of magnitude ~|ref|max are rounded before the sum (as the
-                # reference's per-rank F.linear outputs are), so the absolute error scales
-                # with the largest output, not with each element
-                scale = float(ref.abs().max())
-                torch.testing.assert_close(got.float().cpu(), ref, rtol=2e-2, atol=1e-2 * scale)
+                    for p in parts:
+                        want += p.float()
+                    assert torch.equal(x.cpu(), _bf(want)), f"all_reduce {m}x{n} call {it}"
+
+            # all-gather: exact concatenation
+            for it in range(3):
+                parts = [_bf(torch.randn(5, 64, generator=gen(77 + it * 10 + r))) for r in range(world)]
+                got = cm.all_gather(parts[rank].to(dev))
+                assert torch.equal(got.cpu(), torch.cat(parts)), f"all_gather call {it}"
+
+            # fused row-parallel GEMM + all-reduce (o_proj / down_proj shards, ragged shapes, bias)
+            # (1100, 2048, 2048): more rows than the communicator's buffer takes at once (512 x
+            # 2048), so the call runs as several complete launches of resident tiles
+            shapes = [(143, 2048, 2048), (143, 2048, 5632), (1, 2048, 2048), (33, 200, 192),
+                      (256, 2048, 512), (1100, 2048, 2048)]
+            for it in range(2):
+                for (m, n, k_full) in shapes:
+                    k = k_full // world
+                    xs = [_bf(torch.randn(m, k, generator=gen(5 + r + 100 * it))) for r in range(world)]
+                    ws = [_bf(torch.randn(n, k, generator=gen(50 + r)) * 0.05) for r in range(world)]
+                    bias = _bf(torch.randn(n, generator=gen(9)) * 0.1) if n == 200 else None
+                    b_dev = bias.to(dev) if bias is not None else None
+                    got = cm.gemm_allreduce(xs[rank].to(dev), ws[rank].to(dev), b_dev)
+                    # exact: every rank's partial through the same single-GPU kernel (up to 256
+                    # rows both take the same tile plan; larger calls run as several launches
+                    # with the fused variant's one-wave plan, checked by tolerance below)
+                    if m <= 256:
+                        want = torch.zeros(m, n)
+                        for r in range(world):
+                            part = ops.linear(xs[r].to(dev), ws[r].to(dev), b_dev)
+                            want += part.float().cpu()
+                        assert torch.equal(got.cpu(), _bf(want)), \
+                            f"gemm_allreduce {m}x{n}x{k_full} call {it}"
+                    ref = sum(xs[r].float() @ ws[r].float().t() for r in range(world))
+                    if bias is not None:
+                        ref = ref + world * bias.float()
+                    # bf16 partials of magnitude ~|ref|max are rounded before the sum (as the
+                    # reference's per-rank F.linear outputs are), so the absolute error scales
+                    # with the largest output, not with each element
+                    scale = float(ref.abs().max())
+                    torch.testing.assert_close(got.float().cpu(), ref, rtol=2e-2, atol=1e-2 * scale)
         torch.cuda.synchronize()
         assert ops.device_error_word(reset=True) == 0
 
