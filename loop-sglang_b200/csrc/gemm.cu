@@ -582,8 +582,11 @@ __global__ void __launch_bounds__(kThreads, 2)
           // goes to the tile owner's recv slot as tagged words, rows of N elements
           const bf16 v4[4] = {__float2bfloat16_rn(o0), __float2bfloat16_rn(o1),
                               __float2bfloat16_rn(o2), __float2bfloat16_rn(o3)};
-          comm_put4(p.comm, tile_n % p.comm.world, ar_epoch,
-                    static_cast<int64_t>(m0 + m) * p.N + col, v4);
+          // quads past N (a ragged last tile; N % 4 == 0) would land on the next row's
+          // elements, which another region's words occupy
+          if (col < p.N)
+            comm_put4(p.comm, tile_n % p.comm.world, ar_epoch,
+                      static_cast<int64_t>(m0 + m) * p.N + col, v4);
         } else {
           store4(y, ldy, m0 + m, col, ncols, o0, o1, o2, o3);
         }
