@@ -279,7 +279,9 @@ def parity_stamp(model, cpu_weights: dict | None, rank: int, world: int,
     def oracle_logits(dtype: torch.dtype) -> list[torch.Tensor]:
         w = (om.with_fp32_matrices(cpu_weights) if dtype == torch.bfloat16
              else {k: v.float() for k, v in cpu_weights.items()})
-        oracle = om.LoopedModel(ocfg, w, policy)
+        # with the tensor-parallel ranks' rounding points (row-parallel partials rounded
+        # before their sum, as the reference's per-rank F.linear + all-reduce)
+        oracle = om.LoopedModel(ocfg, w, policy, tp=world)
         if policy == "last_exited":
             pool = om.SlotKVPool(oracle.slot_layout(), num_pages, cfg.kv_heads, cfg.head_dim,
                                  dtype)

@@ -214,6 +214,8 @@ class LoopedModel:
     cfg: LoopedConfig
     weights: dict[str, torch.Tensor]
     policy: str = "depth_indexed"
+    # tensor-parallel ranks whose rounding points the row-parallel linears reproduce
+    tp: int = 1
     cos_sin: torch.Tensor = field(init=False)
 
     def __post_init__(self) -> None:
@@ -236,6 +238,20 @@ class LoopedModel:
     # -- sublayers -------------------------------------------------------------
     def _w(self, name: str) -> torch.Tensor:
         return self.weights[name]
+
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """``LinearOProj`` / ``LinearRowParallel`` over ``tp`` ranks (layers/linear.py:92-128
+        with distributed/impl.py:63-70): rank r's ``F.linear`` over its contiguous slice of
+        the input features is rounded to the working dtype, then the ranks' outputs are
+        summed -- in rank order in fp32 and rounded once, which is NCCL's result for two
+        ranks and the order of this repository's fused all-reduce for any number."""
+        if self.tp == 1:
+            return ops.linear(x, w)
+        k = x.shape[-1] // self.tp
+        acc = torch.zeros(x.shape[0], w.shape[0], dtype=torch.float32)
+        for r in range(self.tp):
+            acc += ops.linear(x[:, r * k:(r + 1) * k], w[:, r * k:(r + 1) * k]).float()
+        return acc.to(x.dtype)
 
     def attention(self, p: str, x: torch.Tensor, cache_layer: int, batch: Batch, pool,
                   depth) -> torch.Tensor:
@@ -266,12 +282,12 @@ class LoopedModel:
         pool.store(cache_layer, k, v, out_loc)
         o = ops.paged_attention(q, pool.k_cache(cache_layer), pool.v_cache(cache_layer), table,
                                 batch.cache_seqlens, batch.cu_seqlens_q, self.scale)
-        return ops.linear(o.reshape(-1, qd), self._w(f"{p}.self_attn.o_proj.weight"))
+        return self._row_parallel(o.reshape(-1, qd), self._w(f"{p}.self_attn.o_proj.weight"))
 
     def mlp(self, p: str, x: torch.Tensor) -> torch.Tensor:
         """``GatedMLP.forward`` (models/utils.py:45-50): gate_up rows are ``[gate; up]``."""
         gu = ops.linear(x, self._w(f"{p}.mlp.gate_up_proj.weight"))
-        return ops.linear(ops.silu_and_mul(gu), self._w(f"{p}.mlp.down_proj.weight"))
+        return self._row_parallel(ops.silu_and_mul(gu), self._w(f"{p}.mlp.down_proj.weight"))
 
     def ouro_layer(self, p, x, residual, cache_layer, batch, pool, depth):
         """``OuroDecoderLayer.forward`` (ouro.py:37-53), the sandwich-norm layer."""

@@ -77,12 +77,14 @@ def make_pool(model: LoopedModel, num_pages: int, page_size: int, dtype):
     return PagedKVPool(model.num_kv_layers, num_pages, page_size, c.kv_heads, c.head_dim, dtype)
 
 
-def replay_cb(name: str, dtype=torch.float32) -> tuple[dict, dict[str, torch.Tensor], object]:
-    """Oracle logits for every step of a CB fixture; returns (fixture, logits-by-step, pool)."""
+def replay_cb(name: str, dtype=torch.float32,
+              tp: int = 1) -> tuple[dict, dict[str, torch.Tensor], object]:
+    """Oracle logits for every step of a CB fixture; returns (fixture, logits-by-step, pool).
+    ``tp``: the rounding points of that many tensor-parallel ranks."""
     cfg, policy = CB_CASES[name]
     fx = load(name)
     weights = make_weights(cfg, int(fx["seed"]), dtype=dtype, gate_bias=0.0)
-    model = LoopedModel(cfg, weights, policy)
+    model = LoopedModel(cfg, weights, policy, tp=tp)
     pool = make_pool(model, NUM_PAGES, int(fx["page_size"]), dtype)
     out = {}
     for prefix, is_prefill in cb_steps(fx):
@@ -93,12 +95,14 @@ def replay_cb(name: str, dtype=torch.float32) -> tuple[dict, dict[str, torch.Ten
     return fx, out, pool
 
 
-def replay_cdb(name: str, dtype=torch.float32) -> tuple[dict, dict[str, torch.Tensor]]:
-    """Oracle prefill, prelude, mixed-depth core phases and coda for a CDB fixture."""
+def replay_cdb(name: str, dtype=torch.float32,
+               tp: int = 1) -> tuple[dict, dict[str, torch.Tensor]]:
+    """Oracle prefill, prelude, mixed-depth core phases and coda for a CDB fixture
+    (``tp``: the rounding points of that many tensor-parallel ranks)."""
     cfg, policy = CDB_CASES[name]
     fx = load(name)
     weights = make_weights(cfg, int(fx["seed"]), dtype=dtype, gate_bias=0.3)
-    model = LoopedModel(cfg, weights, policy)
+    model = LoopedModel(cfg, weights, policy, tp=tp)
     pool = make_pool(model, CDB_NUM_PAGES, 1, dtype)
     res: dict[str, torch.Tensor] = {}
     pre = batch_from(fx, "prefill", fx["prefill_ids"], True)

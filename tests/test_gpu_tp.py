@@ -121,13 +121,15 @@ def _worker(rank: int, world: int, port: int, errq) -> None:
 
         for name in ("ouro_cb_depth_indexed", "ouro_cb_shared", "ouro_cb_last_exited"):
             _, got = gpu_replay_cb(name, comm=cm)
-            _, ref, _ = replay_cb(name, dtype=torch.bfloat16)
+            # the oracle with the two ranks' rounding points (each rank's row-parallel
+            # partial rounded to bf16 before the sum, as the reference's F.linear + NCCL)
+            _, ref, _ = replay_cb(name, dtype=torch.bfloat16, tp=world)
             for prefix, logits in got.items():
                 assert rel_err(logits, ref[prefix]) < 2e-2, (name, prefix)
                 assert greedy_agrees(logits, ref[prefix]), (name, prefix)
         for name in ("ouro_cdb_last_exited", "ouro_cdb_shared"):
             fx, got = gpu_replay_cdb(name, comm=cm)
-            _, ref = replay_cdb(name, dtype=torch.bfloat16)
+            _, ref = replay_cdb(name, dtype=torch.bfloat16, tp=world)
             assert rel_err(got["prefill_logits"], ref["prefill_logits"]) < 2e-2, name
             k = 0
             while f"core{k}_rows" in fx:
