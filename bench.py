@@ -79,6 +79,26 @@ def agree_min(n: int, world: int, dev) -> int:
     return int(t.item())
 
 
+def init_nccl(dev, seconds: int) -> None:
+    """The job's NCCL process group, created (and its communicator initialised by a first
+    barrier) with file descriptor 1 pointed at stderr: NCCL may print its version banner
+    on stdout, where rank 0's one JSON line must stand alone."""
+    import datetime
+
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=seconds),
+                                             device_id=dev)
+        torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def log(msg: str) -> None:
     print(msg, file=sys.stderr, flush=True)
 
@@ -548,10 +568,7 @@ def run_b200(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
+        init_nccl(dev, 300)
     radix = args.workload == "radix"
     cfg = LoopedConfig(**(OURO_26B if radix else OURO_14B))
     out_tokens, mid = (RADIX_OUT, RADIX_MID) if radix else (OUT_TOKENS, MID)
@@ -872,10 +889,7 @@ def run_b200_cdb(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
+        init_nccl(dev, 300)
     cfg = LoopedConfig(**{**OURO_14B, "exit_threshold": 0.2})
     t0 = time.perf_counter()
     comm = None
@@ -1102,10 +1116,7 @@ def run_b200_prefill(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
+        init_nccl(dev, 300)
     cfg = LoopedConfig(**OURO_14B)
     prompts = request_lengths()[: args.batch or PREFILL_REQS]
     n_tok = int(prompts.sum())
@@ -1283,10 +1294,7 @@ def run_b200_huginn(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                             device_id=dev)
+        init_nccl(dev, 600)
     cfg = LoopedConfig(**HUGINN)
     t0 = time.perf_counter()
     weights = gpu_weights(cfg, dev, SEED)
