@@ -213,8 +213,9 @@ int lsb_gemm(void* y, int64_t ldy, const void* x, int64_t ldx, const void* w, in
  * tuning: 0 automatic (the default), 1 one wide tile of all tokens for
  * 257..384 tokens (two MMAs of up to 192 tokens per K step, one CTA per SM;
  * never chosen automatically), 2 tiles of at most 96 tokens for 257..512
- * tokens, 3 one CTA per SM for every tile size. No counterpart in the
- * reference (its cuBLAS heuristics). */
+ * tokens, 3 one CTA per SM for every tile size, 4 tiles of 256 weight rows on
+ * CTA pairs (tcgen05 cta_group::2; calls without the fused all-reduce). No
+ * counterpart in the reference (its cuBLAS heuristics). */
 int lsb_gemm_force_plan(int32_t mode);
 /* Largest token-tile width later lsb_gemm* calls may use (0 automatic; else a
  * multiple of 16 in 16..256), for the same benchmarks and tuning. */

@@ -131,6 +131,36 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Pair variants (tcgen05 cta_group::2): a CTA pair shares one MMA of 256 weight rows (each
+// CTA holds 128 of them and half of the tokens); the even CTA issues it. The pair's TMA
+// loads complete on the even CTA's stage barrier (a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t bar_cluster, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Arrival, once this thread's MMAs so far have completed, on the mbarrier at a
+// shared::cluster address (this CTA's or its pair peer's).
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          bar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   __syncwarp();
   asm volatile("barrier.cluster.arrive.aligned;\n" ::: "memory");
@@ -213,7 +243,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
-template <int EPI, bool CLUSTER, bool AR>
+template <int EPI, bool CLUSTER, bool AR, bool PAIR = false>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmap_w,
                         const __grid_constant__ CUtensorMap tmap_x,
@@ -222,8 +252,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  static_assert(!PAIR || (CLUSTER && !AR), "pair tiles run as clusters, without the all-reduce");
   const int stages = p.stages;
-  const int b_bytes = p.bn * kBK * 2;
+  // a pair CTA holds half of the tile's tokens (of every MMA half)
+  const int b_bytes = (PAIR ? p.bn / 2 : p.bn) * kBK * 2;
   const int stage_bytes = kABytes + b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
   uint64_t* empty = full + kMaxStages;
@@ -234,9 +266,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = CLUSTER ? p.splits : 1;
-  const int split = CLUSTER ? static_cast<int>(cluster_rank()) : 0;
-  const int tile_n = blockIdx.x / S, tile_m = blockIdx.y;
+  // Pair variants: cluster rank r = 2 * split + member; member 0 (the even CTA) issues the
+  // pair's MMAs. tile_n is this CTA's 128-row weight block either way.
+  const int crank = CLUSTER ? static_cast<int>(cluster_rank()) : 0;
+  const int member = PAIR ? (crank & 1) : 0;
+  const int split = PAIR ? (crank >> 1) : crank;
+  const int tile_n = PAIR ? (blockIdx.x / (2 * S)) * 2 + member : blockIdx.x / S;
+  const int tile_m = blockIdx.y;
   const int n0 = tile_n * kBM, m0 = tile_m * p.bn;
+  const uint32_t leader = static_cast<uint32_t>(crank - member);
   const int kblocks = (p.K + kBK - 1) / kBK;
   const int kb_begin = static_cast<int>(static_cast<int64_t>(kblocks) * split / S);
   const int kb_end = static_cast<int>(static_cast<int64_t>(kblocks) * (split + 1) / S);
@@ -245,8 +283,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   // different block spreads those reads over all of x instead of having every CTA
   // hit the same L2 lines at the same moment. (The fp32 sum order per tile changes
   // with it; results stay deterministic.)
+  // (both CTAs of a pair must walk the same K blocks in the same order)
   const int rot = nk > 0 && !(p.flags & kFlagNoRotate)
-                      ? static_cast<int>((static_cast<int64_t>(tile_n) * 7 + tile_m * 3) % nk)
+                      ? static_cast<int>((static_cast<int64_t>(PAIR ? tile_n >> 1 : tile_n) * 7 +
+                                          tile_m * 3) % nk)
                       : 0;
   uint32_t tmem_cols = 32;
   while (tmem_cols < static_cast<uint32_t>(p.bn)) tmem_cols <<= 1;
@@ -267,13 +307,24 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(tmem_cols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (PAIR) {
+      // both CTAs of the pair allocate together (same warp, same slot offset)
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(tmem_slot)),
+                   "r"(tmem_cols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;");
   __syncthreads();
+  // a pair's loads complete on the even CTA's barriers and its MMAs write both CTAs'
+  // accumulators: both CTAs' barriers and TMEM exist before either starts
+  if (PAIR) cluster_sync_all();
   asm volatile("tcgen05.fence::after_thread_sync;");
   const uint32_t tmem_base = *tmem_slot;
   bool have_acc = false;
@@ -287,23 +338,37 @@ __global__ void __launch_bounds__(kThreads, 2)
       auto kb_of = [&](int i) { return kb_begin + (i + rot) % nk; };
       const bool hints = p.flags & kFlagCacheHints;
       const uint64_t pol_w = policy_evict_first(), pol_x = policy_evict_last();
+      // the barrier a stage's loads complete on: this CTA's, or for a pair the even CTA's
+      auto bar_of = [&](uint64_t* bar) { return map_rank(smem_u32(bar), leader); };
       auto load_w = [&](uint8_t* dst, uint64_t* bar, int kb) {
         const CUtensorMap* map = kb < p.kb1 ? &tmap_w : &tmap_w2;
         const int kx = (kb < p.kb1 ? kb : kb - p.kb1) * kBK;
-        if (hints) tma_load_2d_hint(dst, map, bar, kx, n0, pol_w);
+        if (PAIR) tma_load_2d_pair(dst, map, bar_of(bar), kx, n0);
+        else if (hints) tma_load_2d_hint(dst, map, bar, kx, n0, pol_w);
         else tma_load_2d(dst, map, bar, kx, n0);
       };
       auto load_x = [&](uint8_t* dst, uint64_t* bar, int kb) {
         const CUtensorMap* map = kb < p.kb1 ? &tmap_x : &tmap_x2;
         const int kx = (kb < p.kb1 ? kb : kb - p.kb1) * kBK;
         for (int h = 0; h < p.halves; ++h) {
-          uint8_t* d = dst + h * p.bh * kBK * 2;
-          if (hints) tma_load_2d_hint(d, map, bar, kx, m0 + h * p.bh, pol_x);
-          else tma_load_2d(d, map, bar, kx, m0 + h * p.bh);
+          if (PAIR) {  // this member's half of MMA half h: bh / 2 tokens
+            const int hb = p.bh / 2;
+            tma_load_2d_pair(dst + h * hb * kBK * 2, map, bar_of(bar), kx,
+                             m0 + h * p.bh + member * hb);
+          } else {
+            uint8_t* d = dst + h * p.bh * kBK * 2;
+            if (hints) tma_load_2d_hint(d, map, bar, kx, m0 + h * p.bh, pol_x);
+            else tma_load_2d(d, map, bar, kx, m0 + h * p.bh);
+          }
         }
       };
+      // the expected bytes of a stage: both CTAs' loads for a pair, counted on the even CTA
+      auto expect = [&](uint64_t* bar) {
+        if (!PAIR) mbar_expect_tx(bar, static_cast<uint32_t>(stage_bytes));
+        else if (member == 0) mbar_expect_tx(bar, static_cast<uint32_t>(2 * stage_bytes));
+      };
       for (int i = 0; i < pre; ++i) {
-        mbar_expect_tx(&full[i], static_cast<uint32_t>(stage_bytes));
+        expect(&full[i]);
         load_w(smem + i * stage_bytes, &full[i], kb_of(i));
       }
       asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -313,14 +378,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t round = static_cast<uint32_t>(i / stages);
         if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, p.error_flag)) break;
         uint8_t* a_tile = smem + s * stage_bytes;
-        mbar_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
+        expect(&full[s]);
         const int kb = kb_of(i);
         load_w(a_tile, &full[s], kb);
         load_x(a_tile + kABytes, &full[s], kb);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && member == 0) {  // a pair's odd CTA issues nothing: its data rides along
       bool ok = true;
       for (int i = 0; i < nk; ++i) {
         const int s = i % stages;
@@ -336,17 +401,34 @@ __global__ void __launch_bounds__(kThreads, 2)
           // half h: tokens h*bh .. h*bh+bh-1 (rows of the B tile, 128 bytes each; bh is a
           // multiple of 16, so the half starts on a 1024-byte swizzle atom) into TMEM
           // columns h*bh ..
-          const uint64_t bdesc = smem_desc(a_tile + kABytes + h * p.bh * kBK * 2);
+          // (pair: this CTA holds the half's first bh / 2 tokens, the odd CTA the rest, at
+          // the same offset; bh / 2 is a multiple of 8, a whole swizzle atom)
+          const uint64_t bdesc =
+              smem_desc(a_tile + kABytes + h * (PAIR ? p.bh / 2 : p.bh) * kBK * 2);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             // advance 16 bf16 = 32 bytes along K inside the swizzle atom
-            umma_f16(tmem_base + static_cast<uint32_t>(h * p.bh), adesc + 2 * kk, bdesc + 2 * kk,
-                     p.idesc, (i > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t d = tmem_base + static_cast<uint32_t>(h * p.bh);
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            if (PAIR) umma_f16_pair(d, adesc + 2 * kk, bdesc + 2 * kk, p.idesc, acc);
+            else umma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, p.idesc, acc);
           }
         }
-        umma_commit(&empty[s]);
+        if (PAIR) {  // frees the stage in both CTAs
+          umma_commit_pair(map_rank(smem_u32(&empty[s]), leader));
+          umma_commit_pair(map_rank(smem_u32(&empty[s]), leader + 1));
+        } else {
+          umma_commit(&empty[s]);
+        }
       }
-      if (ok) umma_commit(tmem_full);
+      if (ok) {
+        if (PAIR) {
+          umma_commit_pair(map_rank(smem_u32(tmem_full), leader));
+          umma_commit_pair(map_rank(smem_u32(tmem_full), leader + 1));
+        } else {
+          umma_commit(tmem_full);
+        }
+      }
     }
   }
   __syncwarp();
@@ -393,7 +475,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int j = 0; j < 16; ++j) {
         if (c0 + j < tokens) {
           const uint32_t a = recv_addr + 4u * static_cast<uint32_t>((split * per + jl) * kBM + row);
-          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(a, o)),
+          // the owner of slice o: split o of this CTA's member (pair) or of the cluster
+          const uint32_t owner = PAIR ? static_cast<uint32_t>(2 * o + member) : static_cast<uint32_t>(o);
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(map_rank(a, owner)),
                        "f"(__uint_as_float(v[j]))
                        : "memory");
         }
@@ -612,8 +696,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(tmem_cols));
+    if (PAIR)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(tmem_cols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(tmem_cols));
   }
   (void)have_acc;
 }
@@ -656,6 +744,7 @@ int make_tmap(CUtensorMap* map, const void* ptr, int64_t rows, int64_t k, int64_
 struct Plan {
   int bn, halves, stages, splits, tiles_n, tiles_m;
   size_t smem;
+  bool pair = false;  // tiles of 256 weight rows on CTA pairs (tiles_n counts 128-row blocks)
 };
 
 // Plan selection for benchmarks and tuning (lsb_gemm_force_plan): 0 automatic.
@@ -679,7 +768,15 @@ int num_sms() {
 using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                         const CUtensorMap, GemmParams);
 
-Kernel kernel_for(bool cluster, int epilogue, bool ar = false) {
+Kernel kernel_for(bool cluster, int epilogue, bool ar = false, bool pair = false) {
+  static const Kernel pair_kernels[kEpiKinds] = {
+      gemm_tcgen05_kernel<LSB_EPI_NONE, true, false, true>,
+      gemm_tcgen05_kernel<LSB_EPI_BIAS, true, false, true>,
+      gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, true, false, true>,
+      gemm_tcgen05_kernel<LSB_EPI_SWIGLU, true, false, true>,
+      gemm_tcgen05_kernel<kEpiArgmax, true, false, true>,
+      gemm_tcgen05_kernel<kEpiRope, true, false, true>};
+  if (pair) return pair_kernels[epilogue];
   static const Kernel kernels[2][kEpiKinds] = {
       {gemm_tcgen05_kernel<LSB_EPI_NONE, false, false>, gemm_tcgen05_kernel<LSB_EPI_BIAS, false, false>,
        gemm_tcgen05_kernel<LSB_EPI_BIAS_AFTER_ROUND, false, false>,
@@ -700,15 +797,16 @@ constexpr int kMaxSmem = 227 * 1024;
 
 // Raises a kernel's dynamic shared-memory limit once per device (needed before both
 // the launch and the occupancy queries below).
-int configure(bool cluster, int epilogue, bool ar = false) {
+int configure(bool cluster, int epilogue, bool ar = false, bool pair = false) {
   static std::mutex mu;
-  static uint64_t done[64] = {0};  // bit (ar*16 + cluster*8 + epilogue) per device
+  static uint64_t done[64] = {0};  // bit (pair*24 + ar*16 + cluster*8 + epilogue) per device
   int dev = 0;
   LSB_CUDA(cudaGetDevice(&dev));
-  const uint64_t bit = uint64_t(1) << ((ar ? 16 : 0) + (cluster ? 8 : 0) + epilogue);
+  const uint64_t bit =
+      uint64_t(1) << ((pair ? 24 : 0) + (ar ? 16 : 0) + (cluster ? 8 : 0) + epilogue);
   std::lock_guard<std::mutex> lock(mu);
   if (dev < 64 && (done[dev] & bit)) return LSB_OK;
-  LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue, ar),
+  LSB_CUDA(cudaFuncSetAttribute(kernel_for(cluster, epilogue, ar, pair),
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
   if (dev < 64) done[dev] |= bit;
   return LSB_OK;
@@ -786,7 +884,7 @@ size_t smem_for(int stages, int stage_bytes) {
 // main loop. A split is only used when all clusters of the grid run at once; a
 // cluster left for a second wave would double the kernel's time.
 // Plans lsb_gemm_force_plan can select (automatic otherwise).
-constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3;
+constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3, kPlanPair = 4;
 // Token counts a single wide tile (two MMA halves) covers: its fp32 partials, about
 // bn x 128 x 4 bytes, must fit in the drained stage buffers of one CTA's shared memory.
 constexpr int kWideMax = 384;
@@ -816,6 +914,48 @@ Plan wide_plan(int64_t M, int64_t N, int64_t K) {
   for (int sp = limit; sp >= 2; --sp)
     if (recv_fits(pl.bn, sp, stages, stage_bytes) &&
         pl.tiles_n <= max_active_clusters(sp, pl.smem)) {
+      pl.splits = sp;
+      break;
+    }
+  return pl;
+}
+
+// Tiles of 256 weight rows on CTA pairs (tcgen05 cta_group::2): each CTA of a pair loads
+// its 128 weight rows and half of the token tile, so a token tile crosses into the SMs once
+// per 256 weight rows instead of once per 128 (the decode GEMMs' bound is that ingest).
+// Token tiles as the single-CTA planner cuts them; two CTAs per SM; the K loop split over
+// up to 4 CTA pairs of a cluster (at most 8 CTAs) while all clusters stay co-resident.
+Plan pair_plan(int64_t M, int64_t N, int64_t K) {
+  Plan pl;
+  pl.pair = true;
+  pl.halves = 1;
+  const int64_t m_tiles = (M > 192 && M <= 512) ? (M + 95) / 96 : (M + 255) / 256;
+  int64_t bn = (((M + m_tiles - 1) / m_tiles + 15) / 16) * 16;
+  if (bn > 256) bn = 256;
+  if (bn < 16) bn = 16;
+  pl.bn = static_cast<int>(bn);
+  const int stage_bytes = kABytes + (pl.bn / 2) * kBK * 2;
+  pl.tiles_n = static_cast<int>((N + 2 * kBM - 1) / (2 * kBM)) * 2;
+  pl.tiles_m = static_cast<int>((M + pl.bn - 1) / pl.bn);
+  const int pairs = (pl.tiles_n / 2) * pl.tiles_m;
+  const int kblocks = static_cast<int>((K + kBK - 1) / kBK);
+  const int sms = num_sms();
+  // at least the stages that hold the epilogue's fp32 partials; then as many as two CTAs
+  // per SM allow, or (wide tiles) as many as one CTA's shared memory allows
+  int stages = (pl.bn * kBM * 4 + stage_bytes - 1) / stage_bytes;
+  if (stages < 3) stages = 3;
+  const bool two = 2 * (smem_for(stages, stage_bytes) + 1024) <= static_cast<size_t>(kSmemPerSm);
+  while (stages < kMaxStages &&
+         (two ? 2 * (smem_for(stages + 1, stage_bytes) + 1024) <= static_cast<size_t>(kSmemPerSm)
+              : smem_for(stages + 1, stage_bytes) <= static_cast<size_t>(220 * 1024)))
+    ++stages;
+  pl.stages = stages;
+  pl.smem = smem_for(stages, stage_bytes);
+  const int per_sm = two ? 2 : 1;
+  pl.splits = 1;
+  for (int sp = kMaxSplits / 2 < kblocks ? kMaxSplits / 2 : kblocks; sp >= 2; --sp)
+    if (2 * pairs * sp <= per_sm * sms && recv_fits(pl.bn, sp, stages, stage_bytes) &&
+        pairs <= max_active_clusters(2 * sp, pl.smem)) {
       pl.splits = sp;
       break;
     }
@@ -892,12 +1032,14 @@ Plan plan_for(int64_t M, int64_t N, int64_t K, bool single_wave = false) {
   return pl;
 }
 
-uint32_t make_idesc(int bn) {
+// pair: the MMA spans both CTAs of a pair, M = 256 (128 rows in each)
+uint32_t make_idesc(int bn, bool pair = false) {
+  const int m = pair ? 2 * kBM : kBM;
   return (1u << 4)                                  // D format f32
          | (1u << 7)                                // A format bf16
          | (1u << 10)                               // B format bf16
          | (static_cast<uint32_t>(bn >> 3) << 17)   // N >> 3
-         | (static_cast<uint32_t>(kBM >> 4) << 24); // M >> 4
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M >> 4
 }
 
 }  // namespace
@@ -907,7 +1049,8 @@ using namespace lsb;
 
 extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
   LSB_REQUIRE(out && M > 0 && N > 0 && K > 0, "gemm_plan: bad arguments");
-  const Plan pl = plan_for(M, N, K);
+  const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
+  const Plan pl = force == kPlanPair ? pair_plan(M, N, K) : plan_for(M, N, K);
   out[0] = pl.bn;
   out[1] = pl.tiles_n * pl.tiles_m;
   out[2] = pl.splits;
@@ -917,7 +1060,7 @@ extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
 }
 
 extern "C" int lsb_gemm_force_plan(int32_t mode) {
-  LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanOnePerSm && (mode >> 4) < 8,
+  LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanPair && (mode >> 4) < 8,
               "gemm_force_plan: mode %d", mode);
   g_force_plan.store(mode, std::memory_order_relaxed);
   return LSB_OK;
@@ -987,14 +1130,17 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   // resident at once, so it keeps one CTA per SM and at most one wave.
   const int64_t kb1 = (K + kBK - 1) / kBK;
   const int64_t kb2 = (K2 + kBK - 1) / kBK;
-  Plan pl = plan_for(M, N, (kb1 + kb2) * kBK, comm != nullptr);
+  const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
+  Plan pl = force == kPlanPair && comm == nullptr ? pair_plan(M, N, (kb1 + kb2) * kBK)
+                                                  : plan_for(M, N, (kb1 + kb2) * kBK, comm != nullptr);
   CUtensorMap tw, tx, tw2, tx2;
-  const int bh = pl.bn / pl.halves;  // activation rows per TMA box and per MMA
+  const int bh = pl.bn / pl.halves;  // activation rows per MMA
+  const int xbox = pl.pair ? bh / 2 : bh;  // activation rows per TMA box (a pair CTA's half)
   if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
-  if (int rc = make_tmap(&tx, x, M, K, ldx, bh)) return rc;
+  if (int rc = make_tmap(&tx, x, M, K, ldx, xbox)) return rc;
   if (seg2) {  // each segment's last K block is zero-filled past its own width
     if (int rc = make_tmap(&tw2, static_cast<const bf16*>(w) + K, N, K2, ldw, kBM)) return rc;
-    if (int rc = make_tmap(&tx2, seg2->x2, M, K2, seg2->ldx2, bh)) return rc;
+    if (int rc = make_tmap(&tx2, seg2->x2, M, K2, seg2->ldx2, xbox)) return rc;
   } else {
     tw2 = tw;
     tx2 = tx;
@@ -1014,7 +1160,7 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   p.splits = pl.splits;
   p.epilogue = epilogue;
   p.flags = g_force_plan.load(std::memory_order_relaxed) >> 4;
-  p.idesc = make_idesc(bh);
+  p.idesc = make_idesc(bh, pl.pair);
   p.error_flag = lsb_device_error_flag();
   if (rope) p.rope = *rope;
   else memset(&p.rope, 0, sizeof(p.rope));
@@ -1026,12 +1172,14 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   } else {
     memset(&p.comm, 0, sizeof(p.comm));
   }
-  LSB_REQUIRE(recv_fits(pl.bn, pl.splits, pl.stages, kABytes + pl.bn * kBK * 2),
+  LSB_REQUIRE(recv_fits(pl.bn, pl.splits, pl.stages,
+                        kABytes + (pl.pair ? pl.bn / 2 : pl.bn) * kBK * 2),
               "gemm: plan leaves no room for the epilogue (bn=%d, splits=%d, stages=%d)", pl.bn,
               pl.splits, pl.stages);
-  const bool cluster = pl.splits > 1;
-  if (int rc = configure(cluster, epilogue, ar)) return rc;
-  Kernel kernel = kernel_for(cluster, epilogue, ar);
+  const bool cluster = pl.splits > 1 || pl.pair;
+  const int cluster_x = pl.pair ? 2 * pl.splits : pl.splits;
+  if (int rc = configure(cluster, epilogue, ar, pl.pair)) return rc;
+  Kernel kernel = kernel_for(cluster, epilogue, ar, pl.pair);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tiles_n * pl.splits, pl.tiles_m, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1042,9 +1190,9 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   attrs[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[nattr].val.programmaticStreamSerializationAllowed = 1;
   ++nattr;
-  if (pl.splits > 1) {
+  if (cluster_x > 1) {
     attrs[nattr].id = cudaLaunchAttributeClusterDimension;
-    attrs[nattr].val.clusterDim.x = pl.splits;
+    attrs[nattr].val.clusterDim.x = cluster_x;
     attrs[nattr].val.clusterDim.y = 1;
     attrs[nattr].val.clusterDim.z = 1;
     ++nattr;

@@ -349,13 +349,15 @@ def test_gemm(m: int, n: int, k: int) -> None:
     no_device_errors()
 
 
-@pytest.mark.parametrize("plan", [1, 2, 3])
+@pytest.mark.parametrize("plan", [1, 2, 3, 4])
 @pytest.mark.parametrize("m,n,k,epi", [
     (263, 6144, 2048, "none"), (300, 2048, 5632, "none"), (384, 1024, 2048, "swiglu"),
-    (289, 640, 352, "bias"), (143, 2048, 2048, "none")])
+    (289, 640, 352, "bias"), (143, 2048, 2048, "none"), (16, 2048, 2048, "none"),
+    (70, 11264, 2048, "swiglu")])
 def test_gemm_every_plan(plan: int, m: int, n: int, k: int, epi: str) -> None:
-    """Each tile plan (one wide tile with two MMA halves, 96-token tiles, one CTA per SM)
-    gives the oracle's product, fused epilogues included."""
+    """Each tile plan (one wide tile with two MMA halves, 96-token tiles, one CTA per SM,
+    256-row tiles on CTA pairs) gives the oracle's product, fused epilogues included (640
+    rows: the last pair's second CTA lies wholly past N)."""
     g = gen(m + n + k + plan)
     x = bf(torch.randn(m, k, generator=g))
     w = bf(torch.randn(n, k, generator=g) * 0.05)
