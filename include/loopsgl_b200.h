@@ -460,13 +460,13 @@ int lsb_comm_create(int32_t rank, int32_t world, void* const* buffers, int64_t m
                     lsb_comm** comm);
 int lsb_comm_destroy(lsb_comm* comm);
 /* All-reduce protocol of later calls on this communicator (every rank must choose the
- * same): 0 automatic (one hop for two ranks, else two), 1 one hop -- every rank stores its
+ * same): 0 automatic (per call: one hop for two ranks, and for three or four while a
+ * rank's one-hop sends stay within 1 MB; else two), 1 one hop -- every rank stores its
  * partial into every rank's buffer and sums all of them itself (at most 4 ranks; the
  * same bits on every rank), 2 two hops -- partials to the owner of each region, sums
- * back from it ((world - 1) / world of the bytes each way). The protocols use the
- * buffers differently: every rank's earlier calls must have completed (device
- * synchronise + a host barrier) before any rank's first call under the new one.
- * No counterpart in the reference (its NCCL picks the algorithm). */
+ * back from it ((world - 1) / world of the bytes each way). The two use separate parts
+ * of the buffers, so consecutive calls may use different ones. No counterpart in the
+ * reference (its NCCL picks the algorithm). */
 int lsb_comm_set_protocol(lsb_comm* comm, int32_t mode);
 
 /* In-place sum of x[rows, cols] (row stride ld) over the ranks: the reference's

@@ -78,9 +78,9 @@ class B200Communicator:
 
     def set_protocol(self, mode: int) -> None:
         """All-reduce protocol of later calls (collective: every rank sets the same): 0
-        automatic (one hop for two ranks), 1 one hop (at most 4 ranks), 2 two hops via region
-        owners. The protocols use the buffers differently, so every rank first finishes its
-        calls in flight (device synchronise + barrier)."""
+        automatic (one hop for two ranks, and for up to four while the bytes stay small), 1 one
+        hop (at most 4 ranks), 2 two hops via region owners. Every rank finishes its calls in
+        flight first (device synchronise + barrier), so the switch lands between calls."""
         torch.cuda.synchronize()
         dist.barrier(group=self._group)
         self._call("lsb_comm_set_protocol", self._comm, int(mode))

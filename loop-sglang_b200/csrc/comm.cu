@@ -140,7 +140,8 @@ extern "C" int lsb_comm_create(int32_t rank, int32_t world, void* const* buffers
   c->dev.rank = rank;
   c->dev.world = world;
   c->dev.max_elems = max_elems;
-  c->dev.oneshot = world == 2;  // one hop for two ranks (the same bytes, half the latency)
+  c->protocol = 0;
+  c->dev.oneshot = 0;  // set per call (comm_oneshot_for)
   for (int r = 0; r < kCommMaxWorld; ++r)
     c->dev.base[r] = r < world ? static_cast<uint8_t*>(buffers[r]) : nullptr;
   cudaGetDevice(&c->device);
@@ -152,7 +153,7 @@ extern "C" int lsb_comm_set_protocol(lsb_comm* comm, int32_t mode) {
   LSB_REQUIRE(comm && mode >= 0 && mode <= 2, "comm_set_protocol: bad arguments");
   LSB_REQUIRE(mode != 1 || comm->dev.world <= kOneShotMaxWorld,
               "comm_set_protocol: one-shot takes at most %d ranks", kOneShotMaxWorld);
-  comm->dev.oneshot = mode == 0 ? comm->dev.world == 2 : mode == 1;
+  comm->protocol = mode;
   return LSB_OK;
 }
 
@@ -174,8 +175,10 @@ extern "C" int lsb_allreduce(lsb_comm* comm, void* x, int64_t rows, int64_t cols
   if (row_tile < 1) row_tile = 1;
   while (tiles_n * ((rows + row_tile - 1) / row_tile) > kCommMaxRegions) row_tile *= 2;
   dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>((rows + row_tile - 1) / row_tile));
+  CommDev dev = comm->dev;
+  dev.oneshot = comm_oneshot_for(comm->protocol, dev.world, rows * cols);
   allreduce_kernel<<<grid, kCommThreads, 0, as_stream(stream)>>>(
-      comm->dev, static_cast<bf16*>(x), ld, static_cast<int>(rows), static_cast<int>(cols),
+      dev, static_cast<bf16*>(x), ld, static_cast<int>(rows), static_cast<int>(cols),
       static_cast<int>(row_tile), lsb_device_error_flag());
   return check_launch("lsb_allreduce");
 }

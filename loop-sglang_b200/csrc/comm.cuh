@@ -18,9 +18,10 @@
 // With up to four ranks the all-reduce can instead take one hop ("one-shot"): every
 // rank stores its partial as tagged words into its own slot on every rank, and every
 // rank sums all ranks' words of the region in rank order itself (identical bits
-// everywhere). The slots alternate with the epoch's parity (recv slots 4p .. 4p + 3):
-// a rank that finished call k has every peer's partials of call k, so every peer has
-// finished call k - 1 and no longer reads the slots call k + 1 writes.
+// everywhere). The slots alternate with the epoch's parity (recv slots 4 + 4p .. 7 + 4p,
+// apart from the two-hop slots 0 .. world - 1, so calls may switch protocols freely): a
+// rank that finished call k has every peer's data of call k, so every peer has finished
+// call k - 1 and no longer reads what call k + 1 writes.
 // The all-gather keeps per-region flags (release/acquire at system scope). Every wait is
 // bounded and reports LSB_DEVERR_COMM_TIMEOUT instead of hanging.
 #pragma once
@@ -44,10 +45,12 @@ constexpr int64_t kCommOpBytes = kCommFlagBytes + kCommDoneBytes;
 constexpr int64_t kCommDataOff = kCommFlagsOff + kCommOps * kCommOpBytes;
 
 constexpr int kOneShotMaxWorld = 4;
+// recv slots: two hops use 0 .. world - 1, one hop 4 .. 11 (two parities of 4)
+constexpr int kCommRecvSlots = 12;
 
 struct CommDev {
   int rank, world;
-  int oneshot;        // all-reduce in one hop (world <= kOneShotMaxWorld), else via owners
+  int oneshot;        // this call's all-reduce in one hop (world <= kOneShotMaxWorld)
   int64_t max_elems;  // bf16 elements of one recv slot / the result area / one gather slot
   uint8_t* base[kCommMaxWorld];
 
@@ -68,22 +71,33 @@ struct CommDev {
   }
   // one-shot slot of source `src` on rank r for calls of epoch parity `par`
   __device__ __forceinline__ uint64_t* oneshot_slot(int r, int src, uint32_t par) const {
-    return recv(r, kOneShotMaxWorld * static_cast<int>(par & 1u) + src);
+    return recv(r, kOneShotMaxWorld * (1 + static_cast<int>(par & 1u)) + src);
   }
   __device__ __forceinline__ uint64_t* result(int r) const {
     return reinterpret_cast<uint64_t*>(base[r] + kCommDataOff) +
-           static_cast<int64_t>(kCommMaxWorld) * (max_elems / 2);
+           static_cast<int64_t>(kCommRecvSlots) * (max_elems / 2);
   }
   // all-gather slot `src` of rank r for calls of epoch parity `par`: a rank can run
   // at most one all-gather ahead of a peer that is still copying out of its slots
   __device__ __forceinline__ uint8_t* gather(int r, int src, int par) const {
-    return base[r] + kCommDataOff + (static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 4 +
+    return base[r] + kCommDataOff + (static_cast<int64_t>(kCommRecvSlots) + 1) * max_elems * 4 +
            static_cast<int64_t>(par * kCommMaxWorld + src) * max_elems * 2;
   }
 };
 
+// One hop or two for an all-reduce of `elems` bf16 per rank under protocol `mode` (0
+// automatic, 1 one hop, 2 two hops). Automatic: one hop for two ranks (the same bytes as
+// two hops in half the latency); for three or four while each rank's one-hop sends, (world
+// - 1) x elems x 2 bytes, stay within 1 MB (measured on four B200s: one hop 8.9 vs 10.2 us
+// at 16 x 2048 elements, two hops 25.5 vs 29.3 us at 256 x 2048); else two.
+inline int comm_oneshot_for(int mode, int world, int64_t elems) {
+  if (world > kOneShotMaxWorld || mode == 2) return 0;
+  if (mode == 1 || world == 2) return 1;
+  return static_cast<int64_t>(world - 1) * elems * 2 <= (int64_t(1) << 20) ? 1 : 0;
+}
+
 inline int64_t comm_buffer_bytes(int64_t max_elems) {
-  return kCommDataOff + (static_cast<int64_t>(kCommMaxWorld) + 1) * max_elems * 4 +
+  return kCommDataOff + (static_cast<int64_t>(kCommRecvSlots) + 1) * max_elems * 4 +
          2 * static_cast<int64_t>(kCommMaxWorld) * max_elems * 2;
 }
 
@@ -282,4 +296,5 @@ __device__ __forceinline__ void comm_complete(const CommDev& c, int owner, uint3
 struct lsb_comm {
   lsb::CommDev dev;
   int device;
+  int protocol;  // lsb_comm_set_protocol mode; dev.oneshot is set per call from it
 };

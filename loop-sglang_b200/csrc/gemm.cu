@@ -1167,6 +1167,7 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   const bool ar = comm != nullptr;
   if (ar) {
     p.comm = comm->dev;
+    p.comm.oneshot = comm_oneshot_for(comm->protocol, comm->dev.world, M * N);
     LSB_REQUIRE(static_cast<int64_t>(pl.tiles_n) * pl.splits * pl.tiles_m <= kCommMaxRegions,
                 "gemm_allreduce: too many tiles");
   } else {

@@ -227,7 +227,10 @@ def bench_gemm_ar(args, ops, comm, name: str, nccl=None) -> dict:
     dist.barrier()
     us_allreduce = _time_graph(lambda i: comm.all_reduce(y), args.reps)
     comm.set_protocol(0)
-    oneshot = args.protocol == 1 or (args.protocol == 0 and tp == 2)
+    # the library's automatic rule (comm_oneshot_for): one hop for two ranks, and for up
+    # to four while each rank's one-hop sends stay within 1 MB
+    oneshot = args.protocol == 1 or (args.protocol == 0 and (
+        tp == 2 or (tp <= 4 and (tp - 1) * m * n * 2 <= 1 << 20)))
     us_nccl = us_cublas = 0.0
     if nccl is not None:
         # the reference's path: F.linear (cuBLAS) then an NCCL all-reduce of the result
