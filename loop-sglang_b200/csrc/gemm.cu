@@ -707,6 +707,281 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // ---------------------------------------------------------------------------
+// Persistent variant for token counts in the thousands (prefill): one CTA per SM walks
+// its share of the (128-row weight tile, 256-token tile) grid. The producer and MMA warps
+// run ahead over tile boundaries (one ring of stages for all tiles), and two TMEM
+// accumulators of 256 columns alternate, so warps 4..7 drain tile j -- straight from
+// TMEM to registers to global memory, no shared-memory staging -- while tile j + 1's
+// main loop runs. The K loop of a tile starts at the same rotated block as the
+// single-tile kernel's, so both give the same bits. Row-pair epilogues (SwiGLU: gate row
+// r with up row r + 64; RoPE: dim i with dim i + 64) swap 16-column chunks between the
+// warps of lanes 0-63 and 64-127 through a small shared buffer.
+// ---------------------------------------------------------------------------
+constexpr int kPersistBn = 256;
+constexpr int kPersistStage = kABytes + kPersistBn * kBK * 2;  // 48 KB
+constexpr int kPersistXchFloats = 2 * 2 * 2 * 16 * 32;         // [pair][side][buffer][16][32]
+constexpr int kPersistMinTokens = 1024;
+
+__device__ __forceinline__ void pair_sync(int id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                           const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = p.stages;
+  float* const xch = reinterpret_cast<float*>(smem + stages * kPersistStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xch + kPersistXchFloats);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* acc_full = empty + kMaxStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  int* const epi_ok = reinterpret_cast<int*>(tmem_slot + 1);  // [4]: per epilogue warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_n = (p.N + kBM - 1) / kBM, tiles_m = (p.M + kPersistBn - 1) / kPersistBn;
+  const int tiles = tiles_n * tiles_m;
+  const int kblocks = (p.K + kBK - 1) / kBK;
+  // tile t: weight tile t / tiles_m, token tile t % tiles_m (CTAs running together share
+  // weight tiles in L2)
+  auto rot_of = [&](int tn, int tm) {
+    return (p.flags & kFlagNoRotate) ? 0
+                                     : static_cast<int>((static_cast<int64_t>(tn) * 7 + tm * 3) % kblocks);
+  };
+
+  asm volatile("griddepcontrol.launch_dependents;");
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)));
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)));
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(2 * kPersistBn));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;");
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // ring position over all tiles
+      bool waited = false;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        const int tn = t / tiles_m, tm = t - tn * tiles_m;
+        const int rot = rot_of(tn, tm);
+        bool ok = true;
+        for (int i = 0; i < kblocks; ++i, ++g) {
+          const int s = g % stages;
+          const uint32_t round = static_cast<uint32_t>(g / stages);
+          if (g >= stages && !mbar_wait(&empty[s], (round & 1u) ^ 1u, p.error_flag)) {
+            ok = false;
+            break;
+          }
+          const int kb = (i + rot) % kblocks;
+          uint8_t* a_tile = smem + s * kPersistStage;
+          mbar_expect_tx(&full[s], static_cast<uint32_t>(kPersistStage));
+          tma_load_2d(a_tile, &tmap_w, &full[s], kb * kBK, tn * kBM);
+          if (!waited) {  // weights need nothing from the previous kernel; x does
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            waited = true;
+          }
+          tma_load_2d(a_tile + kABytes, &tmap_x, &full[s], kb * kBK, tm * kPersistBn);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int g = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++j) {
+        const int b = j & 1;
+        // accumulator b is free once the epilogue drained tile j - 2
+        if (j >= 2 && !mbar_wait(&acc_empty[b], static_cast<uint32_t>((j >> 1) - 1) & 1u,
+                                 p.error_flag)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint32_t d = tmem_base + static_cast<uint32_t>(b * kPersistBn);
+        for (int i = 0; i < kblocks; ++i, ++g) {
+          const int s = g % stages;
+          const uint32_t round = static_cast<uint32_t>(g / stages);
+          if (!mbar_wait(&full[s], round & 1u, p.error_flag)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;");
+          const uint8_t* a_tile = smem + s * kPersistStage;
+          const uint64_t adesc = smem_desc(a_tile), bdesc = smem_desc(a_tile + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, p.idesc, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp >= 4) {
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q + 31: weight rows of this warp
+    const int row = 32 * q + lane;
+    constexpr bool kPairRows = EPI == LSB_EPI_SWIGLU || EPI == kEpiRope;
+    const int pr = q & 1;  // warp pair (q, q + 2) for the row-pair epilogues
+    const bool low = q < 2;
+    int j = 0, chunk = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
+      const int b = j & 1;
+      const int tn = t / tiles_m, tm = t - tn * tiles_m;
+      // the four epilogue warps give up together (the row-pair exchange below waits on
+      // hardware barriers between them, which have no bound of their own)
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>(j >> 1) & 1u,
+                                                          p.error_flag));
+      if (lane == 0) epi_ok[q] = got ? 1 : 0;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const bool ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;");
+      const int n0 = tn * kBM, m0 = tm * kPersistBn;
+      const int n = n0 + row;
+      const int tokens = p.M - m0 < kPersistBn ? p.M - m0 : kPersistBn;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(32 * q) << 16) +
+                             static_cast<uint32_t>(b * kPersistBn);
+      float bias = 0.f;
+      if ((EPI == LSB_EPI_BIAS || EPI == LSB_EPI_BIAS_AFTER_ROUND) && n < p.N)
+        bias = __bfloat162float(p.bias[n]);
+      for (int c0 = 0; c0 < tokens; c0 += 16, ++chunk) {
+        uint32_t v[16];
+        tmem_ld16_issue(taddr + static_cast<uint32_t>(c0), v);
+        tmem_ld_wait();
+        if (!kPairRows) {
+          if (n < p.N) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              if (c0 + jj >= tokens) break;
+              float o = __uint_as_float(v[jj]);
+              if (EPI == LSB_EPI_BIAS) o += bias;
+              if (EPI == LSB_EPI_BIAS_AFTER_ROUND) o = round_bf16(o) + bias;
+              p.y[static_cast<int64_t>(m0 + c0 + jj) * p.ldy + n] = __float2bfloat16_rn(o);
+            }
+          }
+          continue;
+        }
+        // row pairs: swap this chunk with the partner warp (rows 64 apart)
+        const int db = chunk & 1;
+        float* mine = xch + (((pr * 2 + (low ? 0 : 1)) * 2 + db) * 16) * 32;
+        const float* theirs = xch + (((pr * 2 + (low ? 1 : 0)) * 2 + db) * 16) * 32;
+        if (EPI == LSB_EPI_SWIGLU) {
+          // the gate warp finishes columns 0..7 of the chunk, the up warp columns 8..15:
+          // each hands the other the half it needs
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) mine[jj * 32 + lane] = __uint_as_float(v[low ? 8 + jj : jj]);
+          pair_sync(2 + pr);
+          const int col = tn * 64 + (row & 63);
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            const int c = low ? jj : 8 + jj;
+            if (c0 + c >= tokens) break;
+            const float own = round_bf16(__uint_as_float(v[c]));
+            const float other = round_bf16(theirs[jj * 32 + lane]);
+            const float out = low ? silu_mul(own, other) : silu_mul(other, own);
+            if (col < p.N / 2)
+              p.y[static_cast<int64_t>(m0 + c0 + c) * p.ldy + col] = __float2bfloat16_rn(out);
+          }
+          continue;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) mine[jj * 32 + lane] = __uint_as_float(v[jj]);
+        pair_sync(2 + pr);
+        // RoPE (128-dim heads, one per weight tile): dim i = row & 63 of head tn. The
+        // chunk's 16 positions and slots come in with one load (lanes 0..15) and
+        // shuffles, and every cos / sin load is issued before the first is used.
+        const RopeParams& rp = p.rope;
+        const int head = tn;
+        const int i = row & 63;
+        const bool rotate = head < rp.hq + rp.hkv;
+        const bool kv = head >= rp.hq;
+        int my_pos = 0;
+        int64_t my_loc = 0;
+        if (lane < 16 && c0 + lane < tokens) {
+          if (rotate) my_pos = rp.positions[m0 + c0 + lane];
+          if (kv) my_loc = rp.out_loc[m0 + c0 + lane];
+        }
+        if (rotate && (my_pos < 0 || my_pos >= rp.max_pos)) {
+          if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_POSITION);
+          my_pos = 0;
+        }
+        float cz[16], sz[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int pos = __shfl_sync(0xffffffffu, my_pos, jj);
+          cz[jj] = sz[jj] = 0.f;
+          if (rotate) {
+            cz[jj] = __ldg(rp.cos_sin + static_cast<int64_t>(pos) * 128 + i);
+            sz[jj] = __ldg(rp.cos_sin + static_cast<int64_t>(pos) * 128 + 64 + i);
+          }
+        }
+        bf16* cache = nullptr;
+        if (kv) {
+          const bool is_k = head < rp.hq + rp.hkv;
+          const int kvh = is_k ? head - rp.hq : head - rp.hq - rp.hkv;
+          cache = (is_k ? rp.k_cache : rp.v_cache) + static_cast<int64_t>(kvh) * 128 + row;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int64_t loc = __shfl_sync(0xffffffffu, my_loc, jj);
+          if (c0 + jj >= tokens) continue;
+          const int64_t tok = m0 + c0 + jj;
+          const float own = round_bf16(__uint_as_float(v[jj]));
+          const float other = round_bf16(theirs[jj * 32 + lane]);
+          float out = own;
+          if (rotate) {
+            float y1, y2;
+            if (low) rope_rotate(own, other, cz[jj], sz[jj], y1, y2);
+            else rope_rotate(other, own, cz[jj], sz[jj], y1, y2);
+            out = low ? y1 : y2;
+          }
+          const bf16 ob = __float2bfloat16_rn(out);
+          p.y[tok * p.ldy + n] = ob;
+          if (kv && loc != 0) {  // k and v heads: their slot too (slot 0 is padding)
+            if (loc < 0 || loc >= rp.num_slots) {
+              if (p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+            } else {
+              cache[loc * rp.slot_stride] = ob;
+            }
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * kPersistBn));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -884,7 +1159,53 @@ size_t smem_for(int stages, int stage_bytes) {
 // main loop. A split is only used when all clusters of the grid run at once; a
 // cluster left for a second wave would double the kernel's time.
 // Plans lsb_gemm_force_plan can select (automatic otherwise).
-constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3, kPlanPair = 4;
+constexpr int kPlanAuto = 0, kPlanWide = 1, kPlanNarrow = 2, kPlanOnePerSm = 3, kPlanPair = 4,
+              kPlanPersistent = 5, kPlanClassic = 6;
+
+// The persistent kernel (see above) serves calls of at least kPersistMinTokens tokens
+// without a fused all-reduce, a second activation segment or the argmax epilogue.
+using PersistKernel = void (*)(const CUtensorMap, const CUtensorMap, GemmParams);
+
+PersistKernel persistent_kernel_for(int epilogue) {
+  static const PersistKernel k[kEpiKinds] = {
+      gemm_persistent_kernel<LSB_EPI_NONE>, gemm_persistent_kernel<LSB_EPI_BIAS>,
+      gemm_persistent_kernel<LSB_EPI_BIAS_AFTER_ROUND>, gemm_persistent_kernel<LSB_EPI_SWIGLU>,
+      nullptr, gemm_persistent_kernel<kEpiRope>};
+  return k[epilogue];
+}
+
+size_t persistent_smem(int stages) {
+  return 1024 + static_cast<size_t>(stages) * kPersistStage + kPersistXchFloats * 4 +
+         (2 * kMaxStages + 4) * 8 + 64;
+}
+
+// Automatic: at least kPersistMinTokens tokens and a tile for every SM (fewer tiles leave
+// SMs idle that the single-tile kernel's split-K would use), plain or bias epilogues only:
+// the row-pair epilogues on four warps take longer than a tile's main loop, so they no
+// longer hide behind it (8256 tokens: SwiGLU 465 vs 447 us, RoPE + KV store 474 vs 313 us
+// for the single-tile kernel, against plain qkv 168 vs 222-320 us).
+bool use_persistent(int64_t M, int64_t N, int epilogue, bool comm, bool seg2) {
+  const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
+  if (comm || seg2 || epilogue == kEpiArgmax || force == kPlanClassic) return false;
+  const int64_t tiles = ((N + kBM - 1) / kBM) * ((M + kPersistBn - 1) / kPersistBn);
+  return force == kPlanPersistent ||
+         (force == kPlanAuto && M >= kPersistMinTokens && tiles >= num_sms() &&
+          epilogue != LSB_EPI_SWIGLU && epilogue != kEpiRope);
+}
+
+int configure_persistent(int epilogue) {
+  static std::mutex mu;
+  static uint32_t done[64] = {0};
+  int dev = 0;
+  LSB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && (done[dev] & (1u << epilogue))) return LSB_OK;
+  LSB_CUDA(cudaFuncSetAttribute(persistent_kernel_for(epilogue),
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem));
+  if (dev < 64) done[dev] |= 1u << epilogue;
+  return LSB_OK;
+}
+
 // Token counts a single wide tile (two MMA halves) covers: its fp32 partials, about
 // bn x 128 x 4 bytes, must fit in the drained stage buffers of one CTA's shared memory.
 constexpr int kWideMax = 384;
@@ -1050,6 +1371,17 @@ using namespace lsb;
 extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
   LSB_REQUIRE(out && M > 0 && N > 0 && K > 0, "gemm_plan: bad arguments");
   const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
+  if (use_persistent(M, N, LSB_EPI_NONE, false, false)) {  // one CTA per SM over all tiles
+    const int64_t tiles = ((N + kBM - 1) / kBM) * ((M + kPersistBn - 1) / kPersistBn);
+    int stages = kMaxStages;
+    while (stages > 2 && persistent_smem(stages) > static_cast<size_t>(kMaxSmem)) --stages;
+    out[0] = kPersistBn;
+    out[1] = static_cast<int32_t>(tiles);
+    out[2] = 1;
+    out[3] = stages;
+    out[4] = static_cast<int32_t>(persistent_smem(stages));
+    return LSB_OK;
+  }
   const Plan pl = force == kPlanPair ? pair_plan(M, N, K) : plan_for(M, N, K);
   out[0] = pl.bn;
   out[1] = pl.tiles_n * pl.tiles_m;
@@ -1060,7 +1392,7 @@ extern "C" int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out) {
 }
 
 extern "C" int lsb_gemm_force_plan(int32_t mode) {
-  LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanPair && (mode >> 4) < 8,
+  LSB_REQUIRE((mode & 15) >= kPlanAuto && (mode & 15) <= kPlanClassic && (mode >> 4) < 8,
               "gemm_force_plan: mode %d", mode);
   g_force_plan.store(mode, std::memory_order_relaxed);
   return LSB_OK;
@@ -1130,6 +1462,47 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
   // resident at once, so it keeps one CTA per SM and at most one wave.
   const int64_t kb1 = (K + kBK - 1) / kBK;
   const int64_t kb2 = (K2 + kBK - 1) / kBK;
+  if (use_persistent(M, N, epilogue, comm != nullptr, seg2 != nullptr)) {
+    CUtensorMap tw, tx;
+    if (int rc = make_tmap(&tw, w, N, K, ldw, kBM)) return rc;
+    if (int rc = make_tmap(&tx, x, M, K, ldx, kPersistBn)) return rc;
+    int stages = kMaxStages;
+    while (stages > 2 && persistent_smem(stages) > static_cast<size_t>(kMaxSmem)) --stages;
+    GemmParams p;
+    memset(&p, 0, sizeof(p));
+    p.y = static_cast<bf16*>(y);
+    p.ldy = ldy;
+    p.bias = static_cast<const bf16*>(bias);
+    p.M = static_cast<int>(M);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(kb1 * kBK);
+    p.kb1 = static_cast<int>(kb1);
+    p.bn = kPersistBn;
+    p.bh = kPersistBn;
+    p.halves = 1;
+    p.stages = stages;
+    p.splits = 1;
+    p.epilogue = epilogue;
+    p.flags = g_force_plan.load(std::memory_order_relaxed) >> 4;
+    p.idesc = make_idesc(kPersistBn);
+    p.error_flag = lsb_device_error_flag();
+    if (rope) p.rope = *rope;
+    if (int rc = configure_persistent(epilogue)) return rc;
+    const int64_t tiles = ((N + kBM - 1) / kBM) * ((M + kPersistBn - 1) / kPersistBn);
+    LSB_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles < num_sms() ? tiles : num_sms()), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = persistent_smem(stages);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    LSB_CUDA(cudaLaunchKernelEx(&cfg, persistent_kernel_for(epilogue), tw, tx, p));
+    return check_launch("lsb_gemm (persistent)");
+  }
   const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
   Plan pl = force == kPlanPair && comm == nullptr ? pair_plan(M, N, (kb1 + kb2) * kBK)
                                                   : plan_for(M, N, (kb1 + kb2) * kBK, comm != nullptr);

@@ -174,6 +174,17 @@ def bench_gemm(args, ops, name: str) -> dict:
     def launch(i):
         ops.gemm(x, ws[i % copies], None, epi, out=y)
 
+    if args.rope and name == "qkv":  # the QKV projection with RoPE + KV store fused
+        hq, hkv, d = n // 3 // 128, n // 3 // 128, 128
+        pos = torch.randint(0, 4000, (m,), dtype=torch.int32, device=dev)
+        cs = torch.randn(4096, d, device=dev)
+        loc = torch.randperm(2 * m, device=dev)[:m].to(torch.int32) + 1
+        kc = torch.empty(2 * m + 2, hkv * d, dtype=torch.bfloat16, device=dev)
+        vc = torch.empty_like(kc)
+
+        def launch(i):  # noqa: F811
+            ops.gemm_rope_store(x, ws[i % copies], pos, cs, hq, hkv, d, kc, vc, loc, out=y)
+
     if args.cublas_only:  # a process that launches only cuBLAS's kernel (profiler captures)
         yc = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
         us_c = _time_graph(lambda i: torch.matmul(x, ws[i % copies].t(), out=yc), args.reps)
@@ -346,6 +357,8 @@ def main(argv=None) -> None:
     gm.add_argument("--tp", type=int, default=1, help="per-rank shard shapes of this TP size")
     gm.add_argument("--cublas", action="store_true",
                     help="also time torch.matmul (cuBLAS) on the same shapes and weights")
+    gm.add_argument("--rope", action="store_true",
+                    help="qkv through the RoPE + KV store epilogue (gemm_rope_store)")
     gm.add_argument("--n", type=int, default=0, help="override the shape's output rows")
     gm.add_argument("--k", type=int, default=0, help="override the shape's reduction size")
     gm.add_argument("--tile", type=int, nargs="+", default=[0],

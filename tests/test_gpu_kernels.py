@@ -379,6 +379,81 @@ def test_gemm_every_plan(plan: int, m: int, n: int, k: int, epi: str) -> None:
     no_device_errors()
 
 
+def _with_plan(mode: int, fn):
+    check(ops.lib().lsb_gemm_force_plan(mode), "force_plan")
+    try:
+        return fn()
+    finally:
+        check(ops.lib().lsb_gemm_force_plan(0), "force_plan")
+
+
+@pytest.mark.parametrize("m,n,k,epi", [
+    (1024, 6144, 2048, "none"), (1100, 640, 352, "bias"), (1300, 1024, 2048, "swiglu"),
+    (2100, 2000, 1024, "bias_after_round"), (300, 2048, 5632, "none"), (8256, 2048, 704, "none")])
+def test_gemm_persistent_matches_oracle_and_single_tile_kernel(m: int, n: int, k: int,
+                                                               epi: str) -> None:
+    """The persistent kernel (one CTA per SM over all tiles, two TMEM accumulators):
+    the oracle's product with every epilogue, ragged token and weight tiles included, and
+    the single-tile kernel's exact bits wherever that kernel's plan cuts the same 256-token
+    tiles without split-K (then every output sums its K blocks in the same order)."""
+    g = gen(m * 3 + n + k)
+    x = bf(torch.randn(m, k, generator=g))
+    w = bf(torch.randn(n, k, generator=g) * 0.05)
+    b = bf(torch.randn(n, generator=g))
+    xd, wd, bd = x.to(DEV), w.to(DEV), b.to(DEV)
+    if epi == "swiglu":
+        wi = ops.swiglu_interleave(wd)
+        run = lambda: ops.gemm(xd, wi, epilogue=ops.LSB_EPI_SWIGLU)  # noqa: E731
+        ref = O.silu_and_mul(O.linear(x, w))
+    elif epi == "bias":
+        run = lambda: ops.gemm(xd, wd, bd, ops.LSB_EPI_BIAS)  # noqa: E731
+        ref = O.linear(x, w, b)
+    elif epi == "bias_after_round":
+        run = lambda: ops.gemm(xd, wd, bd, ops.LSB_EPI_BIAS_AFTER_ROUND)  # noqa: E731
+        ref = O.linear_bias_after_rounding(x, w, b)
+    else:
+        run = lambda: ops.gemm(xd, wd)  # noqa: E731
+        ref = O.linear(x, w)
+    got = [_with_plan(5, run) for _ in range(2)]
+    assert torch.equal(got[0], got[1])
+    close(got[0], ref)
+    classic = _with_plan(6, run)
+    plan = _with_plan(6, lambda: ops.gemm_plan(m, n, k))
+    if plan["splits"] == 1 and plan["tokens_per_tile"] == 256:
+        assert torch.equal(got[0], classic)
+    else:
+        close(got[0], classic.float().cpu())
+    no_device_errors()
+
+
+def test_gemm_persistent_rope_store_equals_single_tile_kernel() -> None:
+    """The QKV projection with RoPE + KV store at a prefill's token count: the persistent
+    kernel's row-pair exchange gives the single-tile kernel's bits, output and caches."""
+    g = gen(77)
+    hq, hkv, d, k, m = 16, 4, 128, 2048, 1024
+    n = (hq + 2 * hkv) * d
+    x = bf(torch.randn(m, k, generator=g)).to(DEV)
+    w = bf(torch.randn(n, k, generator=g) * 0.02).to(DEV)
+    pos = torch.randint(0, 4000, (m,), generator=g, dtype=torch.int32).to(DEV)
+    cs = O.rope_cos_sin_cache(d, 4096, 1e6).to(DEV)
+    slots = 2 * m + 8
+    loc = (torch.randperm(slots - 1, generator=g)[:m] + 1).to(torch.int32)
+    loc[::5] = 0
+    loc = loc.to(DEV)
+    kc0 = bf(torch.randn(slots, hkv * d, generator=g)).to(DEV)
+    vc0 = bf(torch.randn(slots, hkv * d, generator=g)).to(DEV)
+    outs = []
+    for mode in (5, 6):
+        kc, vc = kc0.clone(), vc0.clone()
+        qkv = _with_plan(mode, lambda: ops.gemm_rope_store(x, w, pos, cs, hq, hkv, d, kc, vc, loc))
+        outs.append((qkv, kc, vc))
+    plan = _with_plan(6, lambda: ops.gemm_plan(m, n, k))
+    assert plan["splits"] == 1 and plan["tokens_per_tile"] == 256
+    for a, c in zip(outs[0], outs[1]):
+        assert torch.equal(a, c)
+    no_device_errors()
+
+
 @pytest.mark.parametrize("epi", ["bias", "bias_after_round", "swiglu"])
 @pytest.mark.parametrize("m", [5, 144, 263])
 def test_gemm_epilogues(epi: str, m: int) -> None:
