@@ -711,15 +711,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 // its share of the (128-row weight tile, 256-token tile) grid. The producer and MMA warps
 // run ahead over tile boundaries (one ring of stages for all tiles), and two TMEM
 // accumulators of 256 columns alternate, so warps 4..7 drain tile j -- straight from
-// TMEM to registers to global memory, no shared-memory staging -- while tile j + 1's
-// main loop runs. The K loop of a tile starts at the same rotated block as the
+// TMEM to registers to global memory, no shared-memory staging, two warps per TMEM lane
+// quarter taking alternate 16-column chunks -- while tile j + 1's main loop runs. The K loop of a tile starts at the same rotated block as the
 // single-tile kernel's, so both give the same bits. Row-pair epilogues (SwiGLU: gate row
 // r with up row r + 64; RoPE: dim i with dim i + 64) swap 16-column chunks between the
 // warps of lanes 0-63 and 64-127 through a small shared buffer.
 // ---------------------------------------------------------------------------
 constexpr int kPersistBn = 256;
 constexpr int kPersistStage = kABytes + kPersistBn * kBK * 2;  // 48 KB
-constexpr int kPersistXchFloats = 2 * 2 * 2 * 16 * 32;         // [pair][side][buffer][16][32]
+// [column half][pair][side][buffer][16][32]
+constexpr int kPersistXchFloats = 2 * 2 * 2 * 2 * 16 * 32;
+constexpr int kPersistThreads = 384;  // warps 4..11 drain: two per TMEM lane quarter
 constexpr int kPersistMinTokens = 1024;
 
 __device__ __forceinline__ void pair_sync(int id) {
@@ -727,7 +729,7 @@ __device__ __forceinline__ void pair_sync(int id) {
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kPersistThreads, 1)
     gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmap_w,
                            const __grid_constant__ CUtensorMap tmap_x, GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -740,7 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + kMaxStages;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  int* const epi_ok = reinterpret_cast<int*>(tmem_slot + 1);  // [4]: per epilogue warp
+  int* const epi_ok = reinterpret_cast<int*>(tmem_slot + 1);  // [8]: per epilogue warp
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = (p.N + kBM - 1) / kBM, tiles_m = (p.M + kPersistBn - 1) / kPersistBn;
   const int tiles = tiles_n * tiles_m;
@@ -760,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_w)));
@@ -839,22 +841,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     const int q = warp & 3;  // TMEM lanes 32q .. 32q + 31: weight rows of this warp
+    const int hsel = (warp - 4) >> 2;  // this warp's 16-column chunks: hsel, hsel + 2, ...
+    const int ew = warp - 4;           // epilogue warp index 0..7
     const int row = 32 * q + lane;
     constexpr bool kPairRows = EPI == LSB_EPI_SWIGLU || EPI == kEpiRope;
-    const int pr = q & 1;  // warp pair (q, q + 2) for the row-pair epilogues
+    const int pr = q & 1;  // warp pair (q, q + 2) of the same chunks for row-pair epilogues
     const bool low = q < 2;
     int j = 0, chunk = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++j) {
       const int b = j & 1;
       const int tn = t / tiles_m, tm = t - tn * tiles_m;
-      // the four epilogue warps give up together (the row-pair exchange below waits on
+      // the eight epilogue warps give up together (the row-pair exchange below waits on
       // hardware barriers between them, which have no bound of their own)
       const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[b], static_cast<uint32_t>(j >> 1) & 1u,
                                                           p.error_flag));
-      if (lane == 0) epi_ok[q] = got ? 1 : 0;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      const bool ok = epi_ok[0] && epi_ok[1] && epi_ok[2] && epi_ok[3];
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (lane == 0) epi_ok[ew] = got ? 1 : 0;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      bool ok = true;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ok = ok && epi_ok[e];
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (!ok) break;
       asm volatile("tcgen05.fence::after_thread_sync;");
       const int n0 = tn * kBM, m0 = tm * kPersistBn;
@@ -865,7 +871,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float bias = 0.f;
       if ((EPI == LSB_EPI_BIAS || EPI == LSB_EPI_BIAS_AFTER_ROUND) && n < p.N)
         bias = __bfloat162float(p.bias[n]);
-      for (int c0 = 0; c0 < tokens; c0 += 16, ++chunk) {
+      for (int c0 = 16 * hsel; c0 < tokens; c0 += 32, ++chunk) {
         uint32_t v[16];
         tmem_ld16_issue(taddr + static_cast<uint32_t>(c0), v);
         tmem_ld_wait();
@@ -884,14 +890,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // row pairs: swap this chunk with the partner warp (rows 64 apart)
         const int db = chunk & 1;
-        float* mine = xch + (((pr * 2 + (low ? 0 : 1)) * 2 + db) * 16) * 32;
-        const float* theirs = xch + (((pr * 2 + (low ? 1 : 0)) * 2 + db) * 16) * 32;
+        float* mine = xch + ((((hsel * 2 + pr) * 2 + (low ? 0 : 1)) * 2 + db) * 16) * 32;
+        const float* theirs = xch + ((((hsel * 2 + pr) * 2 + (low ? 1 : 0)) * 2 + db) * 16) * 32;
         if (EPI == LSB_EPI_SWIGLU) {
           // the gate warp finishes columns 0..7 of the chunk, the up warp columns 8..15:
           // each hands the other the half it needs
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) mine[jj * 32 + lane] = __uint_as_float(v[low ? 8 + jj : jj]);
-          pair_sync(2 + pr);
+          pair_sync(2 + pr + 2 * hsel);
           const int col = tn * 64 + (row & 63);
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
@@ -907,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) mine[jj * 32 + lane] = __uint_as_float(v[jj]);
-        pair_sync(2 + pr);
+        pair_sync(2 + pr + 2 * hsel);
         // RoPE (128-dim heads, one per weight tile): dim i = row & 63 of head tn. The
         // chunk's 16 positions and slots come in with one load (lanes 0..15) and
         // shuffles, and every cos / sin load is issued before the first is used.
@@ -1180,17 +1186,15 @@ size_t persistent_smem(int stages) {
 }
 
 // Automatic: at least kPersistMinTokens tokens and a tile for every SM (fewer tiles leave
-// SMs idle that the single-tile kernel's split-K would use), plain or bias epilogues only:
-// the row-pair epilogues on four warps take longer than a tile's main loop, so they no
-// longer hide behind it (8256 tokens: SwiGLU 465 vs 447 us, RoPE + KV store 474 vs 313 us
-// for the single-tile kernel, against plain qkv 168 vs 222-320 us).
+// SMs idle that the single-tile kernel's split-K would use). Measured at 8256 tokens
+// against the single-tile kernel: qkv 171 vs 236 us, qkv with RoPE + KV store 295 vs 316,
+// o_proj 72 vs 86, gate_up + SwiGLU 412 vs 458, down_proj 180 vs 203.
 bool use_persistent(int64_t M, int64_t N, int epilogue, bool comm, bool seg2) {
   const int force = g_force_plan.load(std::memory_order_relaxed) & 15;
   if (comm || seg2 || epilogue == kEpiArgmax || force == kPlanClassic) return false;
   const int64_t tiles = ((N + kBM - 1) / kBM) * ((M + kPersistBn - 1) / kPersistBn);
   return force == kPlanPersistent ||
-         (force == kPlanAuto && M >= kPersistMinTokens && tiles >= num_sms() &&
-          epilogue != LSB_EPI_SWIGLU && epilogue != kEpiRope);
+         (force == kPlanAuto && M >= kPersistMinTokens && tiles >= num_sms());
 }
 
 int configure_persistent(int epilogue) {
@@ -1492,7 +1496,7 @@ static int gemm_impl(void* y, int64_t ldy, const void* x, int64_t ldx, const voi
     LSB_REQUIRE(tiles < (int64_t(1) << 31), "gemm: too many tiles");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(tiles < num_sms() ? tiles : num_sms()), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(kPersistThreads, 1, 1);
     cfg.dynamicSmemBytes = persistent_smem(stages);
     cfg.stream = as_stream(stream);
     cudaLaunchAttribute attr;
