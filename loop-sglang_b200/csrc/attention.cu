@@ -321,9 +321,12 @@ __global__ void __launch_bounds__(kWarps * 32, 6)
 // query heads w, w+16, w+32, w+48; within a warp, lane groups of kLanes lanes own
 // one key each (8 head dims per lane) and 4 keys per lane group are reduced
 // together (a transposing butterfly: 5 shuffles instead of 16 for 4 dot products
-// over 16 lanes). The online softmax, the split partials and the last-arriving
-// merge are those of the kernel above, with one arrival counter per (row, consumer
-// warp).
+// over 16 lanes). The online softmax and the split partials are those of the kernel
+// above. A row whose keys end in one partial is written out by its consumer warp; the
+// rows with several (several splits, several warps per head, or a shared prefix's
+// partials) are merged by a second kernel that waits on this grid (programmatic
+// dependent launch), so the consumers never wait on a global fence or counter between
+// items: an item is a stage-ring pass with no round trip to memory at its end.
 // ---------------------------------------------------------------------------
 constexpr int kConsumerWarps = 16;
 constexpr int kStreamThreads = 32 * (kConsumerWarps + 1);
@@ -394,6 +397,26 @@ __host__ __device__ inline StreamLayout stream_layout(int d, int hq, int hkv, in
   return L;
 }
 
+
+// q . k over 8 head dims held as bf16 pairs, accumulated in fp32 from element 0 up:
+// fma.rn.f32.bf16 takes the bf16 operands as they are (their product is exact in fp32), so
+// no conversion instructions sit between the shared-memory load and the FMAs.
+__device__ __forceinline__ float dot8_bf16(const uint4 q, const uint4 k) {
+  float acc = 0.f;
+  asm("{\n"
+      ".reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
+      "mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
+      "mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
+      "fma.rn.f32.bf16 %0, a0, b0, %0;\n fma.rn.f32.bf16 %0, a1, b1, %0;\n"
+      "fma.rn.f32.bf16 %0, a2, b2, %0;\n fma.rn.f32.bf16 %0, a3, b3, %0;\n"
+      "fma.rn.f32.bf16 %0, a4, b4, %0;\n fma.rn.f32.bf16 %0, a5, b5, %0;\n"
+      "fma.rn.f32.bf16 %0, a6, b6, %0;\n fma.rn.f32.bf16 %0, a7, b7, %0;\n"
+      "}"
+      : "+f"(acc)
+      : "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w), "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w));
+  return acc;
+}
+
 // Sum over the kL lanes of a key group of 4 values per lane. Lane i of the group ends
 // up with the total of value 2*bit(kL/2) + bit(kL/4) of its lane index.
 template <int kL>
@@ -453,6 +476,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
     const int pshift = __ffs(p.page_size) - 1;
     const int total = p.max_splits * p.rows;
     const int q_copy = p.hq * D * 2;
+    const uint64_t evict_first = l2_evict_first_policy();  // every key is read once
     int gs = 0, nitem = 0;
     bool ok = true;
     // (claiming the next item ahead of time was measured to hurt: a CTA that holds two
@@ -567,10 +591,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
           for (int j = 0; j < kMaxStageTokens / 32; ++j) {
             const int i = lane + 32 * j;
             if (i < ntok && ((valid >> i) & 1ull)) {
-              bulk_load(sk + i * row_bytes, p.k_cache + slot[j] * p.slot_stride,
-                        static_cast<uint32_t>(row_bytes), &full[s]);
-              bulk_load(sv + i * row_bytes, p.v_cache + slot[j] * p.slot_stride,
-                        static_cast<uint32_t>(row_bytes), &full[s]);
+              bulk_load_hint(sk + i * row_bytes, p.k_cache + slot[j] * p.slot_stride,
+                             static_cast<uint32_t>(row_bytes), &full[s], evict_first);
+              bulk_load_hint(sv + i * row_bytes, p.v_cache + slot[j] * p.slot_stride,
+                             static_cast<uint32_t>(row_bytes), &full[s], evict_first);
             }
           }
         } else if (lane == 0) {
@@ -581,8 +605,10 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
           auto flush = [&]() {
             if (run_n == 0) return;
             const uint32_t nb = static_cast<uint32_t>(run_n * row_bytes);
-            bulk_load(sk + run_i * row_bytes, p.k_cache + run_slot * p.slot_stride, nb, &full[s]);
-            bulk_load(sv + run_i * row_bytes, p.v_cache + run_slot * p.slot_stride, nb, &full[s]);
+            bulk_load_hint(sk + run_i * row_bytes, p.k_cache + run_slot * p.slot_stride, nb,
+                           &full[s], evict_first);
+            bulk_load_hint(sv + run_i * row_bytes, p.v_cache + run_slot * p.slot_stride, nb,
+                           &full[s], evict_first);
             bytes += 2 * nb;
             run_n = 0;
           };
@@ -662,7 +688,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
     }
     auto head_of = [&](int j) { return heads[j]; };
     const int key_off = (g * row_bytes);  // this lane group's first key in a block
-    float qv[HPW][8], acc[HPW][8], m[HPW], l[HPW];
+    uint4 qw[HPW];
+    float acc[HPW][8], m[HPW], l[HPW];
     int gs = 0, nitem = 0;
     while (true) {
       const int s = gs % stages;
@@ -680,12 +707,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         for (int j = 0; j < HPW; ++j) {
           const int h = head_of(j);
           if (h < p.hq && dim_ok) {
-            unpack8(*reinterpret_cast<const bf16x8*>(qrow + (h * D + 8 * c) * 2), qv[j]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qv[j][e] *= p.scale_log2;
+            qw[j] = *reinterpret_cast<const uint4*>(qrow + (h * D + 8 * c) * 2);
           } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qv[j][e] = 0.f;
+            qw[j] = make_uint4(0u, 0u, 0u, 0u);
           }
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc[j][e] = 0.f;
@@ -716,12 +740,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
 #pragma unroll
             for (int u = 0; u < kStreamUnroll; ++u) {
               part[u] = 0.f;
-              if (dim_ok) {
-                float kf[8];
-                unpack8(*reinterpret_cast<const bf16x8*>(sk + u * kGroups * row_bytes + off), kf);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) part[u] = fmaf(qv[j][e], kf[e], part[u]);
-              }
+              if (dim_ok)
+                part[u] = dot8_bf16(
+                    qw[j], *reinterpret_cast<const uint4*>(sk + u * kGroups * row_bytes + off));
             }
             const float red = butterfly4<kLanes>(part[0], part[1], part[2], part[3], lane);
             float sc[kStreamUnroll];
@@ -729,7 +750,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
             for (int u = 0; u < kStreamUnroll; ++u) {
               const int src = group_base + (u >> 1) * (kLanes / 2) + (u & 1) * (kLanes / 4);
               const float v = __shfl_sync(0xffffffffu, red, src);
-              sc[u] = kvalid[u] ? v : kNegBig;
+              sc[u] = kvalid[u] ? v * p.scale_log2 : kNegBig;
             }
             float mx = m[j];
 #pragma unroll
@@ -791,8 +812,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
         }
         continue;
       }
-      const int64_t nown = static_cast<int64_t>(hd.nsplit) * G;  // this kernel's partials
-      const int64_t nparts = hd.pre + nown;                      // merged with the prefix's
 #pragma unroll
       for (int j = 0; j < HPW; ++j) {
         const int h = head_of(j);
@@ -804,61 +823,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
           if (c == 0) *reinterpret_cast<float2*>(p.ws.partial_ml + idx * 2) = make_float2(m[j], l[j]);
         }
       }
-      // One arrival counter per (row, head): whichever warp delivers a head's last
-      // partial merges that head, without waiting for any other warp.
-      __threadfence();
-      __syncwarp();
-      constexpr int kQuads = D / 4;
-      for (int j = 0; j < HPW; ++j) {
-        const int h = head_of(j);
-        if (h >= p.hq) break;
-        int last = 0;
-        if (lane == 0) {
-          int* counter = p.ws.counters + kRowCounterBase + row * p.hq + h;
-          const int prev = atomicAdd(counter, 1);
-          last = prev == nown - 1;
-          if (last) *counter = 0;  // every partial has arrived: reset for the next launch
-        }
-        if (!__shfl_sync(0xffffffffu, last, 0)) continue;
-        __threadfence();
-        const int64_t base_idx = (row * p.hq + h) * parts;
-        float mt = kNegBig, lt = 0.f;
-        float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
-        // 8 partials per batch: all their loads are in flight before the first is used
-        constexpr int kBatch = 8;
-        for (int64_t s0 = 0; s0 < nparts; s0 += kBatch) {
-          float2 ml[kBatch];
-          float4 po[kBatch];
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            ml[u] = make_float2(kNegBig, 0.f);
-            po[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (s0 + u < nparts) {
-              ml[u] = __ldcg(reinterpret_cast<const float2*>(p.ws.partial_ml + (base_idx + s0 + u) * 2));
-              if (lane < kQuads)
-                po[u] = __ldcg(reinterpret_cast<const float4*>(p.ws.partial_o + (base_idx + s0 + u) * D) + lane);
-            }
-          }
-#pragma unroll
-          for (int u = 0; u < kBatch; ++u) {
-            if (s0 + u >= nparts) break;
-            const float mn = fmaxf(mt, ml[u].x);
-            const float c1 = exp2f(mt - mn), c2 = exp2f(ml[u].x - mn);
-            lt = lt * c1 + ml[u].y * c2;
-            ot.x = ot.x * c1 + po[u].x * c2;
-            ot.y = ot.y * c1 + po[u].y * c2;
-            ot.z = ot.z * c1 + po[u].z * c2;
-            ot.w = ot.w * c1 + po[u].w * c2;
-            mt = mn;
-          }
-        }
-        if (lane < kQuads) {
-          const float inv = lt > 0.f ? 1.f / lt : 0.f;
-          bf162* dst = reinterpret_cast<bf162*>(p.out + row * p.out_stride + int64_t(h) * D + 4 * lane);
-          dst[0] = __floats2bfloat162_rn(ot.x * inv, ot.y * inv);
-          dst[1] = __floats2bfloat162_rn(ot.z * inv, ot.w * inv);
-        }
-      }
+      // (the rows with more than one partial are merged by stream_combine_kernel, launched
+      // right after this grid: no fence or arrival count holds up the next stage)
     }
   }
   // Every CTA has drained the queue once the finished count reaches the grid: the
@@ -872,6 +838,80 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
       queue[1] = 0;
       __threadfence();
     }
+  }
+}
+
+// Merge of the streaming kernel's split partials: one warp per (row, query head) whose
+// keys ended in more than one partial, taking partials 0, 1, ... of the row and head in
+// that order (online rescaling by the running maximum), then normalising once.
+template <int D>
+__global__ void __launch_bounds__(128) stream_combine_kernel(StreamParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the streaming grid's partials
+  allow_dependent_launch();
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= static_cast<int64_t>(p.rows) * p.hq) return;
+  const int row = static_cast<int>(wid / p.hq);
+  const int h = static_cast<int>(wid - static_cast<int64_t>(row) * p.hq);
+  int b = row;
+  if (p.rows != p.num_reqs) {
+    int lo = 0, hi = p.num_reqs - 1;  // request of the row
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.cu_seqlens_q[mid] <= row) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+  }
+  int64_t kv_len = static_cast<int64_t>(p.cache_seqlens[b]) - (p.cu_seqlens_q[b + 1] - 1 - row);
+  if (kv_len > p.max_seqlen) kv_len = p.max_seqlen;  // flagged by the streaming kernel
+  int kb0 = 0, pre = 0;
+  if (p.row_prefix) {
+    kb0 = p.row_prefix[row];
+    if (kb0 > 0) pre = (kb0 + p.prefix_chunk - 1) / p.prefix_chunk;
+  }
+  const int64_t span = kv_len - kb0;
+  const int64_t nsplit = span > 0 ? (span + p.chunk - 1) / p.chunk : 1;
+  const int G = p.warps_per_head;
+  if (nsplit == 1 && G == 1 && pre == 0) return;  // written by its consumer warp
+  const int64_t nparts = pre + nsplit * G;
+  constexpr int kQuads = D / 4;
+  const int64_t base_idx = (static_cast<int64_t>(row) * p.hq + h) * p.parts;
+  float mt = kNegBig, lt = 0.f;
+  float4 ot = make_float4(0.f, 0.f, 0.f, 0.f);
+  // 8 partials per batch: all their loads are in flight before the first is used
+  constexpr int kBatch = 8;
+  for (int64_t s0 = 0; s0 < nparts; s0 += kBatch) {
+    float2 ml[kBatch];
+    float4 po[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      ml[u] = make_float2(kNegBig, 0.f);
+      po[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s0 + u < nparts) {
+        ml[u] = __ldcg(reinterpret_cast<const float2*>(p.ws.partial_ml + (base_idx + s0 + u) * 2));
+        if (lane < kQuads)
+          po[u] = __ldcg(reinterpret_cast<const float4*>(p.ws.partial_o + (base_idx + s0 + u) * D) + lane);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      if (s0 + u >= nparts) break;
+      const float mn = fmaxf(mt, ml[u].x);
+      const float c1 = exp2f(mt - mn), c2 = exp2f(ml[u].x - mn);
+      lt = lt * c1 + ml[u].y * c2;
+      ot.x = ot.x * c1 + po[u].x * c2;
+      ot.y = ot.y * c1 + po[u].y * c2;
+      ot.z = ot.z * c1 + po[u].z * c2;
+      ot.w = ot.w * c1 + po[u].w * c2;
+      mt = mn;
+    }
+  }
+  if (lane < kQuads) {
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    bf162* dst = reinterpret_cast<bf162*>(p.out + static_cast<int64_t>(row) * p.out_stride +
+                                          int64_t(h) * D + 4 * lane);
+    dst[0] = __floats2bfloat162_rn(ot.x * inv, ot.y * inv);
+    dst[1] = __floats2bfloat162_rn(ot.z * inv, ot.w * inv);
   }
 }
 
@@ -1017,17 +1057,34 @@ static int stream_attention(void* out, int64_t out_stride, const void* q, int64_
   const int64_t items = rows * splits;
   const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
   const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
-  auto launch = [&](auto kernel) -> int {
+  // rows whose keys can end in more than one partial need the combine kernel
+  const bool combine = splits > 1 || wph > 1 || row_prefix != nullptr;
+  auto launch = [&](auto kernel, auto combine_kernel) -> int {
     LSB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   lay.total));
     kernel<<<grid, kStreamThreads, lay.total, as_stream(stream)>>>(sp);
-    return check_launch("lsb_paged_attention");
+    int rc = check_launch("lsb_paged_attention");
+    if (rc != LSB_OK || !combine) return rc;
+    const int64_t warps = rows * hq;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((warps + 3) / 4), 1, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = as_stream(stream);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    LSB_CUDA(cudaLaunchKernelEx(&cfg, combine_kernel, sp));
+    return check_launch("lsb_paged_attention (combine)");
   };
-#define LSB_STREAM_DISPATCH(DIM)                                                  \
-  if (head_dim == DIM) {                                                        \
-    if (hpw == 1) return launch(paged_attention_stream_kernel<DIM, 1>);         \
-    if (hpw == 2) return launch(paged_attention_stream_kernel<DIM, 2>);         \
-    return launch(paged_attention_stream_kernel<DIM, 4>);                       \
+#define LSB_STREAM_DISPATCH(DIM)                                                         \
+  if (head_dim == DIM) {                                                               \
+    if (hpw == 1)                                                                      \
+      return launch(paged_attention_stream_kernel<DIM, 1>, stream_combine_kernel<DIM>); \
+    if (hpw == 2)                                                                      \
+      return launch(paged_attention_stream_kernel<DIM, 2>, stream_combine_kernel<DIM>); \
+    return launch(paged_attention_stream_kernel<DIM, 4>, stream_combine_kernel<DIM>);   \
   }
   LSB_STREAM_DISPATCH(32)
   LSB_STREAM_DISPATCH(64)

@@ -135,6 +135,9 @@ def bench_attention(args, ops) -> dict:
         extra = {"us_unshared": round(us, 2),
                  "prefix_groups": 0 if grp is None else grp.num_groups}
         us = _time_graph(launch_shared, args.reps)
+    if args.vs_trtllm:
+        extra.update(_trtllm_decode_arm(args, q, kv, table_d, seqlens, max_seqlen, scale,
+                                        num_pages, out, ctx))
     kv_tokens = int(ctx.sum()) - (rows - min(rows, groups)) * sp * page  # shared pages once
     kv_bytes = kv_tokens * hkv * d * 2 * 2
     nbytes = kv_bytes + rows * hq * d * 2 * 2
@@ -144,6 +147,45 @@ def bench_attention(args, ops) -> dict:
             "shared_prefix": sp * page, "groups": groups, **extra,
             "us": round(us, 2), "GBps": round(nbytes / us / 1e3, 1),
             "per_row_GBps": round((int(ctx.sum()) * hkv * d * 4 + rows * hq * d * 4) / us / 1e3, 1)}
+
+
+def _trtllm_decode_arm(args, q, kv, table_d, seqlens, max_seqlen, scale, num_pages, out,
+                       ctx) -> dict:
+    """The reference's sm100 decode call on the same pool, page table and queries.
+
+    The reference's TensorRT-LLM backend (attention/trtllm.py:80-91) calls FlashInfer's
+    ``trtllm_batch_decode_with_kv_cache`` with the layer's (k, v) pages in NHD layout
+    ([pages, page_size, kv_heads, head_dim], the same bytes as this library's
+    [slots, kv_heads, head_dim] pool), bmm1_scale = head_dim ** -0.5, bmm2_scale = 1 and a
+    zeroed 128 MiB workspace. Returns its time per launch (same graph timing) and the
+    largest difference from this library's output; reads every row's own keys (the call
+    has no shared-prefix form).
+    """
+    from flashinfer.decode import trtllm_batch_decode_with_kv_cache
+
+    page, hkv, d = args.page, args.kv_heads, args.head_dim
+    k_pages = kv[0].view(num_pages, page, hkv, d)
+    v_pages = kv[1].view(num_pages, page, hkv, d)
+    workspace = torch.zeros(128 * 2**20, dtype=torch.uint8, device=q.device)
+    ref_out = torch.empty_like(q)
+
+    def launch_ref(_i):
+        trtllm_batch_decode_with_kv_cache(
+            query=q, kv_cache=(k_pages, v_pages), workspace_buffer=workspace,
+            block_tables=table_d, seq_lens=seqlens, max_seq_len=max_seqlen,
+            bmm1_scale=scale, bmm2_scale=1.0, kv_layout="NHD", out=ref_out,
+            out_dtype=q.dtype)
+
+    try:
+        us = _time_graph(launch_ref, args.reps)
+    except Exception as exc:  # the library may lack a kernel for this shape
+        return {"trtllm": f"unavailable: {type(exc).__name__}: {str(exc).splitlines()[0][:160]}"}
+    diff = (ref_out.float() - out.float()).abs().max().item()
+    kv_bytes = int(ctx.sum()) * hkv * d * 2 * 2
+    nbytes = kv_bytes + q.shape[0] * q.shape[1] * d * 2 * 2
+    return {"trtllm_us": round(us, 2), "trtllm_GBps": round(nbytes / us / 1e3, 1),
+            "trtllm_max_abs_diff": round(diff, 5),
+            "out_max_abs": round(out.float().abs().max().item(), 4)}
 
 
 def tp_shape(name: str, tp: int) -> tuple[int, int, bool]:
@@ -347,6 +389,9 @@ def main(argv=None) -> None:
     at.add_argument("--shared-prefix", type=int, default=0,
                     help="tokens of each row's context shared with its group (page multiple)")
     at.add_argument("--groups", type=int, default=4, help="prefix groups (rows interleaved)")
+    at.add_argument("--vs-trtllm", action="store_true",
+                    help="also time FlashInfer's trtllm-gen decode (the reference's sm100 "
+                         "backend) on the same pool and check its output")
     at.add_argument("--force", type=int, nargs="+", default=[0],
                     help="kernel selections to time: 0 automatic, 1 tensor-core kernel, 2 not")
     gm = sub.add_parser("gemm")
