@@ -31,6 +31,9 @@ extern "C" {
 const char* lsb_last_error(void);
 /* ABI version, bumped on any signature change. */
 int lsb_abi_version(void);
+/* Kernels this library has enqueued in this process so far, over every entry point and
+ * thread (an entry point may enqueue one or several, e.g. paged attention's merge). */
+int64_t lsb_kernel_launch_count(void);
 
 /* Reads the sticky device error word that kernels set, instead of faulting,
  * when they meet an out-of-range index: LSB_DEVERR_* bits. reset != 0 clears it.

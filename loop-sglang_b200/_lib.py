@@ -40,6 +40,7 @@ F = c_float
 SIGNATURES: dict[str, tuple[object, list]] = {
     "lsb_last_error": (ctypes.c_char_p, []),
     "lsb_abi_version": (ctypes.c_int, []),
+    "lsb_kernel_launch_count": (c_int64, []),
     "lsb_device_error_word": (ctypes.c_int, [P, I32, P]),
     "lsb_rmsnorm": (ctypes.c_int, [P, I64, P, I64, P, I64, I64, F, P]),
     "lsb_fused_add_rmsnorm": (ctypes.c_int, [P, P, P, I64, I64, F, P]),
@@ -152,30 +153,12 @@ def check(rc: int, what: str) -> None:
     raise LsbError(f"{what} failed ({rc}): {msg}")
 
 
-_launches = 0
-_NOT_LAUNCHES = {"lsb_device_error_word", "lsb_comm_alloc", "lsb_comm_free", "lsb_ipc_handle",
-                 "lsb_ipc_open", "lsb_ipc_close", "lsb_comm_create", "lsb_comm_destroy",
-                 "lsb_gemm_plan", "lsb_gemm_argmax_tiles", "lsb_gemm_force_plan",
-                 "lsb_gemm_force_tile_tokens",
-                 "lsb_attention_force_kernel", "lsb_comm_set_protocol",
-                 "lsb_fast_compare_key", "lsb_radix_create", "lsb_radix_destroy", "lsb_radix_match",
-                 "lsb_radix_insert", "lsb_radix_lock", "lsb_radix_indices", "lsb_radix_evict",
-                 "lsb_radix_size_info", "lsb_radix_check"}
-
-
 def launch_count() -> int:
-    """Kernels launched through ``call`` so far in this process (one per call)."""
-    return _launches
-
-
-# entry points that enqueue more than one kernel per call
-_MULTI_LAUNCH = {"lsb_paged_attention_shared_prefix": 2}
+    """Kernels the library has enqueued so far in this process (its own count, taken at
+    every successful launch inside the C entry points)."""
+    return int(lib().lsb_kernel_launch_count())
 
 
 def call(name: str, *args) -> None:
-    """Invoke a launching entry point and count the kernels it enqueues (one, unless listed
-    in ``_MULTI_LAUNCH``)."""
-    global _launches
+    """Invoke an entry point and raise on a non-zero status."""
     check(getattr(lib(), name)(*args), name)
-    if name not in _NOT_LAUNCHES:
-        _launches += _MULTI_LAUNCH.get(name, 1)

@@ -1,9 +1,14 @@
-// Error state and ABI version of the C entry points.
+// Error state, ABI version and launch count of the C entry points.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace lsb {
 
 static thread_local char g_last_error[1024] = "";
+static std::atomic<int64_t> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -17,6 +22,10 @@ void set_error(const char* fmt, ...) {
 extern "C" const char* lsb_last_error(void) { return lsb::g_last_error; }
 
 extern "C" int lsb_abi_version(void) { return 1; }
+
+extern "C" int64_t lsb_kernel_launch_count(void) {
+  return lsb::g_launches.load(std::memory_order_relaxed);
+}
 
 // ---------------------------------------------------------------------------
 // Sticky device error word: kernels OR LSB_DEVERR_* bits into it instead of

@@ -28,14 +28,17 @@ inline int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+void note_launch();  // one kernel enqueued (lsb_kernel_launch_count)
+
 // Checks the launch that just happened (configuration errors surface here;
-// asynchronous faults surface at the next synchronising call).
+// asynchronous faults surface at the next synchronising call) and counts it.
 inline int check_launch(const char* what) {
   cudaError_t e = cudaPeekAtLastError();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(LSB_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   }
+  note_launch();
   return LSB_OK;
 }
 

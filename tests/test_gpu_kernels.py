@@ -222,6 +222,29 @@ def test_paged_attention(d: int, page: int, mode: str) -> None:
     no_device_errors()
 
 
+@pytest.mark.parametrize("kv_lens,launches", [([40, 50, 60, 64], 1), ([40, 3000, 900, 4100], 2)])
+def test_paged_attention_launch_count(kv_lens: list[int], launches: int) -> None:
+    """The library counts every kernel it enqueues: a decode call whose rows each end in
+    one partial is one launch; one with split rows adds the partial merge (and its output
+    still matches the oracle)."""
+    from loop_sglang_b200 import _lib
+
+    hq = hkv = 16
+    d, page = 128, 16
+    q, kc, vc, table, seq, cu = _paged_case(gen(sum(kv_lens)), hq, hkv, d, page, [1] * 4, kv_lens)
+    scale = d ** -0.5
+    kd = kc.to(DEV).view(-1, hkv * d)
+    vd = vc.to(DEV).view(-1, hkv * d)
+    args = (q.to(DEV), kd, vd, table.to(DEV), seq.to(DEV), cu.to(DEV), page,
+            int(table.shape[1] * page), scale, hkv)
+    ops.paged_attention(*args)  # workspace allocation and first-call setup
+    before = _lib.launch_count()
+    got = ops.paged_attention(*args)
+    assert _lib.launch_count() - before == launches
+    close(got, O.paged_attention(q, kc, vc, table, seq, cu, scale))
+    no_device_errors()
+
+
 @pytest.mark.parametrize("hq,hkv,d", [(16, 16, 128), (8, 2, 64), (55, 55, 96), (4, 4, 32)])
 @pytest.mark.parametrize("page", [1, 16])
 def test_paged_attention_prefill_tensor_cores(hq: int, hkv: int, d: int, page: int) -> None:
