@@ -361,6 +361,7 @@ struct StreamParams {
   int num_reqs, rows, hq, hkv, page_size;
   int chunk, max_splits, stages;
   int sub;              // blocks of stream_tokens(D) keys per stage
+  int lane_per_page;    // producer issues a stage's page runs from one lane each
   int warps_per_head;   // consumer warps sharing a query head (1 when hq >= 16)
   int64_t parts;        // partial slots per (row, head)
   // Shared prefixes (null: none): keys [0, row_prefix[r]) of row r are covered by
@@ -596,6 +597,47 @@ __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kern
               bulk_load_hint(sv + i * row_bytes, p.v_cache + slot[j] * p.slot_stride,
                              static_cast<uint32_t>(row_bytes), &full[s], evict_first);
             }
+          }
+        } else if (p.lane_per_page) {
+          // One page run per lane (lane j copies the stage's keys in its j-th page): a stage
+          // of many short pages is issued in parallel instead of copy by copy from one lane
+          // (2 KV heads x 128, 16-token pages: four pages per stage, 102 -> 81 us at 256 rows).
+          const int pg0 = pow2 ? (t0 >> pshift) : t0 / p.page_size;
+          const int tl = t0 + (ntok > 0 ? ntok : 1) - 1;
+          const int npg = ntok > 0 ? (pow2 ? (tl >> pshift) : tl / p.page_size) - pg0 + 1 : 0;
+          int i0 = 0, n = 0;
+          int64_t slot0 = 0;
+          bool in = false;
+          if (lane < npg) {
+            const int pg = pg0 + lane;
+            const int tb = t0 > pg * p.page_size ? t0 : pg * p.page_size;
+            const int te = t0 + ntok < (pg + 1) * p.page_size ? t0 + ntok : (pg + 1) * p.page_size;
+            i0 = tb - t0;
+            n = te - tb;
+            slot0 = static_cast<int64_t>(s_pages[pg - p_first]) * p.page_size +
+                    (tb - pg * p.page_size);
+            in = slot0 >= 0 && slot0 + n <= p.num_slots;
+            if (!in && p.error_flag) atomicOr(p.error_flag, LSB_DEVERR_SLOT);
+          }
+          uint64_t valid = in ? ((n >= 64 ? ~0ull : ((1ull << n) - 1ull)) << i0) : 0ull;
+          uint32_t bytes = in ? static_cast<uint32_t>(2 * n * row_bytes) : 0u;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            valid |= __shfl_xor_sync(0xffffffffu, valid, o);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+          }
+          if (lane == 0) {
+            h.valid = valid;
+            hdr[s] = h;
+            mbar_expect_tx(&full[s], bytes);
+          }
+          __syncwarp();
+          if (in) {
+            const uint32_t nb = static_cast<uint32_t>(n * row_bytes);
+            bulk_load_hint(sk + i0 * row_bytes, p.k_cache + slot0 * p.slot_stride, nb, &full[s],
+                           evict_first);
+            bulk_load_hint(sv + i0 * row_bytes, p.v_cache + slot0 * p.slot_stride, nb, &full[s],
+                           evict_first);
           }
         } else if (lane == 0) {
           uint64_t valid = 0;
@@ -1048,6 +1090,9 @@ static int stream_attention(void* out, int64_t out_stride, const void* q, int64_
   if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
   if (sub < 1) sub = 1;
   sp.sub = sub;
+  // a stage spanning four or more pages is issued one page run per producer lane (measured:
+  // faster from four pages per stage, slower at one or two)
+  sp.lane_per_page = page_size >= 8 && tb * sub >= 4 * page_size ? 1 : 0;
   const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0, sub);
   int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
   if (stages > kMaxStreamStages) stages = kMaxStreamStages;

@@ -272,6 +272,9 @@ def test_paged_attention_prefill_tensor_cores(hq: int, hkv: int, d: int, page: i
     (16, 8, 128, 1),    # scattered 2 KB rows: streaming kernel, one bulk copy pair per key
     (4, 4, 128, 1),     # scattered 1 KB rows (a TP=4 rank): per-CTA kernel, a warp per head
     (2, 2, 128, 1),     # a TP=8 rank: per-CTA kernel, two key sub-streams per head
+    (2, 2, 128, 16),    # a TP=8 rank on 16-token pages: four pages per stage, one per lane
+    (2, 2, 128, 12),    # the same with pages whose size is not a power of two
+    (4, 2, 64, 8),      # eight 8-token pages per stage, grouped-query KV
     (1, 1, 64, 1),      # one head: four key sub-streams merged in shared memory
     (3, 1, 128, 1),     # three heads: one warp idle, grouped-query KV
 ])
