@@ -32,6 +32,25 @@ constexpr float kNegBig = -1e30f;
 
 __host__ __device__ constexpr int lanes_for(int d) { return d <= 32 ? 4 : (d <= 64 ? 8 : 16); }
 
+// q . k over 8 head dims held as bf16 pairs, accumulated in fp32 from element 0 up:
+// fma.rn.f32.bf16 takes the bf16 operands as they are (their product is exact in fp32), so
+// no conversion instructions sit between the shared-memory load and the FMAs.
+__device__ __forceinline__ float dot8_bf16(const uint4 q, const uint4 k) {
+  float acc = 0.f;
+  asm("{\n"
+      ".reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
+      "mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
+      "mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
+      "fma.rn.f32.bf16 %0, a0, b0, %0;\n fma.rn.f32.bf16 %0, a1, b1, %0;\n"
+      "fma.rn.f32.bf16 %0, a2, b2, %0;\n fma.rn.f32.bf16 %0, a3, b3, %0;\n"
+      "fma.rn.f32.bf16 %0, a4, b4, %0;\n fma.rn.f32.bf16 %0, a5, b5, %0;\n"
+      "fma.rn.f32.bf16 %0, a6, b6, %0;\n fma.rn.f32.bf16 %0, a7, b7, %0;\n"
+      "}"
+      : "+f"(acc)
+      : "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w), "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w));
+  return acc;
+}
+
 constexpr int kMaxChunk = 1024;  // keys per split (upper bound)
 
 int64_t chunk_for(int64_t rows, int32_t hq, int64_t max_seqlen) {
@@ -124,15 +143,9 @@ __global__ void __launch_bounds__(kWarps * 32, 6)
   const bool dim_ok = c < kVec;
   const int kvh = head_ok ? h / (hq / hkv) : 0;
 
-  float qv[8];
-  if (head_ok && dim_ok) {
-    unpack8(*reinterpret_cast<const bf16x8*>(q + row * q_stride + int64_t(h) * D + 8 * c), qv);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qv[e] *= scale_log2;
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) qv[e] = 0.f;
-  }
+  uint4 qw = make_uint4(0u, 0u, 0u, 0u);  // raw bf16 pairs; the score is scaled once
+  if (head_ok && dim_ok)
+    qw = *reinterpret_cast<const uint4*>(q + row * q_stride + int64_t(h) * D + 8 * c);
   float acc[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
@@ -178,15 +191,10 @@ __global__ void __launch_bounds__(kWarps * 32, 6)
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         float part = 0.f;
-        if (valid[u] && dim_ok) {
-          float kf[8];
-          unpack8(kr[u], kf);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) part = fmaf(qv[e], kf[e], part);
-        }
+        if (valid[u] && dim_ok) part = dot8_bf16(qw, *reinterpret_cast<const uint4*>(&kr[u]));
 #pragma unroll
         for (int o = kLanes / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        s[u] = valid[u] ? part : kNegBig;
+        s[u] = valid[u] ? part * scale_log2 : kNegBig;
       }
       float mx = m;
 #pragma unroll
@@ -399,24 +407,6 @@ __host__ __device__ inline StreamLayout stream_layout(int d, int hq, int hkv, in
 }
 
 
-// q . k over 8 head dims held as bf16 pairs, accumulated in fp32 from element 0 up:
-// fma.rn.f32.bf16 takes the bf16 operands as they are (their product is exact in fp32), so
-// no conversion instructions sit between the shared-memory load and the FMAs.
-__device__ __forceinline__ float dot8_bf16(const uint4 q, const uint4 k) {
-  float acc = 0.f;
-  asm("{\n"
-      ".reg .b16 a0, a1, a2, a3, a4, a5, a6, a7, b0, b1, b2, b3, b4, b5, b6, b7;\n"
-      "mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n mov.b32 {a4, a5}, %3;\n mov.b32 {a6, a7}, %4;\n"
-      "mov.b32 {b0, b1}, %5;\n mov.b32 {b2, b3}, %6;\n mov.b32 {b4, b5}, %7;\n mov.b32 {b6, b7}, %8;\n"
-      "fma.rn.f32.bf16 %0, a0, b0, %0;\n fma.rn.f32.bf16 %0, a1, b1, %0;\n"
-      "fma.rn.f32.bf16 %0, a2, b2, %0;\n fma.rn.f32.bf16 %0, a3, b3, %0;\n"
-      "fma.rn.f32.bf16 %0, a4, b4, %0;\n fma.rn.f32.bf16 %0, a5, b5, %0;\n"
-      "fma.rn.f32.bf16 %0, a6, b6, %0;\n fma.rn.f32.bf16 %0, a7, b7, %0;\n"
-      "}"
-      : "+f"(acc)
-      : "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w), "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w));
-  return acc;
-}
 
 // Sum over the kL lanes of a key group of 4 values per lane. Lane i of the group ends
 // up with the total of value 2*bit(kL/2) + bit(kL/4) of its lane index.
