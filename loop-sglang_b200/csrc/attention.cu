@@ -90,6 +90,24 @@ int64_t workspace_bytes_for(int64_t rows, int32_t hq, int32_t d, int64_t splits)
   return (b + 255) & ~int64_t(255);
 }
 
+// Sum over the kL lanes of a key group of 4 values per lane. Lane i of the group ends
+// up with the total of value 2*bit(kL/2) + bit(kL/4) of its lane index.
+template <int kL>
+__device__ __forceinline__ float butterfly4(float v0, float v1, float v2, float v3, int lane) {
+  const bool b1 = lane & (kL / 2);
+  float k0 = b1 ? v2 : v0, k1 = b1 ? v3 : v1;
+  const float s0 = b1 ? v0 : v2, s1 = b1 ? v1 : v3;
+  k0 += __shfl_xor_sync(0xffffffffu, s0, kL / 2);
+  k1 += __shfl_xor_sync(0xffffffffu, s1, kL / 2);
+  const bool b0 = lane & (kL / 4);
+  float k = b0 ? k1 : k0;
+  const float sx = b0 ? k0 : k1;
+  k += __shfl_xor_sync(0xffffffffu, sx, kL / 4);
+#pragma unroll
+  for (int o = kL / 8; o > 0; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
+  return k;
+}
+
 template <int D, int KSUB>
 __global__ void __launch_bounds__(kWarps * 32, 6)
     paged_attention_kernel(bf16* __restrict__ out, int64_t out_stride,
@@ -187,14 +205,23 @@ __global__ void __launch_bounds__(kWarps * 32, 6)
           }
         }
       }
+      static_assert(kUnroll == 4, "the butterfly reduces four keys per lane group");
+      float part[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        part[u] = 0.f;
+        if (valid[u] && dim_ok) part[u] = dot8_bf16(qw, *reinterpret_cast<const uint4*>(&kr[u]));
+      }
+      // the 4 keys' sums over the group's lanes in 5 shuffles, then each broadcast from
+      // the lane that holds it
+      const float red = butterfly4<kLanes>(part[0], part[1], part[2], part[3], lane);
+      const int group_base = lane & ~(kLanes - 1);
       float s[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        float part = 0.f;
-        if (valid[u] && dim_ok) part = dot8_bf16(qw, *reinterpret_cast<const uint4*>(&kr[u]));
-#pragma unroll
-        for (int o = kLanes / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        s[u] = valid[u] ? part * scale_log2 : kNegBig;
+        const int src = group_base + (u >> 1) * (kLanes / 2) + (u & 1) * (kLanes / 4);
+        const float v = __shfl_sync(0xffffffffu, red, src);
+        s[u] = valid[u] ? v * scale_log2 : kNegBig;
       }
       float mx = m;
 #pragma unroll
@@ -408,23 +435,6 @@ __host__ __device__ inline StreamLayout stream_layout(int d, int hq, int hkv, in
 
 
 
-// Sum over the kL lanes of a key group of 4 values per lane. Lane i of the group ends
-// up with the total of value 2*bit(kL/2) + bit(kL/4) of its lane index.
-template <int kL>
-__device__ __forceinline__ float butterfly4(float v0, float v1, float v2, float v3, int lane) {
-  const bool b1 = lane & (kL / 2);
-  float k0 = b1 ? v2 : v0, k1 = b1 ? v3 : v1;
-  const float s0 = b1 ? v0 : v2, s1 = b1 ? v1 : v3;
-  k0 += __shfl_xor_sync(0xffffffffu, s0, kL / 2);
-  k1 += __shfl_xor_sync(0xffffffffu, s1, kL / 2);
-  const bool b0 = lane & (kL / 4);
-  float k = b0 ? k1 : k0;
-  const float sx = b0 ? k0 : k1;
-  k += __shfl_xor_sync(0xffffffffu, sx, kL / 4);
-#pragma unroll
-  for (int o = kL / 8; o > 0; o >>= 1) k += __shfl_xor_sync(0xffffffffu, k, o);
-  return k;
-}
 
 template <int D, int HPW>
 __global__ void __launch_bounds__(kStreamThreads, 1) paged_attention_stream_kernel(StreamParams p) {
