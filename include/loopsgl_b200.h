@@ -106,12 +106,15 @@ int lsb_store_kv(void* k_cache, void* v_cache, int64_t slot_stride, int64_t num_
  * context longer than max_seqlen is cut at max_seqlen and flagged.
  * Up to 64 query heads (and a stage of 8-32 tokens of every KV head within
  * 64 KB) run on persistent CTAs, one per SM, that take (row, key split) items
- * from a queue and stream the keys into shared memory with bulk copies; larger
- * head counts run one CTA per (row, 4 heads, split). Either way the keys of long
- * rows are split; the partial results and the queue go to the caller's
- * workspace (required: lsb_paged_attention_workspace_size bytes, zeroed once
- * before first use; its head holds counters that every call leaves zeroed, so
- * one workspace serves calls of any shape). head_dim 32, 64, 96 or 128.
+ * from a queue and stream the keys into shared memory with bulk copies (a
+ * second, small kernel chained by programmatic dependent launch then merges the
+ * rows whose keys ended in several partials, so a call enqueues one or two
+ * kernels, both capturable); larger head counts run one CTA per (row, 4 heads,
+ * split). Either way the keys of long rows are split; the partial results and
+ * the queue go to the caller's workspace (required:
+ * lsb_paged_attention_workspace_size bytes, zeroed once before first use; its
+ * head holds counters that every call leaves zeroed, so one workspace serves
+ * calls of any shape). head_dim 32, 64, 96 or 128.
  * Slots outside [0, num_slots) are skipped and flagged in the device error
  * word instead of being read.  Replaces the backends'
  * attention call (attention/trtllm.py:80-91 decode, :62-78 prefill;
