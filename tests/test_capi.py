@@ -64,3 +64,18 @@ def test_workspace_size_queries_are_host_only() -> None:
     # split-K partials are reduced in distributed shared memory: no workspace
     assert lib.lsb_gemm_workspace_size(144, 6144, 2048) == 0
     assert lib.lsb_paged_attention_workspace_size(144, 16, 128, 2304) > 0
+
+
+def test_launch_count_ignores_rejected_calls() -> None:
+    """The library counts only launches that happened: calls rejected by validation (no
+    device needed) leave the count where it was."""
+    pkg = load_package()
+    lib = pkg._lib.lib()
+    before = pkg._lib.launch_count()
+    p = ctypes.c_void_p(16)
+    for _ in range(3):
+        rc = lib.lsb_paged_attention(p, 8, p, 8, p, p, 8, 1, p, 1, p, p, 1, 1, 1, 1, 80, 16, 16,
+                                     ctypes.c_float(1.0), None, 0, None)
+        assert rc == pkg._lib.LSB_ERR_INVALID
+    assert pkg._lib.launch_count() == before
+
