@@ -371,7 +371,7 @@ constexpr int kStreamStageBudget = 64 * 1024;  // bytes of K + V per stage
 constexpr int kStreamSmemBudget = 220 * 1024;
 constexpr int kMaxStreamStages = 16;
 constexpr int kMaxStageTokens = 64;  // bits of the per-stage valid mask
-constexpr int kRowCounterBase = 2;  // counters[0]: next item, [1]: CTAs finished
+// workspace counters of the streaming kernel: [0] next work item, [1] CTAs finished
 
 enum : int { kItemFirst = 1, kItemLast = 2, kStreamExit = 4 };
 
@@ -1006,9 +1006,9 @@ extern "C" int lsb_attention_force_kernel(int32_t mode) {
   return LSB_OK;
 }
 
-// The streaming kernel runs when its stage fits and its per-(row, warp) counters fit
-// the counter region; otherwise the per-CTA kernel does.
-static bool use_stream(int64_t rows, int32_t hq, int32_t hkv, int32_t d, int32_t page_size,
+// The streaming kernel runs when its stage fits (and, for scattered slots, when a key's
+// row is large enough for bulk copies to pay); otherwise the per-CTA kernel does.
+static bool use_stream(int32_t hq, int32_t hkv, int32_t d, int32_t page_size,
                        int64_t slot_stride) {
   // Keys whose slots are scattered (one-token pages: last-exited versions) cost the
   // streaming kernel one pair of bulk copies per key; below 2 KB of K per key (fewer than
@@ -1017,7 +1017,7 @@ static bool use_stream(int64_t rows, int32_t hq, int32_t hkv, int32_t d, int32_t
   const bool packed = slot_stride == static_cast<int64_t>(hkv) * d;
   const bool scattered = page_size < 8 || !packed;
   if (scattered && hkv * d * 2 < 2048) return false;
-  return stream_eligible(hq, hkv, d) && rows * hq <= kCounterCap - kRowCounterBase;
+  return stream_eligible(hq, hkv, d);
 }
 
 extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, int32_t head_dim,
@@ -1210,7 +1210,7 @@ extern "C" int lsb_paged_attention(void* out, int64_t out_stride, const void* q,
     const int64_t max_q = rows < max_seqlen ? rows : max_seqlen;
     return launch_prefill_attention(pp, max_q, head_dim, as_stream(stream));
   }
-  if (use_stream(rows, hq, hkv, head_dim, page_size, slot_stride))
+  if (use_stream(hq, hkv, head_dim, page_size, slot_stride))
     return stream_attention(out, out_stride, q, q_stride, k_cache, v_cache, slot_stride,
                             num_slots, page_table, pt_stride, cache_seqlens, cu_seqlens_q,
                             num_reqs, rows, hq, hkv, head_dim, page_size, max_seqlen, scale,
@@ -1283,11 +1283,11 @@ extern "C" int lsb_paged_attention_shared_prefix(
   if (rows != num_reqs)
     return fail(LSB_ERR_UNSUPPORTED,
                 "paged_attention_shared_prefix: decode rows only (one query row per request)");
-  if (!use_stream(rows, hq, hkv, head_dim, page_size, slot_stride))
+  if (!use_stream(hq, hkv, head_dim, page_size, slot_stride))
     return fail(LSB_ERR_UNSUPPORTED,
                 "paged_attention_shared_prefix: needs the streaming decode kernel (packed pool, "
-                "at most %d query heads, %lld counters)",
-                kStreamMaxHeads, (long long)(kCounterCap - kRowCounterBase));
+                "at most %d query heads, a stage of every KV head within 64 KB)",
+                kStreamMaxHeads);
   LSB_REQUIRE(max_group_prefix <= max_seqlen, "paged_attention_shared_prefix: prefix too long");
   const int chunk = prefix_chunk_for(max_group_prefix, num_groups, max_group_rows, hq);
   const int64_t prefix_parts = (max_group_prefix + chunk - 1) / chunk;
