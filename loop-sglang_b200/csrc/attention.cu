@@ -351,8 +351,9 @@ __global__ void __launch_bounds__(kWarps * 32, 6)
 // copies the row's q (all heads) into one of two q buffers and streams the
 // split's keys in stages of T tokens -- the K and V rows of every KV head of a
 // token (hkv x D x 2 bytes each) -- with cp.async.bulk into a ring of shared-memory
-// stages (one copy per run of consecutive slots inside a page), completing on the
-// stage's mbarrier. The 16 consumer warps compute from shared memory: warp w owns
+// stages (one evict-first copy per run of consecutive slots inside a page, issued from
+// one lane, or from one lane per page when a stage spans four pages or more), completing
+// on the stage's mbarrier. The 16 consumer warps compute from shared memory: warp w owns
 // query heads w, w+16, w+32, w+48; within a warp, lane groups of kLanes lanes own
 // one key each (8 head dims per lane) and 4 keys per lane group are reduced
 // together (a transposing butterfly: 5 shuffles instead of 16 for 4 dot products
