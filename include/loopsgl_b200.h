@@ -129,6 +129,16 @@ int lsb_paged_attention(void* out, int64_t out_stride, const void* q, int64_t q_
                         int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
                         void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The launch plan lsb_paged_attention picks for a decode call (one query row per
+ * request) of this shape on the current device (diagnostics, host only, nothing
+ * launched): out[0] 1 for the streaming kernel, 0 for the per-CTA kernel; out[1]
+ * keys per work item (split); out[2] splits of a max_seqlen row; streaming only
+ * (else 0): out[3] pipeline stages, out[4] keys per stage, out[5] 1 when the
+ * producer issues a stage's page runs one per lane. No counterpart in the reference. */
+int lsb_paged_attention_plan(int64_t rows, int32_t hq, int32_t hkv, int32_t head_dim,
+                             int32_t page_size, int64_t max_seqlen, int64_t slot_stride,
+                             int32_t* out);
+
 /* Kernel selection of later lsb_paged_attention calls of this process, for
  * benchmarks and tuning: 0 automatic (calls with several query rows per request
  * take the tensor-core kernel, decode calls the streaming or per-CTA kernel),
@@ -274,15 +284,15 @@ int lsb_gemm_argmax(void* pairs, int64_t ld_pairs, const void* x, int64_t ldx, c
 int lsb_argmax_pairs(int32_t* out, const void* pairs, int64_t shards, int64_t rows,
                      int64_t tiles, int64_t ld_pairs, int64_t shard_cols, void* stream);
 
-/* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
- * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
- * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */
 /* The launch plan lsb_gemm picks for an M x N x K product on the current device
  * (diagnostics): out[0] tokens per tile, out[1] output tiles, out[2] split-K
  * factor (CTAs per cluster), out[3] pipeline stages, out[4] dynamic shared
  * memory bytes per CTA. */
 int lsb_gemm_plan(int64_t M, int64_t N, int64_t K, int32_t* out);
 
+/* Reorders a [2*I, K] gate_up weight ([gate; up], models/weight.py:136-141)
+ * into 128-row tiles of 64 gate rows followed by the matching 64 up rows, the
+ * layout LSB_EPI_SWIGLU reads. I % 64 == 0. out must not alias w. */
 int lsb_swiglu_interleave(void* out, const void* w, int64_t inter, int64_t K, void* stream);
 
 /* ---------------------------------------------- loop-step exit kernels ---

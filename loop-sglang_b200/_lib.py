@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
                                          P]),
     "lsb_store_kv": (ctypes.c_int, [P, P, I64, I64, P, I64, P, I64, P, I64, I64, P]),
     "lsb_paged_attention_workspace_size": (c_int64, [I64, I32, I32, I64]),
+    "lsb_paged_attention_plan": (ctypes.c_int, [I64, I32, I32, I32, I32, I64, I64, P]),
     "lsb_paged_attention": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64, P, P, I64, I64,
                                            I32, I32, I32, I32, I64, F, P, I64, P]),
     "lsb_paged_attention_noalloc": (ctypes.c_int, [P, I64, P, I64, P, P, I64, I64, P, I64, P, P,

@@ -1037,6 +1037,36 @@ extern "C" int64_t lsb_paged_attention_workspace_size(int64_t rows, int32_t hq, 
   return bytes;
 }
 
+// The streaming launch's shape for a call: keys per work item, splits of the longest row,
+// blocks of stream_tokens(D) keys per stage, pipeline stages and the producer's issue mode.
+struct StreamShape {
+  int64_t chunk, splits;
+  int sub, stages, stage_bytes, lane_per_page;
+};
+
+static StreamShape stream_shape(int64_t rows, int32_t hq, int32_t hkv, int32_t head_dim,
+                                int32_t page_size, int64_t max_seqlen) {
+  StreamShape sh;
+  sh.chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
+  sh.splits = (max_seqlen + sh.chunk - 1) / sh.chunk;
+  // blocks per stage: about 64 KB of K+V per stage, at most 64 keys
+  const int tb = stream_tokens(head_dim);
+  int sub = kStreamStageBudget / (2 * tb * hkv * head_dim * 2);
+  if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
+  if (sub < 1) sub = 1;
+  sh.sub = sub;
+  // a stage spanning four or more pages is issued one page run per producer lane (measured:
+  // faster from four pages per stage, slower at one or two)
+  sh.lane_per_page = page_size >= 8 && tb * sub >= 4 * page_size ? 1 : 0;
+  const StreamLayout probe =
+      stream_layout(head_dim, hq, hkv, static_cast<int>(sh.chunk), page_size, 0, sub);
+  int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
+  if (stages > kMaxStreamStages) stages = kMaxStreamStages;
+  sh.stages = stages;
+  sh.stage_bytes = probe.stage_bytes;
+  return sh;
+}
+
 // The streaming kernel's launch. row_prefix (nullable): per row, the leading keys a kernel
 // launched before this one has covered with ceil(row_prefix / prefix_chunk) partials (at
 // most prefix_parts) in this workspace; this launch streams the rest and merges.
@@ -1048,8 +1078,9 @@ static int stream_attention(void* out, int64_t out_stride, const void* q, int64_
                             int32_t head_dim, int32_t page_size, int64_t max_seqlen, float scale,
                             const int32_t* row_prefix, int prefix_chunk, int64_t prefix_parts,
                             void* workspace, int64_t workspace_bytes, void* stream) {
-  const int64_t chunk = stream_chunk_for(rows, max_seqlen, head_dim, hkv);
-  const int64_t splits = (max_seqlen + chunk - 1) / chunk;
+  const StreamShape sh = stream_shape(rows, hq, hkv, head_dim, page_size, max_seqlen);
+  const int64_t chunk = sh.chunk;
+  const int64_t splits = sh.splits;
   LSB_REQUIRE(splits <= 65535 && rows * splits < (int64_t(1) << 31),
               "paged_attention: max_seqlen too large");
   const int wph = stream_warps_per_head(hq);
@@ -1085,21 +1116,12 @@ static int stream_attention(void* out, int64_t out_stride, const void* q, int64_
   sp.prefix_chunk = prefix_chunk;
   sp.warps_per_head = wph;
   sp.error_flag = lsb_device_error_flag();
-  // blocks per stage: about 64 KB of K+V per stage, at most 64 keys
-  const int tb = stream_tokens(head_dim);
-  int sub = kStreamStageBudget / (2 * tb * hkv * head_dim * 2);
-  if (sub > kMaxStageTokens / tb) sub = kMaxStageTokens / tb;
-  if (sub < 1) sub = 1;
-  sp.sub = sub;
-  // a stage spanning four or more pages is issued one page run per producer lane (measured:
-  // faster from four pages per stage, slower at one or two)
-  sp.lane_per_page = page_size >= 8 && tb * sub >= 4 * page_size ? 1 : 0;
-  const StreamLayout probe = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, 0, sub);
-  int stages = (kStreamSmemBudget - probe.total) / probe.stage_bytes;
-  if (stages > kMaxStreamStages) stages = kMaxStreamStages;
-  LSB_REQUIRE(stages >= 2, "paged_attention: stage of %d bytes too large", probe.stage_bytes);
-  sp.stages = stages;
-  const StreamLayout lay = stream_layout(head_dim, hq, hkv, sp.chunk, page_size, stages, sub);
+  sp.sub = sh.sub;
+  sp.lane_per_page = sh.lane_per_page;
+  LSB_REQUIRE(sh.stages >= 2, "paged_attention: stage of %d bytes too large", sh.stage_bytes);
+  sp.stages = sh.stages;
+  const StreamLayout lay =
+      stream_layout(head_dim, hq, hkv, sp.chunk, page_size, sh.stages, sh.sub);
   const int64_t items = rows * splits;
   const int grid = static_cast<int>(items < num_sms_attention() ? items : num_sms_attention());
   const int hpw = (hq + kConsumerWarps - 1) / kConsumerWarps;
@@ -1138,6 +1160,33 @@ static int stream_attention(void* out, int64_t out_stride, const void* q, int64_
   LSB_STREAM_DISPATCH(128)
 #undef LSB_STREAM_DISPATCH
   return fail(LSB_ERR_UNSUPPORTED, "paged_attention: head_dim %d", head_dim);
+}
+
+extern "C" int lsb_paged_attention_plan(int64_t rows, int32_t hq, int32_t hkv, int32_t head_dim,
+                                        int32_t page_size, int64_t max_seqlen,
+                                        int64_t slot_stride, int32_t* out) {
+  LSB_REQUIRE(out, "paged_attention_plan: null output");
+  LSB_REQUIRE(rows > 0 && page_size > 0 && max_seqlen > 0, "paged_attention_plan: bad sizes");
+  LSB_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 96 || head_dim == 128,
+              "paged_attention_plan: head_dim %d unsupported (32, 64, 96, 128)", head_dim);
+  LSB_REQUIRE(hq > 0 && hkv > 0 && hq % hkv == 0, "paged_attention_plan: bad heads %d/%d", hq,
+              hkv);
+  if (use_stream(hq, hkv, head_dim, page_size, slot_stride)) {
+    const StreamShape sh = stream_shape(rows, hq, hkv, head_dim, page_size, max_seqlen);
+    out[0] = 1;
+    out[1] = static_cast<int32_t>(sh.chunk);
+    out[2] = static_cast<int32_t>(sh.splits);
+    out[3] = sh.stages;
+    out[4] = stream_tokens(head_dim) * sh.sub;
+    out[5] = sh.lane_per_page;
+  } else {
+    const int64_t chunk = chunk_for(rows, hq, max_seqlen);
+    out[0] = 0;
+    out[1] = static_cast<int32_t>(chunk);
+    out[2] = static_cast<int32_t>((max_seqlen + chunk - 1) / chunk);
+    out[3] = out[4] = out[5] = 0;
+  }
+  return LSB_OK;
 }
 
 // Keys per split of a group's shared prefix: enough (group, split, head) CTAs for two per

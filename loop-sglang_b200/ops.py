@@ -552,6 +552,18 @@ def gemm_plan(m: int, n: int, k: int) -> dict:
             "smem": out[4], "ctas": out[1] * out[2]}
 
 
+def attention_plan(rows: int, hq: int, hkv: int, head_dim: int, page_size: int,
+                   max_seqlen: int, slot_stride: int | None = None) -> dict:
+    """The launch plan ``paged_attention`` uses for a decode call of this shape (host only)."""
+    out = (ctypes.c_int32 * 6)()
+    stride = hkv * head_dim if slot_stride is None else slot_stride
+    check(lib().lsb_paged_attention_plan(rows, hq, hkv, head_dim, page_size, max_seqlen, stride,
+                                         out), "paged_attention_plan")
+    return {"kernel": "streaming" if out[0] else "per_cta", "keys_per_item": out[1],
+            "splits": out[2], "stages": out[3], "keys_per_stage": out[4],
+            "lane_per_page": bool(out[5])}
+
+
 def kv_snapshot_bytes(n: int, row_bytes: int, num_layers: int, core_start: int = 0,
                       core_end: int = 0, steps: int = 1, versioned: bool = False) -> int:
     """Host bytes of an n-token KV snapshot (see ``lsb_kv_snapshot_bytes``)."""

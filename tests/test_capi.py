@@ -79,3 +79,26 @@ def test_launch_count_ignores_rejected_calls() -> None:
         assert rc == pkg._lib.LSB_ERR_INVALID
     assert pkg._lib.launch_count() == before
 
+
+
+def test_attention_plan_is_host_only() -> None:
+    """The decode attention plan (kernel, item size, stages, producer issue mode) is pure
+    host logic: 16 KV heads of 128 stream 8 keys per 64 KB stage from one producer lane;
+    a TP=8 rank's 2 heads stream 64 keys (four 16-token pages) one page run per lane, but
+    not on 64-token pages; Huginn's 55 x 96 heads and scattered 1 KB rows take the per-CTA
+    kernel."""
+    from loop_sglang_b200 import ops
+
+    load_package()
+    p = ops.attention_plan(143, 16, 16, 128, 16, 1448)
+    assert p["kernel"] == "streaming" and p["keys_per_stage"] == 8 and p["stages"] == 3
+    assert not p["lane_per_page"] and p["keys_per_item"] * p["splits"] >= 1448
+    p = ops.attention_plan(256, 2, 2, 128, 16, 2112)
+    assert p["kernel"] == "streaming" and p["keys_per_stage"] == 64 and p["lane_per_page"]
+    assert p["keys_per_item"] >= 512  # at least 512 KB of K+V per item with few heads
+    assert not ops.attention_plan(256, 2, 2, 128, 64, 2112)["lane_per_page"]
+    assert ops.attention_plan(64, 55, 55, 96, 16, 1033)["kernel"] == "per_cta"
+    assert ops.attention_plan(512, 4, 4, 128, 1, 900)["kernel"] == "per_cta"
+    assert ops.attention_plan(512, 16, 16, 128, 1, 900)["kernel"] == "streaming"
+    with pytest.raises(ValueError):
+        ops.attention_plan(4, 16, 16, 80, 16, 64)
